@@ -1,0 +1,200 @@
+/*
+ * mkv.h — C ABI of the B200 paged KV-cache library (libmkv.so).
+ *
+ * The library implements the two halves of mini-kvllm's per-layer attention hot path:
+ *   - the KV append (store new K/V rows into block-table pages, optionally
+ *     quantised to FP8 E4M3 with a per-tensor scale), and
+ *   - the paged-attention decode (one query token per sequence, GQA head
+ *     grouping, FP8 dequantisation fused into the page loads, online softmax,
+ *     split-KV partitioning with a merge kernel).
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, and a
+ * CUDA stream passed as `void*` (a `cudaStream_t`; NULL = legacy default stream).
+ * Nothing here allocates device memory: the decode's split-KV scratch and the FP8
+ * calibration words are caller-provided workspaces. All launches are asynchronous
+ * on `stream` and contain no host synchronisation, so they can be captured in a
+ * CUDA graph.
+ *
+ * Each function returns MKV_OK (0) or an error code; mkv_last_error() then holds a
+ * message for the calling thread. Argument errors are detected on the host before
+ * any CUDA call. Index values read on the device (slots, block-table entries) are
+ * bounds-checked in the kernels: an out-of-range entry is skipped, never
+ * dereferenced, and counted in the optional `invalid_count` word.
+ *
+ * Tensor layouts (row-major, innermost last):
+ *   key/value     (num_tokens, num_kv_heads, head_dim)   strides given per call
+ *   k/v cache     (num_blocks, block_size, num_kv_heads, head_dim)   contiguous
+ *   slot_mapping  (num_tokens,)              int32 or int64, -1 = skip this token
+ *   query / out   (num_seqs, num_heads, head_dim)        strides given per call
+ *   block_tables  (num_seqs, max_num_blocks) int32 or int64, -1 = no page
+ *   context_lens  (num_seqs,)                int32 or int64
+ *   k/v scale     one float32 each (per-tensor FP8 scale)
+ *
+ * Reference: heart1128/mini-kvllm, src/myvllm/layers/attention.py. Each entry
+ * point below names the reference function it replaces.
+ */
+#ifndef MKV_H_
+#define MKV_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Symbol visibility: the library is built with hidden visibility; only these are exported. */
+#if defined(__GNUC__)
+#define MKV_API __attribute__((visibility("default")))
+#else
+#define MKV_API
+#endif
+
+/* Element types (also the dtype of query/out and key/value). */
+#define MKV_DTYPE_F32 0
+#define MKV_DTYPE_F16 1
+#define MKV_DTYPE_BF16 2
+#define MKV_DTYPE_FP8_E4M3 3
+
+/* Integer index types for slot_mapping / block_tables / context_lens. */
+#define MKV_INDEX_I32 0
+#define MKV_INDEX_I64 1
+
+/* Status codes. */
+#define MKV_OK 0
+#define MKV_ERR_INVALID_ARGUMENT 1
+#define MKV_ERR_UNSUPPORTED 2
+#define MKV_ERR_WORKSPACE 3
+#define MKV_ERR_CUDA 4
+
+/* Library version string ("major.minor.patch"). */
+MKV_API const char* mkv_version(void);
+
+/* Human-readable name of a status code. */
+MKV_API const char* mkv_status_string(int status);
+
+/* Message describing the last error returned on the calling thread ("" if none). */
+MKV_API const char* mkv_last_error(void);
+
+/*
+ * KV append, same dtype in and out (bf16, fp16 or fp32).
+ * Replaces store_kvcache (attention.py:67-108) and its kernel
+ * store_kvcache_kernel (attention.py:7-64):
+ *     k_cache.view(-1, KVH, D)[slot_mapping[t]] = key[t]   (same for value)
+ * Tokens whose slot is negative are skipped (the reference skips slot -1,
+ * attention.py:29-30). Slots >= num_blocks*block_size are skipped and counted in
+ * *invalid_count when that pointer is non-NULL (device int32, accumulated).
+ * Strides are in elements; head_dim must be contiguous.
+ */
+MKV_API int mkv_store_kvcache(const void* key, const void* value,
+                      int64_t key_stride_token, int64_t key_stride_head,
+                      int64_t value_stride_token, int64_t value_stride_head,
+                      void* k_cache, void* v_cache,
+                      int64_t num_blocks, int32_t block_size,
+                      const void* slot_mapping, int32_t slot_index_type,
+                      int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                      int32_t dtype, int32_t* invalid_count, void* stream);
+
+/*
+ * Device-side, sentinel-aware per-tensor FP8 calibration of the K and V scales.
+ * Replaces the host block of store_kvcache_fp8 (attention.py:315-323):
+ *     if scale == 1.0:  scale = dtype(max(amax(|x|), dtype(1e-8)) * fp32(1/448))
+ * i.e. the value torch produces for `x.abs().amax().clamp(min=1e-8) / 448.0` on a
+ * CUDA tensor of the key dtype (bf16/fp16/fp32; torch divides by a Python scalar
+ * as a multiplication by its float32 reciprocal), stored as float32. A scale that
+ * already differs from 1.0 is left untouched (the scale is frozen after the first
+ * calibration). The amax covers every token of key/value, including tokens whose
+ * slot is -1, exactly as the reference's key.abs().amax().
+ * `work` is a caller-provided device buffer of MKV_FP8_CALIB_WORK_BYTES bytes that
+ * must be zero before the first call; every call leaves it zero again. Calls that
+ * share one `work` buffer must be ordered on one stream.
+ */
+#define MKV_FP8_CALIB_WORK_BYTES 16
+MKV_API int mkv_calibrate_fp8_scales(const void* key, const void* value,
+                             int64_t key_stride_token, int64_t key_stride_head,
+                             int64_t value_stride_token, int64_t value_stride_head,
+                             int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t dtype, float* k_scale, float* v_scale,
+                             void* work, void* stream);
+
+/*
+ * KV append with FP8 E4M3 quantisation, per-tensor scales read on the device.
+ * Replaces the per-tensor branch of store_kvcache_fp8_kernel
+ * (attention.py:118-191, 182-191):
+ *     cache[slot] = e4m3(clamp(float(x) / scale, -448, 448))
+ * with IEEE division and round-to-nearest-even conversion. Slot rules as in
+ * mkv_store_kvcache. head_dim must be a multiple of 16.
+ */
+MKV_API int mkv_store_kvcache_fp8(const void* key, const void* value,
+                          int64_t key_stride_token, int64_t key_stride_head,
+                          int64_t value_stride_token, int64_t value_stride_head,
+                          void* k_cache, void* v_cache,
+                          const float* k_scale, const float* v_scale,
+                          int64_t num_blocks, int32_t block_size,
+                          const void* slot_mapping, int32_t slot_index_type,
+                          int64_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t dtype, int32_t* invalid_count, void* stream);
+
+/*
+ * Number of KV splits the decode uses for this shape when num_splits = 0 (auto).
+ * Host-only; depends on shapes, never on device data.
+ */
+MKV_API int32_t mkv_paged_decode_num_splits(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                                    int32_t head_dim, int32_t block_size, int32_t max_num_blocks);
+
+/*
+ * Bytes of workspace the decode needs for this shape and split count
+ * (num_splits = 0 means the automatic choice). 0 when no split is used.
+ */
+MKV_API size_t mkv_paged_decode_workspace_bytes(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                                        int32_t head_dim, int32_t block_size,
+                                        int32_t max_num_blocks, int32_t num_splits);
+
+/*
+ * Paged-attention decode over a bf16 / fp16 / fp32 cache.
+ * Replaces paged_attention_decode (attention.py:895-950) and its kernel
+ * paged_attention_decode_kernel (attention.py:517-646):
+ *     out[b, h] = softmax_t(scale * q[b, h] . K[b, kvh(h), t]) V[b, kvh(h), t]
+ * over t < min(context_lens[b], max_num_blocks*block_size), with page
+ * block_tables[b, t / block_size] and row t % block_size; kvh(h) = h / (H / KVH).
+ * Tokens on a page entry that is -1 (or outside [0, num_blocks)) are skipped,
+ * as in the reference. A sequence with no visible token yields NaN (0/0), as in
+ * the reference. out has query's dtype. workspace may be NULL when
+ * mkv_paged_decode_workspace_bytes(...) is 0.
+ */
+MKV_API int mkv_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
+                     const void* k_cache, const void* v_cache, int32_t cache_dtype,
+                     int64_t num_blocks, int32_t block_size,
+                     const void* block_tables, int32_t block_table_index_type,
+                     int64_t block_table_stride_seq, int32_t max_num_blocks,
+                     const void* context_lens, int32_t context_lens_index_type,
+                     int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                     float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
+                     void* workspace, size_t workspace_bytes, int32_t num_splits,
+                     int32_t* invalid_count, void* stream);
+
+/*
+ * Paged-attention decode over an FP8 E4M3 cache with per-tensor scales
+ * (device float32 each). Replaces paged_attention_decode_quantized
+ * (attention.py:1213-1268) for kv_cache_dtype "fp8_per_tensor", i.e.
+ * paged_attention_decode_fp8_kernel with PER_TOKEN_HEAD=0 (attention.py:953-1121):
+ * K = float(k_fp8) * k_scale and V = float(v_fp8) * v_scale, dequantised as the
+ * pages are loaded. Other arguments as in mkv_paged_decode.
+ */
+MKV_API int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
+                         const void* k_cache, const void* v_cache,
+                         const float* k_scale, const float* v_scale,
+                         int64_t num_blocks, int32_t block_size,
+                         const void* block_tables, int32_t block_table_index_type,
+                         int64_t block_table_stride_seq, int32_t max_num_blocks,
+                         const void* context_lens, int32_t context_lens_index_type,
+                         int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                         float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
+                         void* workspace, size_t workspace_bytes, int32_t num_splits,
+                         int32_t* invalid_count, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MKV_H_ */

@@ -1,0 +1,331 @@
+"""Drop-in replacements for mini-kvllm's paged KV-cache hot path.
+
+The four functions keep the reference's names, argument order and meaning
+(heart1128/mini-kvllm, src/myvllm/layers/attention.py):
+
+  store_kvcache(key, value, k_cache, v_cache, slot_mapping, block_size)           # :67
+  store_kvcache_fp8(key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping,
+                    block_size, kv_cache_dtype)                                    # :281
+  paged_attention_decode(query, k_cache, v_cache, block_tables, context_lens, scale,
+                         num_heads, num_kv_heads, head_dim, block_size)            # :895
+  paged_attention_decode_quantized(query, k_cache, v_cache, k_scale, v_scale,
+                         block_tables, context_lens, scale, num_heads, num_kv_heads,
+                         head_dim, block_size, kv_cache_dtype)                     # :1213
+
+and `Attention` keeps the module contract of attention.py:1617-1807 (cache tensors and
+scales injected as attributes by the model runner, metadata read from the global
+context). Each call maps tensors to raw pointers and strides and launches the sm_100a
+kernels of libmkv.so on the current CUDA stream; there is no Triton, no CPU path and
+no fallback. Nothing synchronises with the host, so the decode step (append + decode)
+can be captured in a CUDA graph, including the FP8 path whose per-tensor scale is
+calibrated on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import nn
+
+from .. import _lib
+from ..utils.context import get_context
+
+FP8_E4M3_MAX = 448.0
+
+_DTYPES = {
+    torch.float32: _lib.DTYPE_F32,
+    torch.float16: _lib.DTYPE_F16,
+    torch.bfloat16: _lib.DTYPE_BF16,
+    torch.float8_e4m3fn: _lib.DTYPE_FP8_E4M3,
+}
+_INDEX = {torch.int32: _lib.INDEX_I32, torch.int64: _lib.INDEX_I64}
+_FLOAT_IO = (torch.float32, torch.float16, torch.bfloat16)
+
+
+class _on_device:
+    """Makes `device` current for the duration of a launch (no-op when it already is)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
+def _require_cuda(fn: str, *tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError(f"{fn}: all tensors must be CUDA tensors (got {t.device})")
+        if t.device != dev:
+            raise ValueError(f"{fn}: tensors are on different devices ({dev} and {t.device})")
+    return dev
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _index_tensor(t: torch.Tensor, fn: str, what: str) -> torch.Tensor:
+    if t.dtype not in _INDEX:
+        raise ValueError(f"{fn}: {what} must be int32 or int64 (got {t.dtype})")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _row_major_tokens(x: torch.Tensor) -> torch.Tensor:
+    """(T, KVH, D) view whose last dim is contiguous (strides of dims 0/1 may be anything)."""
+    return x if x.stride(-1) == 1 else x.contiguous()
+
+
+def _check_cache(fn: str, k_cache: torch.Tensor, v_cache: torch.Tensor, block_size: int,
+                 num_kv_heads: int, head_dim: int) -> int:
+    if k_cache.shape != v_cache.shape or k_cache.dtype != v_cache.dtype:
+        raise ValueError(f"{fn}: K and V cache shapes/dtypes must match")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError(f"{fn}: caches must be contiguous (num_blocks, block_size, num_kv_heads, head_dim)")
+    row = block_size * num_kv_heads * head_dim
+    if row <= 0 or k_cache.numel() % row != 0:
+        raise ValueError(f"{fn}: cache of shape {tuple(k_cache.shape)} is not a whole number of "
+                         f"({block_size}, {num_kv_heads}, {head_dim}) blocks")
+    return k_cache.numel() // row
+
+
+# ---------------------------------------------------------------------------------- append
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                  v_cache: torch.Tensor, slot_mapping: torch.Tensor, block_size: int) -> None:
+    """Stores key/value (num_tokens, num_kv_heads, head_dim) into the paged caches
+    (num_blocks, block_size, num_kv_heads, head_dim) at slot_mapping[t]; slot -1 skips
+    the token. Reference: attention.py:67-108 (kernel 7-64)."""
+    fn = "store_kvcache"
+    num_tokens, num_kv_heads, head_dim = key.shape
+    assert k_cache.shape == v_cache.shape, "K and V cache shapes must match"
+    assert slot_mapping.numel() == num_tokens, "Slot mapping size must match number of tokens"
+    dev = _require_cuda(fn, key, value, k_cache, v_cache, slot_mapping)
+    if k_cache.dtype not in _DTYPES:
+        raise ValueError(f"{fn}: unsupported cache dtype {k_cache.dtype}")
+    key, value = _row_major_tokens(key), _row_major_tokens(value)
+    if key.dtype != k_cache.dtype:  # the reference's tl.store converts to the cache dtype
+        key, value = key.to(k_cache.dtype), value.to(k_cache.dtype)
+    num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
+    slots = _index_tensor(slot_mapping.reshape(-1), fn, "slot_mapping")
+    lib = _lib.load()
+    with _on_device(dev):
+        st = lib.mkv_store_kvcache(
+            key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1),
+            value.stride(0), value.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
+            num_blocks, block_size, slots.data_ptr(), _INDEX[slots.dtype], num_tokens,
+            num_kv_heads, head_dim, _DTYPES[k_cache.dtype], None, _stream(dev))
+    _lib.check(fn, st)
+
+
+_calib_work: dict[int, torch.Tensor] = {}
+
+
+def _calibration_work(device: torch.device) -> torch.Tensor:
+    """Per-device 16-byte scratch of the FP8 calibration kernel (zero between calls)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _calib_work.get(idx)
+    if buf is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(
+                "store_kvcache_fp8: run one FP8 append eagerly on this device before CUDA-graph "
+                "capture (its calibration scratch must be allocated outside the capture)")
+        buf = torch.zeros(_lib.FP8_CALIB_WORK_BYTES, dtype=torch.uint8, device=device)
+        _calib_work[idx] = buf
+    return buf
+
+
+def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                      v_cache: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
+                      slot_mapping: torch.Tensor, block_size: int, kv_cache_dtype: str) -> None:
+    """Quantises key/value to FP8 E4M3 with per-tensor scales and stores them into the
+    paged caches. While a scale still holds the sentinel 1.0 it is first calibrated from
+    this batch (bf16/fp16/fp32 amax / 448, computed on the device); afterwards it stays
+    frozen. Reference: attention.py:281-333 (calibration 315-323, kernel 118-191)."""
+    fn = "store_kvcache_fp8"
+    if kv_cache_dtype != "fp8_per_tensor":
+        raise NotImplementedError(
+            f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented (only 'fp8_per_tensor')")
+    num_tokens, num_kv_heads, head_dim = key.shape
+    dev = _require_cuda(fn, key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping)
+    if key.dtype not in _FLOAT_IO or value.dtype != key.dtype:
+        raise ValueError(f"{fn}: key/value must share a float32/float16/bfloat16 dtype")
+    if k_cache.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise ValueError(f"{fn}: caches must be float8_e4m3fn (got {k_cache.dtype})")
+    if k_scale.dtype != torch.float32 or v_scale.dtype != torch.float32 or \
+            k_scale.numel() < 1 or v_scale.numel() < 1:
+        raise ValueError(f"{fn}: k_scale/v_scale must be float32 tensors with one element")
+    assert slot_mapping.numel() == num_tokens, "Slot mapping size must match number of tokens"
+    key, value = _row_major_tokens(key), _row_major_tokens(value)
+    num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
+    slots = _index_tensor(slot_mapping.reshape(-1), fn, "slot_mapping")
+    lib = _lib.load()
+    dt = _DTYPES[key.dtype]
+    with _on_device(dev):
+        stream = _stream(dev)
+        work = _calibration_work(dev)
+        st = lib.mkv_calibrate_fp8_scales(
+            key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
+            value.stride(1), num_tokens, num_kv_heads, head_dim, dt, k_scale.data_ptr(),
+            v_scale.data_ptr(), work.data_ptr(), stream)
+        _lib.check("mkv_calibrate_fp8_scales", st)
+        st = lib.mkv_store_kvcache_fp8(
+            key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
+            value.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_scale.data_ptr(),
+            v_scale.data_ptr(), num_blocks, block_size, slots.data_ptr(), _INDEX[slots.dtype],
+            num_tokens, num_kv_heads, head_dim, dt, None, stream)
+    _lib.check(fn, st)
+
+
+# ---------------------------------------------------------------------------------- decode
+def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, context_lens,
+            scale, num_heads, num_kv_heads, head_dim, block_size, num_splits: int = 0):
+    if query.dim() != 3 or query.shape[1] != num_heads or query.shape[2] != head_dim:
+        raise ValueError(f"{fn}: query must be (batch, {num_heads}, {head_dim}), got {tuple(query.shape)}")
+    if query.dtype not in _FLOAT_IO:
+        raise ValueError(f"{fn}: unsupported query dtype {query.dtype}")
+    tensors = [query, k_cache, v_cache, block_tables, context_lens]
+    if k_scale is not None:
+        tensors += [k_scale, v_scale]
+    dev = _require_cuda(fn, *tensors)
+    batch_size = query.shape[0]
+    max_num_blocks = block_tables.shape[1]
+    query = query if query.stride(-1) == 1 else query.contiguous()
+    output = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    if batch_size == 0:
+        return output
+    if block_tables.stride(-1) != 1:
+        block_tables = block_tables.contiguous()
+    if block_tables.dtype not in _INDEX:
+        raise ValueError(f"{fn}: block_tables must be int32 or int64 (got {block_tables.dtype})")
+    lens = _index_tensor(context_lens.reshape(-1), fn, "context_lens")
+    if lens.numel() != batch_size or block_tables.shape[0] < batch_size:
+        raise ValueError(f"{fn}: context_lens/block_tables do not cover {batch_size} sequences")
+    num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
+    lib = _lib.load()
+    ws_bytes = lib.mkv_paged_decode_workspace_bytes(batch_size, num_heads, num_kv_heads, head_dim,
+                                                    block_size, max_num_blocks, num_splits)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
+    ws_ptr = ws.data_ptr() if ws is not None else None
+    with _on_device(dev):
+        stream = _stream(dev)
+        if k_scale is None:
+            st = lib.mkv_paged_decode(
+                query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
+                k_cache.data_ptr(), v_cache.data_ptr(), _DTYPES[k_cache.dtype], num_blocks,
+                block_size, block_tables.data_ptr(), _INDEX[block_tables.dtype],
+                block_tables.stride(0), max_num_blocks, lens.data_ptr(), _INDEX[lens.dtype],
+                batch_size, num_heads, num_kv_heads, head_dim, float(scale), output.data_ptr(),
+                output.stride(0), output.stride(1), ws_ptr, ws_bytes, num_splits, None, stream)
+        else:
+            st = lib.mkv_paged_decode_fp8(
+                query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
+                k_cache.data_ptr(), v_cache.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
+                num_blocks, block_size, block_tables.data_ptr(), _INDEX[block_tables.dtype],
+                block_tables.stride(0), max_num_blocks, lens.data_ptr(), _INDEX[lens.dtype],
+                batch_size, num_heads, num_kv_heads, head_dim, float(scale), output.data_ptr(),
+                output.stride(0), output.stride(1), ws_ptr, ws_bytes, num_splits, None, stream)
+    _lib.check(fn, st)
+    return output
+
+
+def paged_attention_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                           block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
+                           num_heads: int, num_kv_heads: int, head_dim: int,
+                           block_size: int, num_splits: int = 0) -> torch.Tensor:
+    """Decode attention of query (batch, num_heads, head_dim) over the paged K/V of each
+    sequence: tokens t < context_lens[b] on pages block_tables[b, t // block_size],
+    GQA kv head = h // (num_heads // num_kv_heads). Returns (batch, num_heads, head_dim)
+    in the query dtype. Reference: attention.py:895-950 (kernel 517-646).
+    `num_splits` (0 = automatic) forces the split-KV count; it is not in the reference."""
+    if k_cache.dtype == torch.float8_e4m3fn:
+        raise ValueError("paged_attention_decode: FP8 caches go through paged_attention_decode_quantized")
+    return _decode("paged_attention_decode", query, k_cache, v_cache, None, None, block_tables,
+                   context_lens, scale, num_heads, num_kv_heads, head_dim, block_size, num_splits)
+
+
+def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
+                                     v_cache: torch.Tensor, k_scale: torch.Tensor,
+                                     v_scale: torch.Tensor, block_tables: torch.Tensor,
+                                     context_lens: torch.Tensor, scale: float, num_heads: int,
+                                     num_kv_heads: int, head_dim: int, block_size: int,
+                                     kv_cache_dtype: str, num_splits: int = 0) -> torch.Tensor:
+    """Decode attention over an FP8 E4M3 paged cache with per-tensor scales: pages are
+    dequantised as float(e4m3) * scale while they are loaded. Reference:
+    attention.py:1213-1268 with paged_attention_decode_fp8_kernel (953-1121)."""
+    fn = "paged_attention_decode_quantized"
+    if kv_cache_dtype != "fp8_per_tensor":
+        raise NotImplementedError(
+            f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented (only 'fp8_per_tensor')")
+    if k_cache.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise ValueError(f"{fn}: caches must be float8_e4m3fn (got {k_cache.dtype})")
+    if k_scale.dtype != torch.float32 or v_scale.dtype != torch.float32:
+        raise ValueError(f"{fn}: k_scale/v_scale must be float32")
+    return _decode(fn, query, k_cache, v_cache, k_scale, v_scale, block_tables, context_lens,
+                   scale, num_heads, num_kv_heads, head_dim, block_size, num_splits)
+
+
+# ---------------------------------------------------------------------------------- module
+class Attention(nn.Module):
+    """Attention layer with a paged KV cache (reference attention.py:1617-1807).
+
+    The model runner injects `k_cache`/`v_cache` (per-layer views of one
+    (2, L, num_blocks, block_size, KVH, D) allocation), `kv_cache_dtype`, and for FP8 the
+    per-layer `k_scale`/`v_scale` (float32, shape (1,), initialised to the sentinel 1.0).
+    `forward` appends the step's K/V at context.slot_mapping and, for a decode batch,
+    returns (batch, num_heads * head_dim). Prefill attention is outside this library."""
+
+    def __init__(self, num_heads: int, head_dim: int, scale: float = 1.0,
+                 num_kv_heads: int | None = None, block_size: int = 16):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.scale = scale
+        self.num_kv_heads = num_kv_heads if num_kv_heads is not None else num_heads
+        self.block_size = block_size
+        self.k_cache = self.v_cache = torch.tensor([])
+        self.kv_cache_dtype = "auto"
+        self.k_scale = None
+        self.v_scale = None
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        context = get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        fp8 = self.kv_cache_dtype == "fp8_per_tensor"
+        if self.kv_cache_dtype not in ("auto", "fp8_per_tensor"):
+            raise NotImplementedError(f"kv_cache_dtype {self.kv_cache_dtype!r} is not implemented")
+        if k_cache.numel() > 0 and v_cache.numel() > 0 and context.slot_mapping is not None:
+            if k.dim() == 4:
+                b, n, kvh, d = k.shape
+                k, v = k.reshape(b * n, kvh, d), v.reshape(b * n, kvh, d)
+            if fp8:
+                store_kvcache_fp8(k, v, k_cache, v_cache, self.k_scale, self.v_scale,
+                                  context.slot_mapping, self.block_size, self.kv_cache_dtype)
+            else:
+                store_kvcache(k, v, k_cache, v_cache, context.slot_mapping, self.block_size)
+        scale = self.scale / (self.head_dim ** 0.5)
+        if context.is_prefill:
+            raise NotImplementedError(
+                "prefill / mixed-batch attention is not part of this library (decode hot path only)")
+        if fp8:
+            o = paged_attention_decode_quantized(
+                q, k_cache, v_cache, self.k_scale, self.v_scale, context.block_tables,
+                context.context_lens, scale, self.num_heads, self.num_kv_heads, self.head_dim,
+                self.block_size, self.kv_cache_dtype)
+        else:
+            o = paged_attention_decode(
+                q, k_cache, v_cache, context.block_tables, context.context_lens, scale,
+                self.num_heads, self.num_kv_heads, self.head_dim, self.block_size)
+        return o.reshape(o.shape[0], self.num_heads * self.head_dim)

@@ -1,0 +1,215 @@
+"""Generates tests/golden/*.npz by running the reference's own code on seeded inputs.
+
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py [--reference-src DIR]
+
+DIR is the reference's `src` directory (heart1128/mini-kvllm; default
+/root/reference/src); its parent must hold benchmark_decoding.py. The script needs
+the reference only while it runs: the fixtures it writes carry the inputs (or the
+seed and a SHA-256 of them) and the reference's outputs, and the tests read only
+those files.
+
+What runs, per fixture (all on the CPU):
+  append_bf16      store_kvcache (attention.py:67), Triton kernel interpreted
+  append_fp8       store_kvcache_fp8 (attention.py:281), per-tensor mode, twice
+                   (calibration on the first call, frozen scale on the second). The
+                   Triton interpreter's fp32->e4m3 cast is known to be wrong for values
+                   that round up into the next binade, so the kernel is run with float32
+                   "caches": it then stores clamp(x / scale, -448, 448) as fp32, and the
+                   fixture keeps those values plus the scales the reference calibrated.
+  decode_small     paged_attention_decode (attention.py:895), interpreted, fp32, with
+                   ragged lengths, -1 padding and a -1 page inside one context
+  decode_fp8       paged_attention_decode_quantized(..., 'fp8_per_tensor')
+                   (attention.py:1213) on e4m3-representable values held in fp32 caches
+  decode_config1   decode_torch_optimized (benchmark_decoding.py:145-198, loaded from
+                   the file's source text because the module's imports are stale) on
+                   B=4, H=16, KVH=8, D=128, BS=16, ctx ~ U[64, 512]
+"""
+from __future__ import annotations
+
+import argparse
+import ast
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _load_reference(src: str):
+    os.environ.setdefault("TRITON_INTERPRET", "1")
+    sys.path.insert(0, src)
+    import torch  # noqa: F401
+    from myvllm.layers import attention as ref_attn  # the reference module itself
+
+    bench_path = os.path.join(os.path.dirname(src), "benchmark_decoding.py")
+    text = open(bench_path).read()
+    tree = ast.parse(text)
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "decode_torch_optimized")
+    mod = ast.Module(body=[fn], type_ignores=[])
+    ns: dict = {"torch": __import__("torch")}
+    exec(compile(mod, bench_path, "exec"), ns)
+    return ref_attn, ns["decode_torch_optimized"]
+
+
+def _sha(*arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def _bf16_bits(t):
+    import torch
+    return t.contiguous().view(torch.int16).numpy().astype(np.uint16)
+
+
+def make_append_bf16(ref_attn, rng):
+    import torch
+    T, KVH, D, NB, BS = 37, 2, 32, 12, 4
+    key = torch.from_numpy(rng.standard_normal((T, KVH, D)).astype(np.float32)).to(torch.bfloat16)
+    value = torch.from_numpy(rng.standard_normal((T, KVH, D)).astype(np.float32)).to(torch.bfloat16)
+    slots = torch.from_numpy(rng.permutation(NB * BS)[:T].astype(np.int64))
+    slots[[3, 10, 11, 30]] = -1
+    kc0 = torch.from_numpy(rng.standard_normal((NB, BS, KVH, D)).astype(np.float32)).to(torch.bfloat16)
+    vc0 = torch.from_numpy(rng.standard_normal((NB, BS, KVH, D)).astype(np.float32)).to(torch.bfloat16)
+    kc, vc = kc0.clone(), vc0.clone()
+    ref_attn.store_kvcache(key, value, kc, vc, slots, BS)
+    return dict(key=_bf16_bits(key), value=_bf16_bits(value), slot_mapping=slots.numpy(),
+                k_cache_in=_bf16_bits(kc0), v_cache_in=_bf16_bits(vc0),
+                k_cache_out=_bf16_bits(kc), v_cache_out=_bf16_bits(vc),
+                block_size=np.int64(BS))
+
+
+def make_append_fp8(ref_attn, rng):
+    import torch
+    T, KVH, D, NB, BS = 24, 2, 32, 8, 4
+    out = {}
+    kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float32)
+    vc = torch.zeros(NB, BS, KVH, D, dtype=torch.float32)
+    k_scale = torch.ones(1, dtype=torch.float32)
+    v_scale = torch.ones(1, dtype=torch.float32)
+    perm = rng.permutation(NB * BS)
+    for call in range(2):
+        x = rng.standard_normal((2, T, KVH, D)).astype(np.float32)
+        mask = rng.random((2, T, KVH, D)) < 0.01
+        x = np.where(mask, x * 20.0, x)  # 0.1%-1% outliers x20
+        key = torch.from_numpy(x[0]).to(torch.bfloat16)
+        value = torch.from_numpy(x[1]).to(torch.bfloat16)
+        # second call: 24 slots overlapping the first call's last 16 (overwrites)
+        lo = 0 if call == 0 else NB * BS - T
+        slots = torch.from_numpy(perm[lo:lo + T].astype(np.int64))
+        slots[[1, 7]] = -1
+        ref_attn.store_kvcache_fp8(key, value, kc, vc, k_scale, v_scale, slots, BS, "fp8_per_tensor")
+        out[f"key{call}"] = _bf16_bits(key)
+        out[f"value{call}"] = _bf16_bits(value)
+        out[f"slot_mapping{call}"] = slots.numpy()
+        out[f"k_scale{call}"] = k_scale.numpy().copy()
+        out[f"v_scale{call}"] = v_scale.numpy().copy()
+        out[f"k_quot{call}"] = kc.numpy().copy()  # clamp(x/scale) as fp32, before the e4m3 cast
+        out[f"v_quot{call}"] = vc.numpy().copy()
+    out["block_size"] = np.int64(BS)
+    return out
+
+
+def _paged_inputs(rng, B, H, KVH, D, BS, lens, max_blocks, extra_blocks=3):
+    import torch
+    need = [(n + BS - 1) // BS for n in lens]
+    NB = sum(need) + extra_blocks
+    perm = rng.permutation(NB)
+    bt = np.full((B, max_blocks), -1, dtype=np.int32)
+    pos = 0
+    for b, nb in enumerate(need):
+        nb_in = min(nb, max_blocks)
+        bt[b, :nb_in] = perm[pos:pos + nb_in]
+        pos += nb
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    kc = rng.standard_normal((NB, BS, KVH, D)).astype(np.float32)
+    vc = rng.standard_normal((NB, BS, KVH, D)).astype(np.float32)
+    return q, kc, vc, bt, np.asarray(lens, dtype=np.int64)
+
+
+def make_decode_small(ref_attn, rng):
+    import torch
+    B, H, KVH, D, BS, MAXB = 8, 4, 2, 32, 4, 10
+    # 40 = MAXB*BS; 4 = one full block; 45 > MAXB*BS (tokens 40..44 have no table
+    # entry and are dropped); 0 = no visible token (the reference returns 0/0 = NaN)
+    lens = [1, 4, 17, 40, 9, 23, 45, 0]
+    q, kc, vc, bt, cl = _paged_inputs(rng, B, H, KVH, D, BS, lens, MAXB)
+    bt[4, 1] = -1  # a -1 page inside a context: its 4 tokens carry no weight
+    scale = 1.0 / np.sqrt(D)
+    out = ref_attn.paged_attention_decode(
+        torch.from_numpy(q), torch.from_numpy(kc), torch.from_numpy(vc), torch.from_numpy(bt),
+        torch.from_numpy(cl), float(scale), H, KVH, D, BS)
+    return dict(query=q, k_cache=kc, v_cache=vc, block_tables=bt, context_lens=cl,
+                scale=np.float64(scale), num_heads=np.int64(H), num_kv_heads=np.int64(KVH),
+                block_size=np.int64(BS), out=out.numpy())
+
+
+def make_decode_fp8(ref_attn, rng):
+    import torch
+    B, H, KVH, D, BS, MAXB = 4, 8, 2, 32, 8, 6
+    lens = [5, 48, 20, 33]
+    q, kc, vc, bt, cl = _paged_inputs(rng, B, H, KVH, D, BS, lens, MAXB)
+    k8 = torch.from_numpy(kc * 40).to(torch.float8_e4m3fn)  # e4m3 codes
+    v8 = torch.from_numpy(vc * 40).to(torch.float8_e4m3fn)
+    ks = torch.tensor([0.0213623046875], dtype=torch.float32)
+    vs = torch.tensor([0.031982421875], dtype=torch.float32)
+    scale = 1.0 / np.sqrt(D)
+    out = ref_attn.paged_attention_decode_quantized(
+        torch.from_numpy(q), k8.float(), v8.float(), ks, vs, torch.from_numpy(bt),
+        torch.from_numpy(cl), float(scale), H, KVH, D, BS, "fp8_per_tensor")
+    return dict(query=q, k_cache_e4m3=k8.view(torch.uint8).numpy(),
+                v_cache_e4m3=v8.view(torch.uint8).numpy(), k_scale=ks.numpy(), v_scale=vs.numpy(),
+                block_tables=bt, context_lens=cl, scale=np.float64(scale), num_heads=np.int64(H),
+                num_kv_heads=np.int64(KVH), block_size=np.int64(BS), out=out.numpy())
+
+
+def config1_inputs(seed: int = 0):
+    """BASELINE config 1 (shared with tests): B=4, H=16, KVH=8, D=128, BS=16,
+    ctx ~ U[64, 512], pages a random permutation, q/K/V ~ N(0, 1) fp32."""
+    rng = np.random.default_rng(seed)
+    B, H, KVH, D, BS, MAXB = 4, 16, 8, 128, 16, 32
+    lens = rng.integers(64, 513, size=B).tolist()
+    q, kc, vc, bt, cl = _paged_inputs(rng, B, H, KVH, D, BS, lens, MAXB, extra_blocks=0)
+    return dict(query=q, k_cache=kc, v_cache=vc, block_tables=bt, context_lens=cl,
+                num_heads=H, num_kv_heads=KVH, head_dim=D, block_size=BS)
+
+
+def make_decode_config1(decode_torch_optimized):
+    import torch
+    inp = config1_inputs(0)
+    D = inp["head_dim"]
+    scale = 1.0 / np.sqrt(D)
+    out = decode_torch_optimized(
+        torch.from_numpy(inp["query"]), torch.from_numpy(inp["k_cache"]),
+        torch.from_numpy(inp["v_cache"]), torch.from_numpy(inp["block_tables"]),
+        torch.from_numpy(inp["context_lens"]), float(scale), inp["num_heads"],
+        inp["num_kv_heads"], D, inp["block_size"])
+    digest = _sha(inp["query"], inp["k_cache"], inp["v_cache"], inp["block_tables"], inp["context_lens"])
+    return dict(seed=np.int64(0), inputs_sha256=np.array(digest), scale=np.float64(scale),
+                context_lens=inp["context_lens"], out=out.numpy())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-src", default="/root/reference/src")
+    args = ap.parse_args()
+    ref_attn, dto = _load_reference(args.reference_src)
+    jobs = [
+        ("append_bf16", lambda: make_append_bf16(ref_attn, np.random.default_rng(101))),
+        ("append_fp8", lambda: make_append_fp8(ref_attn, np.random.default_rng(202))),
+        ("decode_small", lambda: make_decode_small(ref_attn, np.random.default_rng(303))),
+        ("decode_fp8", lambda: make_decode_fp8(ref_attn, np.random.default_rng(404))),
+        ("decode_config1", lambda: make_decode_config1(dto)),
+    ]
+    for name, job in jobs:
+        data = job()
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **data)
+        print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+
+
+if __name__ == "__main__":
+    main()

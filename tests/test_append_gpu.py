@@ -1,0 +1,221 @@
+"""KV append on the GPU through the C ABI (Python wrappers) against the CPU oracle:
+bf16/fp16/fp32 copies and FP8 E4M3 quantisation must be bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, mkv_module
+from oracle import fp8_scale_ref, quantize_fp8_ref, store_kvcache_fp8_ref, store_kvcache_ref
+
+pytestmark = pytest.mark.gpu
+attn = mkv_module("layers.attention")
+lib_mod = mkv_module("_lib")
+wl = mkv_module("workloads")
+
+
+def _case(T, KVH, D, NB, BS, dtype, seed, neg=(), slot_dtype=torch.int64):
+    g = torch.Generator().manual_seed(seed)
+    key = torch.randn(T, KVH, D, generator=g).to(dtype)
+    value = torch.randn(T, KVH, D, generator=g).to(dtype)
+    slots = torch.randperm(NB * BS, generator=g)[:T].to(slot_dtype)
+    for i in neg:
+        slots[i] = -1
+    kc = torch.randn(NB, BS, KVH, D, generator=g).to(dtype)
+    vc = torch.randn(NB, BS, KVH, D, generator=g).to(dtype)
+    return key, value, slots, kc, vc
+
+
+def _bits(t):
+    return t.view(torch.uint8) if t.element_size() == 1 else t.view(torch.int16 if t.element_size() == 2 else torch.int32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D,BS", [(128, 16), (128, 256), (64, 1), (40, 8), (20, 4)])
+@pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
+def test_store_kvcache_bit_exact(dtype, D, BS, slot_dtype):
+    key, value, slots, kc, vc = _case(77, 4, D, 40, BS, dtype, 1, neg=(0, 5, 76), slot_dtype=slot_dtype)
+    ek, ev = kc.clone(), vc.clone()
+    store_kvcache_ref(key, value, ek, ev, slots, BS)
+    dk, dv = kc.cuda(), vc.cuda()
+    attn.store_kvcache(key.cuda(), value.cuda(), dk, dv, slots.cuda(), BS)
+    assert torch.equal(_bits(dk.cpu()), _bits(ek)) and torch.equal(_bits(dv.cpu()), _bits(ev))
+
+
+def test_store_kvcache_strided_source():
+    """K/V as column slices of a fused qkv projection (token stride != KVH*D)."""
+    T, H, KVH, D, BS, NB = 50, 8, 2, 128, 16, 8
+    qkv = torch.randn(T, (H + 2 * KVH) * D, dtype=torch.bfloat16, device="cuda")
+    k = qkv[:, H * D:(H + KVH) * D].view(T, KVH, D)
+    v = qkv[:, (H + KVH) * D:].view(T, KVH, D)
+    assert not k.is_contiguous()
+    slots = torch.randperm(NB * BS)[:T].cuda()
+    kc = torch.zeros(NB, BS, KVH, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    attn.store_kvcache(k, v, kc, vc, slots, BS)
+    ek, ev = torch.zeros_like(kc).cpu(), torch.zeros_like(vc).cpu()
+    store_kvcache_ref(k.cpu(), v.cpu(), ek, ev, slots.cpu(), BS)
+    assert torch.equal(kc.cpu().view(torch.int16), ek.view(torch.int16))
+    assert torch.equal(vc.cpu().view(torch.int16), ev.view(torch.int16))
+
+
+def test_out_of_range_slots_are_skipped_and_counted():
+    lib = lib_mod.load()
+    T, KVH, D, NB, BS = 6, 2, 128, 4, 16
+    key = torch.randn(T, KVH, D, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(NB, BS, KVH, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    slots = torch.tensor([0, NB * BS, 5, 10 ** 9, -1, 63], dtype=torch.int64, device="cuda")
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = lib.mkv_store_kvcache(key.data_ptr(), key.data_ptr(), KVH * D, D, KVH * D, D,
+                               kc.data_ptr(), vc.data_ptr(), NB, BS, slots.data_ptr(), 1, T, KVH,
+                               D, lib_mod.DTYPE_BF16, counter.data_ptr(),
+                               torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert int(counter) == 2
+    flat = kc.view(-1, KVH, D)
+    assert torch.equal(flat[0], key[0]) and torch.equal(flat[5], key[2]) and torch.equal(flat[63], key[5])
+    assert int((flat.float().abs().sum(dim=(1, 2)) != 0).sum()) == 3
+
+
+def test_golden_append_bf16_through_cuda():
+    g = golden("append_bf16")
+    b = lambda a: torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+    kc, vc = b(g["k_cache_in"]).cuda(), b(g["v_cache_in"]).cuda()
+    attn.store_kvcache(b(g["key"]).cuda(), b(g["value"]).cuda(), kc, vc,
+                       torch.from_numpy(g["slot_mapping"]).cuda(), int(g["block_size"]))
+    assert np.array_equal(kc.cpu().view(torch.int16).numpy().astype(np.uint16), g["k_cache_out"])
+    assert np.array_equal(vc.cpu().view(torch.int16).numpy().astype(np.uint16), g["v_cache_out"])
+
+
+def test_config2_append_bf16_bit_exact():
+    w = wl.config2(seed=3)
+    KVH, D = w.key.shape[1:]
+    kc = torch.zeros(w.num_blocks, w.block_size, KVH, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    attn.store_kvcache(w.key, w.value, kc, vc, w.slot_mapping, w.block_size)
+    ek, ev = torch.zeros_like(kc).cpu(), torch.zeros_like(vc).cpu()
+    store_kvcache_ref(w.key.cpu(), w.value.cpu(), ek, ev, w.slot_mapping.cpu(), w.block_size)
+    assert torch.equal(kc.cpu().view(torch.int16), ek.view(torch.int16))
+    assert torch.equal(vc.cpu().view(torch.int16), ev.view(torch.int16))
+
+
+# ------------------------------------------------------------------------------ FP8
+def _torch_cuda_scale(x):
+    """The reference's own expression (attention.py:319-320) evaluated by torch on CUDA."""
+    return float((x.abs().amax().clamp(min=1e-8) / 448.0).item())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("mag", [1.0, 37.0, 1e-3, 0.0])
+def test_fp8_calibration_matches_torch_cuda(dtype, mag):
+    T, KVH, D, NB, BS = 300, 8, 128, 64, 16
+    for seed in range(4):
+        g = torch.Generator().manual_seed(seed)
+        key = (torch.randn(T, KVH, D, generator=g) * mag).to(dtype).cuda()
+        value = (torch.rand(T, KVH, D, generator=g) * mag * 3).to(dtype).cuda()
+        slots = torch.randperm(NB * BS, generator=g)[:T].cuda()
+        kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float8_e4m3fn, device="cuda")
+        vc = torch.zeros_like(kc)
+        ks = torch.ones(1, device="cuda")
+        vs = torch.ones(1, device="cuda")
+        attn.store_kvcache_fp8(key, value, kc, vc, ks, vs, slots, BS, "fp8_per_tensor")
+        assert float(ks) == _torch_cuda_scale(key) == fp8_scale_ref(key.cpu())
+        assert float(vs) == _torch_cuda_scale(value) == fp8_scale_ref(value.cpu())
+
+
+def test_fp8_scale_frozen_after_first_calibration():
+    T, KVH, D, NB, BS = 64, 2, 128, 16, 16
+    kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float8_e4m3fn, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.ones(1, device="cuda")
+    vs = torch.tensor([0.25], device="cuda")  # already calibrated: must stay
+    first = torch.randn(T, KVH, D, dtype=torch.bfloat16, device="cuda")
+    attn.store_kvcache_fp8(first, first, kc, vc, ks, vs, torch.arange(T, device="cuda"), BS,
+                           "fp8_per_tensor")
+    s0 = float(ks)
+    assert s0 == fp8_scale_ref(first.cpu()) and float(vs) == 0.25
+    bigger = first * 100
+    attn.store_kvcache_fp8(bigger, bigger, kc, vc, ks, vs, torch.arange(T, device="cuda"), BS,
+                           "fp8_per_tensor")
+    assert float(ks) == s0 and float(vs) == 0.25
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [128, 64, 48])
+def test_store_kvcache_fp8_bit_exact(dtype, D):
+    T, KVH, NB, BS = 200, 4, 32, 16
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(2, T, KVH, D, generator=g)
+    x = torch.where(torch.rand(x.shape, generator=g) < 0.01, x * 20, x).to(dtype)
+    slots = torch.randperm(NB * BS, generator=g)[:T]
+    slots[[3, 99]] = -1
+    kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float8_e4m3fn)
+    vc = torch.zeros_like(kc)
+    ks, vs = torch.ones(1), torch.ones(1)
+    store_kvcache_fp8_ref(x[0], x[1], kc, vc, ks, vs, slots, BS)
+    dkc, dvc = torch.zeros_like(kc).cuda(), torch.zeros_like(vc).cuda()
+    dks, dvs = torch.ones(1, device="cuda"), torch.ones(1, device="cuda")
+    attn.store_kvcache_fp8(x[0].cuda(), x[1].cuda(), dkc, dvc, dks, dvs, slots.cuda(), BS,
+                           "fp8_per_tensor")
+    assert float(dks) == float(ks) and float(dvs) == float(vs)
+    assert torch.equal(dkc.cpu().view(torch.uint8), kc.view(torch.uint8))
+    assert torch.equal(dvc.cpu().view(torch.uint8), vc.view(torch.uint8))
+
+
+def test_fp8_quantisation_edge_values():
+    """Rounding midpoints, subnormals, saturation, signed zero, inf and NaN (NaN -> -448,
+    as Triton's tl.maximum/tl.minimum return the non-NaN operand)."""
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn).float()
+    v = torch.unique(codes[torch.isfinite(codes)])
+    mids = (v[1:] + v[:-1]) / 2
+    vals = torch.cat([v, mids, torch.nextafter(mids, torch.full_like(mids, 1e9)),
+                      torch.nextafter(mids, torch.full_like(mids, -1e9)),
+                      torch.tensor([0.0, -0.0, 500.0, -1e6, float("inf"), float("-inf"), float("nan")])])
+    D, KVH, BS = 128, 1, 4
+    n = (vals.numel() + D - 1) // D * D
+    x = torch.zeros(n)
+    x[:vals.numel()] = vals
+    T = n // D
+    key = x.view(T, KVH, D)
+    scale = 0.5  # exact: x / 0.5 = 2x
+    expect = quantize_fp8_ref(key, scale)
+    kc = torch.zeros((T + BS - 1) // BS, BS, KVH, D, dtype=torch.float8_e4m3fn, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.tensor([scale], device="cuda")
+    attn.store_kvcache_fp8(key.cuda(), key.cuda(), kc, vc, ks, ks.clone(), torch.arange(T, device="cuda"),
+                           BS, "fp8_per_tensor")
+    got = kc.view(-1, KVH, D)[:T].cpu()
+    assert torch.equal(got.view(torch.uint8), expect.view(torch.uint8))
+
+
+def test_golden_append_fp8_through_cuda():
+    g = golden("append_fp8")
+    b = lambda a: torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+    BS = int(g["block_size"])
+    shape = g["k_quot0"].shape
+    kc = torch.zeros(shape, dtype=torch.float8_e4m3fn, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks, vs = torch.ones(1, device="cuda"), torch.ones(1, device="cuda")
+    for call in (0, 1):
+        attn.store_kvcache_fp8(b(g[f"key{call}"]).cuda(), b(g[f"value{call}"]).cuda(), kc, vc, ks, vs,
+                               torch.from_numpy(g[f"slot_mapping{call}"]).cuda(), BS, "fp8_per_tensor")
+        assert float(ks) == float(g[f"k_scale{call}"][0]) and float(vs) == float(g[f"v_scale{call}"][0])
+    exp_k = torch.from_numpy(g["k_quot1"]).to(torch.float8_e4m3fn).view(torch.uint8)
+    exp_v = torch.from_numpy(g["v_quot1"]).to(torch.float8_e4m3fn).view(torch.uint8)
+    assert torch.equal(kc.cpu().view(torch.uint8), exp_k) and torch.equal(vc.cpu().view(torch.uint8), exp_v)
+
+
+def test_config2_append_fp8_bit_exact():
+    w = wl.config2(seed=5)
+    KVH, D = w.key.shape[1:]
+    kc = torch.zeros(w.num_blocks, w.block_size, KVH, D, dtype=torch.float8_e4m3fn, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks, vs = torch.ones(1, device="cuda"), torch.ones(1, device="cuda")
+    attn.store_kvcache_fp8(w.key, w.value, kc, vc, ks, vs, w.slot_mapping, w.block_size, "fp8_per_tensor")
+    ek, ev = torch.zeros_like(kc).cpu(), torch.zeros_like(vc).cpu()
+    eks, evs = torch.ones(1), torch.ones(1)
+    store_kvcache_fp8_ref(w.key.cpu(), w.value.cpu(), ek, ev, eks, evs, w.slot_mapping.cpu(), w.block_size)
+    assert float(ks) == float(eks) and float(vs) == float(evs)
+    assert torch.equal(kc.cpu().view(torch.uint8), ek.view(torch.uint8))
+    assert torch.equal(vc.cpu().view(torch.uint8), ev.view(torch.uint8))

@@ -1,0 +1,146 @@
+"""C-ABI checks that need no GPU: libmkv.so loads, exports every symbol include/mkv.h
+declares, and its host-side logic (split planning, workspace sizing, argument
+validation) behaves; no call here reaches a CUDA API."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO, mkv_module
+
+lib_mod = mkv_module("_lib")
+
+
+def declared_symbols():
+    text = open(os.path.join(REPO, "include", "mkv.h")).read()
+    return re.findall(r"MKV_API\s+[\w\s\*]+?\b(mkv_\w+)\s*\(", text)
+
+
+def test_header_and_binding_agree():
+    assert sorted(declared_symbols()) == sorted(lib_mod.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(lib_mod.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_header_constants_match_binding():
+    text = open(os.path.join(REPO, "include", "mkv.h")).read()
+    consts = dict(re.findall(r"#define (MKV_\w+) (\d+)", text))
+    assert int(consts["MKV_DTYPE_F32"]) == lib_mod.DTYPE_F32
+    assert int(consts["MKV_DTYPE_F16"]) == lib_mod.DTYPE_F16
+    assert int(consts["MKV_DTYPE_BF16"]) == lib_mod.DTYPE_BF16
+    assert int(consts["MKV_DTYPE_FP8_E4M3"]) == lib_mod.DTYPE_FP8_E4M3
+    assert int(consts["MKV_INDEX_I64"]) == lib_mod.INDEX_I64
+    assert int(consts["MKV_FP8_CALIB_WORK_BYTES"]) == lib_mod.FP8_CALIB_WORK_BYTES
+    assert int(consts["MKV_ERR_WORKSPACE"]) == lib_mod.ERR_WORKSPACE
+
+
+def test_version_and_status_strings():
+    lib = lib_mod.load()
+    assert re.fullmatch(rb"\d+\.\d+\.\d+", lib.mkv_version())
+    assert lib.mkv_status_string(0) == b"MKV_OK"
+    assert lib.mkv_status_string(3) == b"MKV_ERR_WORKSPACE"
+
+
+@pytest.mark.parametrize("B,H,KVH,BS,MAXB,expect", [
+    (256, 32, 8, 256, 32, 8),     # config 3: 1024-token chunks of an 8192-token table
+    (64, 32, 8, 256, 128, 32),    # config 4: 32768 tokens
+    (4, 16, 8, 16, 32, 4),        # config 1: small batch -> 128-token chunks
+    (256, 4, 1, 256, 32, 16),     # config 3 on one of 8 ranks (1 KV head): 512-token chunks
+    (8, 8, 8, 16, 1, 1),          # table fits one chunk -> no split
+])
+def test_split_plan(B, H, KVH, BS, MAXB, expect):
+    lib = lib_mod.load()
+    assert lib.mkv_paged_decode_num_splits(B, H, KVH, 128, BS, MAXB) == expect
+
+
+def test_workspace_bytes():
+    lib = lib_mod.load()
+    n = 256 * 32 * 8
+    acc = (n * 128 * 4 + 255) // 256 * 256
+    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 0) == acc + n * 8
+    assert lib.mkv_paged_decode_workspace_bytes(8, 8, 8, 128, 16, 1, 0) == 0
+    # a forced split count overrides the plan
+    assert lib.mkv_paged_decode_workspace_bytes(2, 4, 2, 64, 16, 8, 4) > 0
+
+
+def _decode_call(lib, **kw):
+    a = dict(q=1 << 20, qsb=4096, qsh=128, qdt=2, k=1 << 21, v=1 << 22, cdt=2, nb=10, bs=16,
+             bt=1 << 23, btt=0, btsb=4, maxb=4, cl=1 << 24, clt=1, B=2, H=8, KVH=2, D=128,
+             scale=0.1, out=1 << 25, osb=1024, osh=128, ws=None, wsb=0, ns=0)
+    a.update(kw)
+    return lib.mkv_paged_decode(a["q"], a["qsb"], a["qsh"], a["qdt"], a["k"], a["v"], a["cdt"],
+                                a["nb"], a["bs"], a["bt"], a["btt"], a["btsb"], a["maxb"],
+                                a["cl"], a["clt"], a["B"], a["H"], a["KVH"], a["D"], a["scale"],
+                                a["out"], a["osb"], a["osh"], a["ws"], a["wsb"], a["ns"], None, None)
+
+
+@pytest.mark.parametrize("kw,status,msg", [
+    (dict(H=7), 1, b"multiple of num_kv_heads"),
+    (dict(D=100), 2, b"head_dim"),
+    (dict(D=512), 2, b"head_dim"),
+    (dict(cdt=3), 1, b"mkv_paged_decode_fp8"),
+    (dict(cdt=1), 2, b"cache dtype"),
+    (dict(btt=7), 1, b"block_table_index_type"),
+    (dict(k=(1 << 21) + 8), 1, b"16-byte aligned"),
+    (dict(maxb=64, ns=0, B=512), 3, b"workspace"),
+    (dict(q=None), 1, b"null pointer"),
+    (dict(bs=0), 1, b"bad sizes"),
+])
+def test_decode_argument_validation(kw, status, msg):
+    lib = lib_mod.load()
+    assert _decode_call(lib, **kw) == status
+    assert msg in lib.mkv_last_error()
+
+
+def test_decode_empty_batch_is_noop():
+    lib = lib_mod.load()
+    assert _decode_call(lib, B=0, q=None, out=None) == 0
+
+
+def test_fp8_decode_requires_scales():
+    lib = lib_mod.load()
+    st = lib.mkv_paged_decode_fp8(1 << 20, 4096, 128, 2, 1 << 21, 1 << 22, None, None, 10, 16,
+                                  1 << 23, 0, 4, 4, 1 << 24, 1, 2, 8, 2, 128, 0.1, 1 << 25, 1024,
+                                  128, None, 0, 0, None, None)
+    assert st == 1 and b"k_scale" in lib.mkv_last_error()
+
+
+def test_store_argument_validation():
+    lib = lib_mod.load()
+    st = lib.mkv_store_kvcache(1 << 20, 1 << 21, 256, 128, 256, 128, 1 << 22, 1 << 23, 10, 16,
+                               1 << 24, 5, 4, 2, 128, 2, None, None)
+    assert st == 1 and b"slot_index_type" in lib.mkv_last_error()
+    st = lib.mkv_store_kvcache(1 << 20, 1 << 21, 256, 128, 256, 128, 1 << 22, 1 << 23, 10, 16,
+                               1 << 24, 1, 4, 2, 128, 9, None, None)
+    assert st == 2 and b"dtype" in lib.mkv_last_error()
+    assert lib.mkv_store_kvcache(None, None, 0, 0, 0, 0, None, None, 10, 16, None, 1, 0, 2, 128,
+                                 2, None, None) == 0  # zero tokens: nothing to do
+    st = lib.mkv_store_kvcache_fp8(1 << 20, 1 << 21, 256, 128, 256, 128, 1 << 22, 1 << 23,
+                                   1 << 24, 1 << 25, 10, 16, 1 << 26, 1, 4, 2, 40, 2, None, None)
+    assert st == 2 and b"multiple of 16" in lib.mkv_last_error()
+    st = lib.mkv_calibrate_fp8_scales(1 << 20, 1 << 21, 256, 128, 256, 128, 4, 2, 128, 3,
+                                      1 << 22, 1 << 23, 1 << 24, None)
+    assert st == 2 and b"f32, f16 or bf16" in lib.mkv_last_error()
+    st = lib.mkv_calibrate_fp8_scales(1 << 20, 1 << 21, 256, 128, 256, 128, 4, 2, 128, 2,
+                                      1 << 22, 1 << 23, (1 << 24) + 4, None)
+    assert st == 1 and b"8-byte aligned" in lib.mkv_last_error()
+
+
+def test_python_wrappers_reject_cpu_tensors(attn):
+    import torch
+    key = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    cache = torch.zeros(8, 16, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        attn.store_kvcache(key, key, cache, cache.clone(), torch.zeros(4, dtype=torch.long), 16)
+    q = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        attn.paged_attention_decode(q, cache, cache, torch.zeros(2, 4, dtype=torch.int32),
+                                    torch.ones(2, dtype=torch.long), 0.1, 8, 2, 128, 16)
+    with pytest.raises(NotImplementedError):
+        attn.paged_attention_decode_quantized(q, cache, cache, None, None, None, None, 0.1, 8, 2,
+                                              128, 16, "fp8_per_token_head")

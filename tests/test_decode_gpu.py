@@ -1,0 +1,260 @@
+"""Paged-attention decode on the GPU through the C ABI against the CPU oracle
+(token-level restatement of the reference kernel, float64) and, at the BASELINE
+configurations' full sizes, against a float32 torch reference on the GPU.
+
+Tolerances: bf16/fp16 outputs atol 2e-2 / rtol 1e-2 (the BASELINE bar, fp32
+accumulation); fp32 outputs atol 2e-5 / rtol 1e-4."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, mkv_module
+from oracle import paged_decode_ref
+
+pytestmark = pytest.mark.gpu
+attn = mkv_module("layers.attention")
+wl = mkv_module("workloads")
+
+TOL = {torch.float32: (2e-5, 1e-4), torch.float16: (2e-2, 1e-2), torch.bfloat16: (2e-2, 1e-2)}
+
+
+def make_paged(B, H, KVH, D, BS, lens, dtype, seed, maxb=None, fp8=False, spare=5):
+    g = torch.Generator().manual_seed(seed)
+    need = [(n + BS - 1) // BS for n in lens]
+    maxb = maxb if maxb is not None else max(max(need), 1)
+    NB = sum(need) + spare
+    perm = torch.randperm(NB, generator=g)
+    bt = torch.full((B, maxb), -1, dtype=torch.int32)
+    pos = 0
+    for b, k in enumerate(need):
+        kk = min(k, maxb)
+        bt[b, :kk] = perm[pos:pos + kk].int()
+        pos += k
+    q = torch.randn(B, H, D, generator=g).to(dtype)
+    if fp8:
+        kc = (torch.randn(NB, BS, KVH, D, generator=g) * 30).to(torch.float8_e4m3fn)
+        vc = (torch.randn(NB, BS, KVH, D, generator=g) * 30).to(torch.float8_e4m3fn)
+    else:
+        kc = torch.randn(NB, BS, KVH, D, generator=g).to(dtype)
+        vc = torch.randn(NB, BS, KVH, D, generator=g).to(dtype)
+    return q, kc, vc, bt, torch.tensor(lens, dtype=torch.int64)
+
+
+def run_cuda(q, kc, vc, bt, cl, scale, H, KVH, D, BS, ks=None, vs=None, splits=0):
+    if ks is None:
+        return attn.paged_attention_decode(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), cl.cuda(), scale,
+                                           H, KVH, D, BS, num_splits=splits).cpu()
+    return attn.paged_attention_decode_quantized(q.cuda(), kc.cuda(), vc.cuda(), ks.cuda(), vs.cuda(),
+                                                 bt.cuda(), cl.cuda(), scale, H, KVH, D, BS,
+                                                 "fp8_per_tensor", num_splits=splits).cpu()
+
+
+def assert_close(out, ref, dtype):
+    atol, rtol = TOL[dtype]
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(out), nan), "NaN pattern differs"
+    diff = (out.double() - ref)[~nan].abs()
+    bound = atol + rtol * ref[~nan].abs()
+    assert bool((diff <= bound).all()), f"max abs err {float(diff.max()):.3e}"
+
+
+LENS = [1, 16, 17, 63, 64, 65, 200, 511, 0, 300]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("H,KVH", [(8, 8), (16, 8), (32, 8), (8, 1), (32, 2), (64, 2)])
+@pytest.mark.parametrize("BS", [16, 256])
+def test_decode_matches_oracle(dtype, H, KVH, BS):
+    D = 128
+    q, kc, vc, bt, cl = make_paged(len(LENS), H, KVH, D, BS, LENS, dtype, seed=H * 7 + KVH + BS)
+    scale = 1.0 / math.sqrt(D)
+    ref = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS)
+    assert_close(run_cuda(q, kc, vc, bt, cl, scale, H, KVH, D, BS), ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("D", [64, 256, 96])
+def test_decode_other_head_dims(dtype, D):
+    H, KVH, BS = 8, 2, 16
+    q, kc, vc, bt, cl = make_paged(len(LENS), H, KVH, D, BS, LENS, dtype, seed=D)
+    scale = 1.0 / math.sqrt(D)
+    ref = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS)
+    assert_close(run_cuda(q, kc, vc, bt, cl, scale, H, KVH, D, BS), ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("H,KVH", [(32, 8), (16, 8), (32, 2)])
+def test_decode_fp8_matches_oracle(dtype, H, KVH):
+    D, BS = 128, 16
+    q, kc, vc, bt, cl = make_paged(len(LENS), H, KVH, D, BS, LENS, dtype, seed=3 + H, fp8=True)
+    ks = torch.tensor([0.0213623046875])
+    vs = torch.tensor([0.031982421875])
+    scale = 1.0 / math.sqrt(D)
+    ref = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS, k_scale=ks, v_scale=vs)
+    assert_close(run_cuda(q, kc, vc, bt, cl, scale, H, KVH, D, BS, ks, vs), ref, dtype)
+
+
+def test_decode_bf16_query_with_large_values_fp8():
+    """bf16 queries far outside f16 range still work on the FP8 path (power-of-two
+    rescaling of the query fragments)."""
+    D, BS, H, KVH = 128, 16, 8, 2
+    q, kc, vc, bt, cl = make_paged(4, H, KVH, D, BS, [40, 90, 7, 128], torch.bfloat16, seed=9, fp8=True)
+    q = (q.float() * 1e6).to(torch.bfloat16)
+    ks, vs = torch.tensor([0.01]), torch.tensor([0.02])
+    scale = 1e-7
+    ref = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS, k_scale=ks, v_scale=vs)
+    assert_close(run_cuda(q, kc, vc, bt, cl, scale, H, KVH, D, BS, ks, vs), ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 64])
+@pytest.mark.parametrize("fp8", [False, True])
+def test_decode_forced_splits(splits, fp8):
+    D, BS, H, KVH = 128, 16, 32, 8
+    lens = [1000, 1, 64, 777, 0, 129]
+    q, kc, vc, bt, cl = make_paged(len(lens), H, KVH, D, BS, lens, torch.bfloat16, seed=splits, fp8=fp8)
+    ks = torch.tensor([0.02]) if fp8 else None
+    vs = torch.tensor([0.03]) if fp8 else None
+    ref = paged_decode_ref(q, kc, vc, bt, cl, 0.0883, H, KVH, D, BS, k_scale=ks, v_scale=vs)
+    assert_close(run_cuda(q, kc, vc, bt, cl, 0.0883, H, KVH, D, BS, ks, vs, splits=splits), ref,
+                 torch.bfloat16)
+
+
+def test_decode_invalid_pages_inside_context():
+    """-1 (and out-of-range) page entries inside a context skip those tokens, like the
+    reference kernel; a context whose pages are all invalid yields NaN."""
+    D, BS, H, KVH = 128, 16, 8, 2
+    lens = [100, 50, 30]
+    q, kc, vc, bt, cl = make_paged(3, H, KVH, D, BS, lens, torch.bfloat16, seed=4)
+    bt[0, 2] = -1
+    bt[1, 1] = 10 ** 6       # out of range: treated as no page
+    bt[2, :2] = -1           # every page of sequence 2 invalid
+    ref = paged_decode_ref(q, kc, vc, bt, cl, 0.1, H, KVH, D, BS)
+    out = run_cuda(q, kc, vc, bt, cl, 0.1, H, KVH, D, BS)
+    assert torch.isnan(out[2]).all()
+    assert_close(out, ref, torch.bfloat16)
+
+
+def test_decode_noncontiguous_query_and_int32_lengths():
+    D, BS, H, KVH = 128, 16, 16, 4
+    q, kc, vc, bt, cl = make_paged(5, H, KVH, D, BS, [5, 60, 33, 100, 17], torch.bfloat16, seed=8)
+    qbig = torch.randn(5, 3 * H, D).to(torch.bfloat16)
+    qbig[:, H:2 * H] = q
+    qv = qbig.cuda()[:, H:2 * H]
+    assert not qv.is_contiguous()
+    out = attn.paged_attention_decode(qv, kc.cuda(), vc.cuda(), bt.cuda(), cl.int().cuda(), 0.09,
+                                      H, KVH, D, BS).cpu()
+    assert_close(out, paged_decode_ref(q, kc, vc, bt, cl, 0.09, H, KVH, D, BS), torch.bfloat16)
+
+
+def test_golden_decode_small_through_cuda():
+    g = golden("decode_small")
+    H, KVH, BS = int(g["num_heads"]), int(g["num_kv_heads"]), int(g["block_size"])
+    q = torch.from_numpy(g["query"])
+    out = run_cuda(q, torch.from_numpy(g["k_cache"]), torch.from_numpy(g["v_cache"]),
+                   torch.from_numpy(g["block_tables"]), torch.from_numpy(g["context_lens"]),
+                   float(g["scale"]), H, KVH, q.shape[2], BS)
+    assert_close(out, torch.from_numpy(g["out"]).double(), torch.float32)
+
+
+def test_golden_decode_fp8_through_cuda():
+    g = golden("decode_fp8")
+    H, KVH, BS = int(g["num_heads"]), int(g["num_kv_heads"]), int(g["block_size"])
+    q = torch.from_numpy(g["query"])
+    out = run_cuda(q, torch.from_numpy(g["k_cache_e4m3"]).view(torch.float8_e4m3fn),
+                   torch.from_numpy(g["v_cache_e4m3"]).view(torch.float8_e4m3fn),
+                   torch.from_numpy(g["block_tables"]), torch.from_numpy(g["context_lens"]),
+                   float(g["scale"]), H, KVH, q.shape[2], BS, torch.from_numpy(g["k_scale"]),
+                   torch.from_numpy(g["v_scale"]))
+    assert_close(out, torch.from_numpy(g["out"]).double(), torch.float32)
+
+
+def test_golden_config1_through_cuda():
+    from golden.make_golden import config1_inputs
+    g = golden("decode_config1")
+    inp = config1_inputs(int(g["seed"]))
+    out = run_cuda(torch.from_numpy(inp["query"]), torch.from_numpy(inp["k_cache"]),
+                   torch.from_numpy(inp["v_cache"]), torch.from_numpy(inp["block_tables"]),
+                   torch.from_numpy(inp["context_lens"]), float(g["scale"]), inp["num_heads"],
+                   inp["num_kv_heads"], inp["head_dim"], inp["block_size"])
+    assert_close(out, torch.from_numpy(g["out"]).double(), torch.float32)
+
+
+# ------------------------------------------------------------------ full-size configs
+def torch_reference(w, seqs):
+    """float32 attention on the GPU for the given sequences (dequantised for FP8)."""
+    H, KVH, D, BS = w.num_heads, w.num_kv_heads, w.head_dim, w.block_size
+    G = H // KVH
+    out = []
+    for b in seqs:
+        n = int(w.context_lens[b])
+        pages = w.block_tables[b, :(n + BS - 1) // BS].long()
+        K = w.k_cache[pages].reshape(-1, KVH, D)[:n].float()
+        V = w.v_cache[pages].reshape(-1, KVH, D)[:n].float()
+        if w.fp8:
+            K, V = K * w.k_scale, V * w.v_scale
+        qb = w.query[b].float().view(KVH, G, D)
+        s = torch.einsum("hgd,thd->hgt", qb, K) * w.scale
+        out.append(torch.einsum("hgt,thd->hgd", torch.softmax(s, -1), V).reshape(H, D))
+    return torch.stack(out)
+
+
+def _decode_w(w, splits=0):
+    if w.fp8:
+        return attn.paged_attention_decode_quantized(
+            w.query, w.k_cache, w.v_cache, w.k_scale, w.v_scale, w.block_tables, w.context_lens,
+            w.scale, w.num_heads, w.num_kv_heads, w.head_dim, w.block_size, "fp8_per_tensor",
+            num_splits=splits)
+    return attn.paged_attention_decode(w.query, w.k_cache, w.v_cache, w.block_tables,
+                                       w.context_lens, w.scale, w.num_heads, w.num_kv_heads,
+                                       w.head_dim, w.block_size, num_splits=splits)
+
+
+@pytest.mark.parametrize("cfg", ["config3", "config4"])
+def test_full_size_config(cfg):
+    w = getattr(wl, cfg)(seed=1, with_append=False)
+    out = _decode_w(w)
+    torch.cuda.synchronize()
+    assert not torch.isnan(out).any()
+    g = torch.Generator().manual_seed(2)
+    seqs = torch.randperm(w.query.shape[0], generator=g)[:12].tolist()
+    seqs += [int(w.context_lens.argmax()), int(w.context_lens.argmin())]
+    ref = torch_reference(w, seqs)
+    atol, rtol = TOL[torch.bfloat16]
+    assert torch.allclose(out[seqs].float(), ref, atol=atol, rtol=rtol)
+    # split-count invariance over the whole batch: one split vs the automatic plan
+    one = _decode_w(w, splits=1)
+    assert torch.allclose(one.float(), out.float(), atol=atol, rtol=rtol)
+
+
+def test_decode_step_in_cuda_graph():
+    """Append + decode (bf16 and FP8) captured once and replayed equal the eager result."""
+    for fp8 in (False, True):
+        w = wl.decode_workload("g", 16, 32, 8, 128, 16, [int(x) for x in torch.randint(1, 600, (16,))],
+                               fp8=fp8, seed=5)
+        ks = torch.ones(1, device="cuda") if fp8 else None
+        vs = torch.ones(1, device="cuda") if fp8 else None
+
+        def step():
+            if fp8:
+                attn.store_kvcache_fp8(w.new_k, w.new_v, w.k_cache, w.v_cache, ks, vs, w.slot_mapping,
+                                       w.block_size, "fp8_per_tensor")
+                return attn.paged_attention_decode_quantized(
+                    w.query, w.k_cache, w.v_cache, ks, vs, w.block_tables, w.context_lens, w.scale,
+                    w.num_heads, w.num_kv_heads, w.head_dim, w.block_size, "fp8_per_tensor")
+            attn.store_kvcache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.slot_mapping, w.block_size)
+            return _decode_w(w)
+
+        eager = step().clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = step()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(static_out, eager)

@@ -1,0 +1,124 @@
+"""Pins the CPU oracle to the reference's own outputs (tests/golden/*.npz, made by
+tests/golden/make_golden.py from heart1128/mini-kvllm's functions)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import (decode_torch_optimized, e4m3_encode_reference, fp8_scale_ref,
+                    paged_decode_ref, quantize_fp8_ref, store_kvcache_fp8_ref, store_kvcache_ref)
+
+
+def bf16(a):
+    return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+
+
+def test_append_bf16_matches_reference():
+    g = golden("append_bf16")
+    kc, vc = bf16(g["k_cache_in"]).clone(), bf16(g["v_cache_in"]).clone()
+    store_kvcache_ref(bf16(g["key"]), bf16(g["value"]), kc, vc, torch.from_numpy(g["slot_mapping"]),
+                      int(g["block_size"]))
+    assert torch.equal(kc.view(torch.int16), bf16(g["k_cache_out"]).view(torch.int16))
+    assert torch.equal(vc.view(torch.int16), bf16(g["v_cache_out"]).view(torch.int16))
+
+
+def test_fp8_calibration_matches_reference():
+    g = golden("append_fp8")
+    # first call calibrates from the batch; the second keeps the frozen scale
+    assert fp8_scale_ref(bf16(g["key0"])) == float(g["k_scale0"][0])
+    assert fp8_scale_ref(bf16(g["value0"])) == float(g["v_scale0"][0])
+    assert float(g["k_scale1"][0]) == float(g["k_scale0"][0])
+    assert float(g["v_scale1"][0]) == float(g["v_scale0"][0])
+
+
+@pytest.mark.parametrize("call", [0, 1])
+def test_fp8_quotients_match_reference(call):
+    """The reference kernel's clamp(x / scale) (captured in fp32 caches) equals the
+    oracle's pre-cast quotient at every written slot."""
+    g = golden("append_fp8")
+    slots = torch.from_numpy(g[f"slot_mapping{call}"])
+    keep = slots != -1
+    for name, scale_key, quot in (("key", "k_scale", "k_quot"), ("value", "v_scale", "v_quot")):
+        x = bf16(g[f"{name}{call}"])
+        s = float(g[f"{scale_key}{call}"][0])
+        q = x.float() / torch.tensor(s, dtype=torch.float32)
+        q = q.clamp(-448.0, 448.0)
+        ref = torch.from_numpy(g[f"{quot}{call}"]).view(-1, x.shape[1], x.shape[2])[slots[keep]]
+        assert torch.equal(q[keep], ref)
+        # and the e4m3 bytes of those quotients are the oracle's quantisation
+        assert torch.equal(quantize_fp8_ref(x, s)[keep].view(torch.uint8),
+                           ref.to(torch.float8_e4m3fn).view(torch.uint8))
+
+
+def test_fp8_append_end_to_end_matches_reference():
+    g = golden("append_fp8")
+    BS = int(g["block_size"])
+    shape = g["k_quot0"].shape
+    kc = torch.zeros(shape, dtype=torch.float8_e4m3fn)
+    vc = torch.zeros(shape, dtype=torch.float8_e4m3fn)
+    ks, vs = torch.ones(1), torch.ones(1)
+    for call in (0, 1):
+        store_kvcache_fp8_ref(bf16(g[f"key{call}"]), bf16(g[f"value{call}"]), kc, vc, ks, vs,
+                              torch.from_numpy(g[f"slot_mapping{call}"]), BS)
+        assert float(ks[0]) == float(g[f"k_scale{call}"][0])
+        assert float(vs[0]) == float(g[f"v_scale{call}"][0])
+    exp_k = torch.from_numpy(g["k_quot1"]).to(torch.float8_e4m3fn)
+    exp_v = torch.from_numpy(g["v_quot1"]).to(torch.float8_e4m3fn)
+    assert torch.equal(kc.view(torch.uint8), exp_k.view(torch.uint8))
+    assert torch.equal(vc.view(torch.uint8), exp_v.view(torch.uint8))
+
+
+def test_e4m3_cast_pinned_by_independent_encoder():
+    rng = np.random.default_rng(7)
+    x = np.concatenate([rng.standard_normal(200_000) * s for s in (1e-3, 0.1, 1, 50, 300)])
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    v = np.unique(codes[np.isfinite(codes)])
+    mids = (v[1:] + v[:-1]) / 2
+    x = np.clip(np.concatenate([x, mids, v, [0.0, -0.0]]), -448, 448).astype(np.float32)
+    t = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(t, e4m3_encode_reference(x))
+
+
+def _decode_inputs(g, fp8=False):
+    H, KVH = int(g["num_heads"]), int(g["num_kv_heads"])
+    q = torch.from_numpy(g["query"])
+    if fp8:
+        kc = torch.from_numpy(g["k_cache_e4m3"]).view(torch.float8_e4m3fn)
+        vc = torch.from_numpy(g["v_cache_e4m3"]).view(torch.float8_e4m3fn)
+    else:
+        kc, vc = torch.from_numpy(g["k_cache"]), torch.from_numpy(g["v_cache"])
+    return q, kc, vc, torch.from_numpy(g["block_tables"]), torch.from_numpy(g["context_lens"]), \
+        float(g["scale"]), H, KVH, q.shape[2], int(g["block_size"])
+
+
+def test_decode_oracle_matches_reference_kernel():
+    g = golden("decode_small")
+    args = _decode_inputs(g)
+    out = paged_decode_ref(*args)
+    ref = torch.from_numpy(g["out"]).double()
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(out), nan)  # context 0 -> NaN in both
+    assert torch.allclose(out[~nan], ref[~nan], atol=2e-6, rtol=1e-5)
+
+
+def test_decode_fp8_oracle_matches_reference_kernel():
+    g = golden("decode_fp8")
+    q, kc, vc, bt, cl, scale, H, KVH, D, BS = _decode_inputs(g, fp8=True)
+    out = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS,
+                           k_scale=torch.from_numpy(g["k_scale"]), v_scale=torch.from_numpy(g["v_scale"]))
+    assert torch.allclose(out, torch.from_numpy(g["out"]).double(), atol=2e-6, rtol=1e-5)
+
+
+def test_decode_config1_oracles_match_reference():
+    from golden.make_golden import _sha, config1_inputs
+    g = golden("decode_config1")
+    inp = config1_inputs(int(g["seed"]))
+    assert _sha(inp["query"], inp["k_cache"], inp["v_cache"], inp["block_tables"],
+                inp["context_lens"]) == str(g["inputs_sha256"]), "seeded input generation drifted"
+    args = (torch.from_numpy(inp["query"]), torch.from_numpy(inp["k_cache"]),
+            torch.from_numpy(inp["v_cache"]), torch.from_numpy(inp["block_tables"]),
+            torch.from_numpy(inp["context_lens"]), float(g["scale"]), inp["num_heads"],
+            inp["num_kv_heads"], inp["head_dim"], inp["block_size"])
+    ref = torch.from_numpy(g["out"])
+    assert torch.allclose(decode_torch_optimized(*args), ref, atol=1e-6, rtol=1e-6)
+    assert torch.allclose(paged_decode_ref(*args).float(), ref, atol=2e-6, rtol=1e-5)
