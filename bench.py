@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the number of sequences (smaller cases for ncu captures)")
     return ap.parse_args()
 
 
@@ -159,9 +161,10 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_workload(cfg: str, rank: int, world: int, device):
+def make_workload(cfg: str, rank: int, world: int, device, batch: int = 0):
     wl = importlib.import_module(PKG + ".workloads")
-    return getattr(wl, cfg)(device=device, seed=0, rank=rank, world_size=world)
+    kw = {"batch": batch} if batch > 0 else {}
+    return getattr(wl, cfg)(device=device, seed=0, rank=rank, world_size=world, **kw)
 
 
 def run_ours(args, rank, world, local):
@@ -173,7 +176,7 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
 
-    w = make_workload(args.config, rank, world, device)
+    w = make_workload(args.config, rank, world, device, args.batch)
     fp8 = w.fp8
     ks = w.k_scale.clone() if fp8 else None
     vs = w.v_scale.clone() if fp8 else None

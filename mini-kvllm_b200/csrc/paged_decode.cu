@@ -45,6 +45,7 @@ struct DecodeParams {
   const uint8_t* v_cache;
   int64_t num_blocks;
   int block_size;
+  int bs_shift;  // log2(block_size) when it is a power of two, else -1
   const void* bt;
   int64_t bt_sb;
   int max_blocks;
@@ -74,14 +75,25 @@ __device__ __forceinline__ int64_t load_ctx(const DecodeParams& p, int seq) {
 
 // Page of logical token t of sequence seq, or -1 when the token has no valid page.
 // Entries outside [0, num_blocks) other than -1 are counted once per (seq, token).
-__device__ __forceinline__ int64_t lookup_page(const DecodeParams& p, int seq, int64_t t,
-                                               bool count) {
-  const int64_t idx = (int64_t)seq * p.bt_sb + t / p.block_size;
+__device__ __forceinline__ int64_t page_of_block(const DecodeParams& p, int seq, int blk,
+                                                 bool count) {
+  const int64_t idx = (int64_t)seq * p.bt_sb + blk;
   const int64_t page = p.bt_i64 ? (int64_t)__ldg((const int64_t*)p.bt + idx)
                                 : (int64_t)__ldg((const int32_t*)p.bt + idx);
   if (page >= 0 && page < p.num_blocks) return page;
   if (page != -1 && count && p.invalid != nullptr) atomicAdd(p.invalid, 1);
   return -1;
+}
+
+// (logical block, row in block) of token t; contexts are < 2^31 tokens (host-checked).
+__device__ __forceinline__ void split_token(const DecodeParams& p, int t, int& blk, int& off) {
+  if (p.bs_shift >= 0) {
+    blk = t >> p.bs_shift;
+    off = t & ((1 << p.bs_shift) - 1);
+  } else {
+    blk = t / p.block_size;
+    off = t - blk * p.block_size;
+  }
 }
 
 // Token range of this CTA's split and the number of splits the sequence uses.
@@ -159,12 +171,16 @@ paged_decode_generic_kernel(const DecodeParams p) {
     uint8_t* vd = vbuf + stage * kGenTile * row_pitch;
     for (int idx = tid; idx < kGenTile * chunks; idx += kThreads) {
       const int r = idx / chunks, c = idx - r * chunks;
-      const int64_t t = t0 + r;
+      const int t = (int)t0 + r;
       int64_t page = -1;
-      if (t < rng.end) page = lookup_page(p, seq, t, count_invalid && c == 0);
+      int blk = 0, boff = 0;
+      if (t < rng.end) {
+        split_token(p, t, blk, boff);
+        page = page_of_block(p, seq, blk, count_invalid && c == 0);
+      }
       const bool ok = page >= 0;
       const int64_t off =
-          ok ? (page * p.block_size + t % p.block_size) * row_stride + head_off + c * 16 : 0;
+          ok ? (page * p.block_size + boff) * row_stride + head_off + c * 16 : 0;
       cp_async_16(smem_u32(kd + r * row_pitch + c * 16), p.k_cache + off, ok ? 16 : 0);
       cp_async_16(smem_u32(vd + r * row_pitch + c * 16), p.v_cache + off, ok ? 16 : 0);
       if (c == 0) valid[stage * kGenTile + r] = ok ? 1 : 0;
@@ -345,20 +361,39 @@ paged_decode_tc_kernel(const DecodeParams p) {
   const int64_t head_off = (int64_t)kvh * ROWB;
   const int ld_c = tid % CPR;
   const int ld_r0 = tid / CPR;
+  // A tile never straddles a page when block_size is a power of two >= the tile.
+  const bool one_page_per_tile = p.bs_shift >= 6;
+  const int end = (int)rng.end;
   auto load_tile = [&](int it) {
     const int stage = it % STAGES;
-    const int64_t t0 = rng.begin + (int64_t)it * kTcTile;
+    const int t0 = (int)rng.begin + it * kTcTile;
     uint8_t* kd = smem + stage * STAGE_BYTES;
     uint8_t* vd = kd + TILE_BYTES;
+    int64_t tile_page = -1;
+    int tile_off = 0;
+    if (one_page_per_tile) {
+      tile_page = page_of_block(p, seq, t0 >> p.bs_shift, count_invalid && tid == 0);
+      tile_off = t0 & ((1 << p.bs_shift) - 1);
+    }
 #pragma unroll
     for (int i = 0; i < PASSES; ++i) {
       const int r = ld_r0 + i * ROWS_PER_PASS;
-      const int64_t t = t0 + r;
+      const int t = t0 + r;
       int64_t page = -1;
-      if (t < rng.end) page = lookup_page(p, seq, t, count_invalid && ld_c == 0);
+      int boff = 0;
+      if (t < end) {
+        if (one_page_per_tile) {
+          page = tile_page;
+          boff = tile_off + r;
+        } else {
+          int blk;
+          split_token(p, t, blk, boff);
+          page = page_of_block(p, seq, blk, count_invalid && ld_c == 0);
+        }
+      }
       const bool ok = page >= 0;
       const int64_t off =
-          ok ? (page * p.block_size + t % p.block_size) * row_stride + head_off + ld_c * 16 : 0;
+          ok ? (page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
       const int soff = r * ROWB + ((ld_c ^ (r & 7)) << 4);
       cp_async_16(smem_u32(kd + soff), p.k_cache + off, ok ? 16 : 0);
       cp_async_16(smem_u32(vd + soff), p.v_cache + off, ok ? 16 : 0);
@@ -747,7 +782,9 @@ int ensure_smem(size_t bytes, int device) {
 template <typename QT, typename CT>
 int launch_generic(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
   const size_t smem = generic_smem_bytes(p.head_dim, sizeof(CT));
-  int st = ensure_smem<paged_decode_generic_kernel<QT, CT>>(smem, device);
+  // opt in once to the largest size this instantiation can use (head_dim 256)
+  int st = ensure_smem<paged_decode_generic_kernel<QT, CT>>(generic_smem_bytes(256, sizeof(CT)),
+                                                            device);
   if (st != MKV_OK) return st;
   paged_decode_generic_kernel<QT, CT><<<grid, kThreads, smem, stream>>>(p);
   return cuda_status(cudaGetLastError(), "paged_decode_generic launch");
@@ -803,6 +840,8 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
     return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
   if (num_seqs > 65535)
     return set_error(MKV_ERR_UNSUPPORTED, "%s: num_seqs > 65535", fn);
+  if ((int64_t)max_blocks * block_size >= ((int64_t)1 << 31))
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: max_num_blocks * block_size must be < 2^31", fn);
   if (head_dim % 16 != 0 || head_dim > 256)
     return set_error(MKV_ERR_UNSUPPORTED,
                      "%s: head_dim must be a multiple of 16 and at most 256 (got %d)", fn,
@@ -840,6 +879,7 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.v_cache = (const uint8_t*)v_cache;
   p.num_blocks = num_blocks;
   p.block_size = block_size;
+  p.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz((unsigned)block_size) : -1;
   p.bt = bt;
   p.bt_sb = bt_sb;
   p.max_blocks = max_blocks;

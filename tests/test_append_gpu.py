@@ -33,7 +33,8 @@ def _bits(t):
 @pytest.mark.parametrize("D,BS", [(128, 16), (128, 256), (64, 1), (40, 8), (20, 4)])
 @pytest.mark.parametrize("slot_dtype", [torch.int64, torch.int32])
 def test_store_kvcache_bit_exact(dtype, D, BS, slot_dtype):
-    key, value, slots, kc, vc = _case(77, 4, D, 40, BS, dtype, 1, neg=(0, 5, 76), slot_dtype=slot_dtype)
+    NB = max(40, (77 + BS - 1) // BS + 3)
+    key, value, slots, kc, vc = _case(77, 4, D, NB, BS, dtype, 1, neg=(0, 5, 76), slot_dtype=slot_dtype)
     ek, ev = kc.clone(), vc.clone()
     store_kvcache_ref(key, value, ek, ev, slots, BS)
     dk, dv = kc.cuda(), vc.cuda()
