@@ -62,6 +62,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the number of sequences (smaller cases for ncu captures)")
+    ap.add_argument("--emulate-shard", type=int, default=1,
+                    help="run rank 0's KV-head shard of an N-way split on this one GPU")
     return ap.parse_args()
 
 
@@ -161,9 +163,11 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_workload(cfg: str, rank: int, world: int, device, batch: int = 0):
+def make_workload(cfg: str, rank: int, world: int, device, batch: int = 0, shard: int = 1):
     wl = importlib.import_module(PKG + ".workloads")
     kw = {"batch": batch} if batch > 0 else {}
+    if world == 1 and shard > 1:  # one rank's shard of an N-way split, on one GPU
+        rank, world = 0, shard
     return getattr(wl, cfg)(device=device, seed=0, rank=rank, world_size=world, **kw)
 
 
@@ -176,7 +180,7 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
 
-    w = make_workload(args.config, rank, world, device, args.batch)
+    w = make_workload(args.config, rank, world, device, args.batch, args.emulate_shard)
     fp8 = w.fp8
     ks = w.k_scale.clone() if fp8 else None
     vs = w.v_scale.clone() if fp8 else None
@@ -317,7 +321,9 @@ def run_ours(args, rank, world, local):
                    "num_seqs": batch, "num_heads": w.meta["num_heads"], "num_kv_heads": w.meta["num_kv_heads"],
                    "head_dim": w.head_dim, "block_size": w.block_size,
                    "max_num_blocks": w.block_tables.shape[1], "num_splits": splits,
-                   "parallelism": f"kv-head tp{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"kv-head tp{world}" if world > 1 else
+                                   f"rank 0 of a {args.emulate_shard}-way kv-head split, one GPU"
+                                   if args.emulate_shard > 1 else "single GPU"),
                    "l2": "working set >> 126 MB L2 (no flush needed)",
                    "step": "append 1 token/seq + paged decode"},
         "decode_tokens_per_s": round(tokens_per_s, 1),

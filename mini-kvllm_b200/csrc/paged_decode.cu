@@ -7,23 +7,29 @@
 // Semantics kept: kv_head = h / (H / KVH); tokens t < context_len whose logical block
 // t / block_size is < max_num_blocks; page = block_tables[b, t / block_size] with -1
 // meaning "skip this token"; FP8 values dequantised as float(e4m3) * scale; output
-// = softmax(scale * q.K) V in fp32, stored in the query dtype.
+// = softmax(scale * q.K) V in fp32, stored in the query dtype; no visible token -> NaN.
 //
 // B200 design (HBM-bound: ~2 * G FLOP per cache byte):
 //   * one CTA per (sequence, kv head, KV split) covers the whole GQA group, so each
 //     page row is read from HBM once, not G times as in the reference's (seq, head) grid;
 //   * pages stream through a multi-stage cp.async ring of 64-token tiles in shared
-//     memory (16-byte chunks, XOR-swizzled so ldmatrix reads are conflict-free);
-//   * QK^T and PV run on the tensor cores (mma.sync m16n8k16, fp32 accumulate) with
-//     the query group as the M=16 rows; FP8 pages are converted e4m3x2 -> f16x2 in
-//     registers straight out of ldmatrix, so dequantisation adds no memory traffic;
-//     the per-tensor K scale is folded into the score scale and V's into the output;
-//   * online softmax in the exp2 domain with quad shuffles; 4 warps split each tile
-//     and merge their (m, l, acc) through shared memory at the end;
-//   * long or ragged contexts are split into fixed-size token chunks (flash-decoding)
-//     and merged by a second kernel; a sequence that fits one chunk writes its output
-//     directly. The split count depends only on shapes, so the launch is graph-safe.
-// A CUDA-core kernel with the same tiling covers fp32 and other head dims.
+//     memory (16-byte chunks, XOR-swizzled so ldmatrix reads are conflict-free); the
+//     CTA's block-table slice is staged in shared memory first;
+//   * QK^T and PV run on the tensor cores (mma.sync m16n8k16, fp32 accumulate) in the
+//     transposed form S^T = K Q^T and O^T = V^T P^T: the 16 tokens of a warp are the
+//     M rows and the query group (padded to 8) is N, so no MMA row is wasted on
+//     padding heads. P^T is re-laid out as the B operand with movmatrix.trans;
+//   * FP8 pages are converted e4m3x2 -> f16x2 in registers straight out of ldmatrix
+//     (head_dim permuted so one ldmatrix word feeds both halves of a fragment), so
+//     dequantisation adds no memory traffic; the K scale is folded into the score
+//     scale and V's into the output;
+//   * online softmax in the exp2 domain; 4 warps split each tile and merge their
+//     (m, l, acc) through shared memory at the end;
+//   * long or ragged contexts are split into fixed-size token chunks (flash-decoding).
+//     Each split writes (m, l, acc) to the workspace and bumps a per-(seq, kv head)
+//     counter; the last split to arrive merges them and writes the output, so there
+//     is no second kernel. The split count depends only on shapes (graph-safe).
+// A CUDA-core kernel with the same tiling and epilogue covers fp32 and other head dims.
 #include <type_traits>
 
 #include "mkv_common.cuh"
@@ -31,11 +37,13 @@
 namespace mkv {
 namespace {
 
-constexpr int kThreads = 128;      // 4 warps per CTA (both kernels)
+constexpr int kThreads = 128;        // 4 warps per CTA (both kernels)
 constexpr int kMaxHeadsPerCta = 16;  // query heads of one KV head handled by a CTA
-constexpr int kTcTile = 64;        // tokens per pipeline stage, tensor-core kernel
-constexpr int kGenTile = 32;       // tokens per pipeline stage, CUDA-core kernel
-constexpr int kChunkAlign = 64;    // split boundaries are multiples of both tiles
+constexpr int kTcTile = 64;          // tokens per pipeline stage, tensor-core kernel
+constexpr int kGenTile = 32;         // tokens per pipeline stage, CUDA-core kernel
+constexpr int kChunkAlign = 64;      // split boundaries are multiples of both tiles
+constexpr int kMaxSplits = 128;  // bounds the merge-weight buffer in shared memory
+constexpr int kMaxBtSmem = 128;      // block-table entries staged in shared memory
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
@@ -56,13 +64,14 @@ struct DecodeParams {
   int group;          // H / KVH
   int heads_per_cta;  // min(group, kMaxHeadsPerCta)
   int head_groups;    // ceil(group / heads_per_cta)
-  float qk_scale_log2;  // attention scale * log2(e)
+  float qk_scale_log2;   // attention scale * log2(e)
   const float* k_scale;  // FP8 per-tensor scales (nullptr for float caches)
   const float* v_scale;
   void* out;
   int64_t o_sb, o_sh;  // elements
-  float* part_acc;  // [num_seqs][num_heads][num_splits][head_dim]
-  float* part_ml;   // [num_seqs][num_heads][num_splits][2] = (m in log2 units, l)
+  float* part_acc;     // [num_seqs][num_heads][num_splits][head_dim]
+  float* part_ml;      // [num_seqs][num_heads][num_splits][2] = (m in log2 units, l)
+  unsigned int* arrivals;  // [num_seqs][num_kv_heads * head_groups], zero between launches
   int num_splits;
   int chunk;  // tokens per split, multiple of kChunkAlign
   int32_t* invalid;
@@ -73,14 +82,13 @@ __device__ __forceinline__ int64_t load_ctx(const DecodeParams& p, int seq) {
                    : (int64_t)__ldg((const int32_t*)p.ctx + seq);
 }
 
-// Page of logical token t of sequence seq, or -1 when the token has no valid page.
-// Entries outside [0, num_blocks) other than -1 are counted once per (seq, token).
-__device__ __forceinline__ int64_t page_of_block(const DecodeParams& p, int seq, int blk,
-                                                 bool count) {
+// Validated page of logical block `blk` of sequence `seq`: -1 when the entry is -1 or
+// outside [0, num_blocks); such out-of-range entries (other than -1) are counted.
+__device__ __forceinline__ int page_of_block(const DecodeParams& p, int seq, int blk, bool count) {
   const int64_t idx = (int64_t)seq * p.bt_sb + blk;
   const int64_t page = p.bt_i64 ? (int64_t)__ldg((const int64_t*)p.bt + idx)
                                 : (int64_t)__ldg((const int32_t*)p.bt + idx);
-  if (page >= 0 && page < p.num_blocks) return page;
+  if (page >= 0 && page < p.num_blocks) return (int)page;
   if (page != -1 && count && p.invalid != nullptr) atomicAdd(p.invalid, 1);
   return -1;
 }
@@ -98,19 +106,107 @@ __device__ __forceinline__ void split_token(const DecodeParams& p, int t, int& b
 
 // Token range of this CTA's split and the number of splits the sequence uses.
 struct SplitRange {
-  int64_t begin, end;
-  int active;
+  int begin, end, active;
 };
 __device__ __forceinline__ SplitRange split_range(const DecodeParams& p, int seq, int split) {
-  int64_t ctx = load_ctx(p, seq);
+  const int64_t ctx = load_ctx(p, seq);
   const int64_t cap = (int64_t)p.max_blocks * p.block_size;
   int64_t eff = ctx < cap ? ctx : cap;
   if (eff < 0) eff = 0;
   SplitRange r;
   r.active = eff > 0 ? (int)((eff + p.chunk - 1) / p.chunk) : 1;
-  r.begin = (int64_t)split * p.chunk;
-  r.end = r.begin + p.chunk < eff ? r.begin + p.chunk : eff;
+  r.begin = split * p.chunk;
+  r.end = (int)((int64_t)r.begin + p.chunk < eff ? (int64_t)r.begin + p.chunk : eff);
   return r;
+}
+
+// Block-table slice of the split in shared memory (validated pages, -1 = none).
+struct BlockSlice {
+  int lo, n;  // first logical block and count; n > kMaxBtSmem = not staged
+};
+__device__ __forceinline__ BlockSlice stage_block_table(const DecodeParams& p, int seq,
+                                                        const SplitRange& rng, int* bt_s,
+                                                        bool count) {
+  BlockSlice s{0, 0};
+  if (rng.end > rng.begin) {
+    int hi, off;
+    split_token(p, rng.begin, s.lo, off);
+    split_token(p, rng.end - 1, hi, off);
+    s.n = hi - s.lo + 1;
+  }
+  if (s.n <= kMaxBtSmem)
+    for (int i = threadIdx.x; i < s.n; i += blockDim.x) bt_s[i] = page_of_block(p, seq, s.lo + i, count);
+  return s;
+}
+__device__ __forceinline__ int slice_page(const DecodeParams& p, int seq, const BlockSlice& s,
+                                          const int* bt_s, int blk) {
+  return s.n <= kMaxBtSmem ? bt_s[blk - s.lo] : page_of_block(p, seq, blk, false);
+}
+
+// ---------------------------------------------------------------- shared epilogue
+// The CTA's result for its nh heads is staged in shared memory: o_s[h * ld + d]
+// (unnormalised), m_s[h] (log2 units), l_s[h]. A sequence with one active split writes
+// out = o * v_scale / l directly. Otherwise the split stores its (m, l, o) partial and
+// the last split to arrive (per-(seq, kv head) counter) merges all partials and writes
+// the output; it also zeroes the counter for the next launch. `wts` needs
+// (active + 1) * nh floats of shared memory.
+template <typename QT>
+__device__ void finish_cta(const DecodeParams& p, int seq, int cta_group, int h0, int nh,
+                           int split, int active, const float* o_s, int ld, const float* m_s,
+                           const float* l_s, float* wts) {
+  const int D = p.head_dim;
+  const float vs = p.v_scale != nullptr ? __ldg(p.v_scale) : 1.0f;
+  QT* op = reinterpret_cast<QT*>(p.out);
+  if (active == 1) {
+    for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
+      const int h = idx / D, d = idx - h * D;
+      op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] =
+          from_f32<QT>(o_s[h * ld + d] * vs / l_s[h]);
+    }
+    return;
+  }
+  const int64_t S = p.num_splits;
+  for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    const int64_t b = ((int64_t)seq * p.num_heads + h0 + h) * S + split;
+    __stcg(p.part_acc + b * D + d, o_s[h * ld + d]);
+    if (d == 0) {
+      __stcg(p.part_ml + b * 2 + 0, m_s[h]);
+      __stcg(p.part_ml + b * 2 + 1, l_s[h]);
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ bool last;
+  unsigned int* ctr = p.arrivals + (int64_t)seq * p.num_kv_heads * p.head_groups + cta_group;
+  if (threadIdx.x == 0) last = atomicAdd(ctr, 1u) == (unsigned)(active - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // merge weights: wts[s * nh + h] = 2^(m_s - M_h); wts[active * nh + h] = v_scale / L_h
+  for (int h = threadIdx.x; h < nh; h += blockDim.x) {
+    const int64_t base = ((int64_t)seq * p.num_heads + h0 + h) * S;
+    float M = -INFINITY;
+    for (int s = 0; s < active; ++s) M = fmaxf(M, __ldcg(p.part_ml + (base + s) * 2));
+    const float mb = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f;
+    for (int s = 0; s < active; ++s) {
+      const float w = exp2f(__ldcg(p.part_ml + (base + s) * 2) - mb);
+      wts[s * nh + h] = w;
+      L = fmaf(w, __ldcg(p.part_ml + (base + s) * 2 + 1), L);
+    }
+    wts[active * nh + h] = vs / L;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    const int64_t base = ((int64_t)seq * p.num_heads + h0 + h) * S;
+    float O = 0.0f;
+#pragma unroll 4
+    for (int s = 0; s < active; ++s) O = fmaf(wts[s * nh + h], __ldcg(p.part_acc + (base + s) * D + d), O);
+    op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O * wts[active * nh + h]);
+  }
+  if (threadIdx.x == 0) *ctr = 0u;
 }
 
 // ============================================================ CUDA-core kernel
@@ -128,15 +224,18 @@ paged_decode_generic_kernel(const DecodeParams p) {
   const int row_bytes = D * EB;
   const int row_pitch = row_bytes + 16;  // padding keeps lane-per-row reads conflict-free
   const int chunks = row_bytes / 16;
+  const int ring = 4 * kGenTile * row_pitch;
+  const int epi = (kMaxHeadsPerCta * D + (kMaxSplits + 1) * kMaxHeadsPerCta) * 4;
 
-  uint8_t* kbuf = smem;                                   // [2][kGenTile][row_pitch]
-  uint8_t* vbuf = kbuf + 2 * kGenTile * row_pitch;         // [2][kGenTile][row_pitch]
-  float* q_s = reinterpret_cast<float*>(vbuf + 2 * kGenTile * row_pitch);  // [16][D]
-  float* s_s = q_s + kMaxHeadsPerCta * D;                 // [16][kGenTile]
-  float* m_s = s_s + kMaxHeadsPerCta * kGenTile;          // [16]
-  float* l_s = m_s + kMaxHeadsPerCta;                     // [16]
-  float* a_s = l_s + kMaxHeadsPerCta;                     // [16]
+  uint8_t* kbuf = smem;                                             // [2][kGenTile][row_pitch]
+  uint8_t* vbuf = kbuf + 2 * kGenTile * row_pitch;                  // [2][kGenTile][row_pitch]
+  float* q_s = reinterpret_cast<float*>(smem + (ring > epi ? ring : epi));  // [16][D]
+  float* s_s = q_s + kMaxHeadsPerCta * D;                          // [16][kGenTile]
+  float* m_s = s_s + kMaxHeadsPerCta * kGenTile;                   // [16]
+  float* l_s = m_s + kMaxHeadsPerCta;                              // [16]
+  float* a_s = l_s + kMaxHeadsPerCta;                              // [16]
   uint8_t* valid = reinterpret_cast<uint8_t*>(a_s + kMaxHeadsPerCta);  // [2][kGenTile]
+  int* bt_s = reinterpret_cast<int*>(valid + 2 * kGenTile);        // [kMaxBtSmem]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
@@ -149,9 +248,9 @@ paged_decode_generic_kernel(const DecodeParams p) {
 
   const SplitRange rng = split_range(p, seq, split);
   if (split > 0 && rng.begin >= rng.end) return;
+  const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
 
   const float ks = kFp8 ? __ldg(p.k_scale) : 1.0f;
-  const float vs = kFp8 ? __ldg(p.v_scale) : 1.0f;
   const float qscale = p.qk_scale_log2 * ks;
   const QT* qp = reinterpret_cast<const QT*>(p.q);
   for (int i = tid; i < kMaxHeadsPerCta * D; i += kThreads) {
@@ -163,24 +262,25 @@ paged_decode_generic_kernel(const DecodeParams p) {
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.0f;
   }
+  __syncthreads();
 
   const int64_t row_stride = (int64_t)p.num_kv_heads * row_bytes;  // bytes between tokens
   const int64_t head_off = (int64_t)kvh * row_bytes;
-  auto load_tile = [&](int64_t t0, int stage) {
+  auto load_tile = [&](int t0, int stage) {
     uint8_t* kd = kbuf + stage * kGenTile * row_pitch;
     uint8_t* vd = vbuf + stage * kGenTile * row_pitch;
     for (int idx = tid; idx < kGenTile * chunks; idx += kThreads) {
       const int r = idx / chunks, c = idx - r * chunks;
-      const int t = (int)t0 + r;
-      int64_t page = -1;
-      int blk = 0, boff = 0;
+      const int t = t0 + r;
+      int page = -1, boff = 0;
       if (t < rng.end) {
+        int blk;
         split_token(p, t, blk, boff);
-        page = page_of_block(p, seq, blk, count_invalid && c == 0);
+        page = slice_page(p, seq, slice, bt_s, blk);
       }
       const bool ok = page >= 0;
       const int64_t off =
-          ok ? (page * p.block_size + boff) * row_stride + head_off + c * 16 : 0;
+          ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + c * 16 : 0;
       cp_async_16(smem_u32(kd + r * row_pitch + c * 16), p.k_cache + off, ok ? 16 : 0);
       cp_async_16(smem_u32(vd + r * row_pitch + c * 16), p.v_cache + off, ok ? 16 : 0);
       if (c == 0) valid[stage * kGenTile + r] = ok ? 1 : 0;
@@ -194,13 +294,13 @@ paged_decode_generic_kernel(const DecodeParams p) {
 #pragma unroll
     for (int j = 0; j < kMaxDpt; ++j) acc[h][j] = 0.0f;
 
-  const int64_t span = rng.end > rng.begin ? rng.end - rng.begin : 0;
-  const int ntiles = (int)((span + kGenTile - 1) / kGenTile);
+  const int span = rng.end > rng.begin ? rng.end - rng.begin : 0;
+  const int ntiles = (span + kGenTile - 1) / kGenTile;
   if (ntiles > 0) load_tile(rng.begin, 0);
   cp_async_commit();
   for (int it = 0; it < ntiles; ++it) {
     const int stage = it & 1;
-    if (it + 1 < ntiles) load_tile(rng.begin + (int64_t)(it + 1) * kGenTile, stage ^ 1);
+    if (it + 1 < ntiles) load_tile(rng.begin + (it + 1) * kGenTile, stage ^ 1);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -262,84 +362,94 @@ paged_decode_generic_kernel(const DecodeParams p) {
   cp_async_wait<0>();
   __syncthreads();
 
-  // write the final output (single split) or this split's partial state
-  const bool direct = rng.active == 1;
+  // stage the result in the (now idle) ring and finish
+  float* o_s = reinterpret_cast<float*>(smem);  // [16][D]
 #pragma unroll
   for (int j = 0; j < kMaxDpt; ++j) {
     const int d = tid + j * kThreads;
-    if (d >= D) continue;
+    if (d < D) {
 #pragma unroll
-    for (int h = 0; h < kMaxHeadsPerCta; ++h) {
-      if (h >= nh) continue;
-      const int head = h0 + h;
-      if (direct) {
-        QT* o = reinterpret_cast<QT*>(p.out);
-        o[(int64_t)seq * p.o_sb + (int64_t)head * p.o_sh + d] =
-            from_f32<QT>(acc[h][j] * vs / l_s[h]);
-      } else {
-        const int64_t base = ((int64_t)seq * p.num_heads + head) * p.num_splits + split;
-        p.part_acc[base * D + d] = acc[h][j];
-        if (d == 0) {
-          p.part_ml[base * 2 + 0] = m_s[h];
-          p.part_ml[base * 2 + 1] = l_s[h];
-        }
-      }
+      for (int h = 0; h < kMaxHeadsPerCta; ++h)
+        if (h < nh) o_s[h * D + d] = acc[h][j];
     }
   }
+  __syncthreads();
+  float* wts = o_s + kMaxHeadsPerCta * D;
+  finish_cta<QT>(p, seq, blockIdx.y, h0, nh, split, rng.active, o_s, D, m_s, l_s, wts);
 }
 
 size_t generic_smem_bytes(int head_dim, int elem_bytes) {
   const int row_pitch = head_dim * elem_bytes + 16;
-  return (size_t)4 * kGenTile * row_pitch + (size_t)kMaxHeadsPerCta * head_dim * 4 +
-         (size_t)kMaxHeadsPerCta * kGenTile * 4 + 3 * kMaxHeadsPerCta * 4 + 2 * kGenTile;
+  const size_t ring = (size_t)4 * kGenTile * row_pitch;
+  const size_t epi = (size_t)kMaxHeadsPerCta * head_dim * 4 +
+                     (size_t)(kMaxSplits + 1) * kMaxHeadsPerCta * 4;
+  return (ring > epi ? ring : epi) + (size_t)kMaxHeadsPerCta * head_dim * 4 +
+         (size_t)kMaxHeadsPerCta * kGenTile * 4 + 3 * kMaxHeadsPerCta * 4 + 2 * kGenTile +
+         kMaxBtSmem * 4;
 }
 
 // ============================================================ tensor-core kernel
 // head_dim = 128; query bf16 with bf16 pages, f16 with f16 pages, or bf16/f16 with
-// e4m3 pages (f16 MMAs). TWO_ROWS = the CTA has more than 8 query heads (MMA rows
-// 8..15 in use).
+// e4m3 pages (f16 MMAs). NT = query heads of the CTA in units of 8 (MMA N tiles).
 template <typename CT> struct TcTraits;
 template <> struct TcTraits<bf16> {
   using MT = bf16;
   static constexpr bool kFp8 = false;
-  static constexpr int kStages = 3;
 };
 template <> struct TcTraits<f16> {
   using MT = f16;
   static constexpr bool kFp8 = false;
-  static constexpr int kStages = 3;
 };
 template <> struct TcTraits<fp8> {
   using MT = f16;
   static constexpr bool kFp8 = true;
-  static constexpr int kStages = 4;
 };
 
 constexpr int kTcD = 128;
 
-template <typename CT>
-constexpr size_t tc_smem_bytes() {
-  return (size_t)TcTraits<CT>::kStages * (2 * kTcTile * kTcD * sizeof(CT) + kTcTile);
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
 }
 
-template <typename QT, typename CT, bool TWO_ROWS>
-__global__ void __launch_bounds__(kThreads, 2)
+// Epilogue buffers (floats), for a CTA of up to 8*NT query heads: the 4 warps' partial
+// O^T [4][8NT][D+4] (warp 0's slot is overwritten in place by the merged O), their m
+// and l [4][8NT] each, the merged m and l [8NT] each, merge weights [kMaxSplits+1][8NT].
+template <int NT>
+constexpr size_t tc_epilogue_bytes() {
+  return (size_t)(4 * 8 * NT * (kTcD + 4) + 8 * 8 * NT + 2 * 8 * NT + (kMaxSplits + 1) * 8 * NT) * 4;
+}
+
+template <typename CT, int NT, int STAGES>
+constexpr size_t tc_front_bytes() {  // ring, reused by the epilogue
+  constexpr size_t ring = (size_t)STAGES * 2 * kTcTile * kTcD * sizeof(CT);
+  return ring > tc_epilogue_bytes<NT>() ? ring : tc_epilogue_bytes<NT>();
+}
+template <typename CT, int NT, int STAGES>
+constexpr size_t tc_smem_bytes() {  // + valid flags + staged block table
+  return tc_front_bytes<CT, NT, STAGES>() + (size_t)STAGES * kTcTile + kMaxBtSmem * 4;
+}
+
+template <typename QT, typename CT, int NT, int STAGES, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
 paged_decode_tc_kernel(const DecodeParams p) {
   using Tr = TcTraits<CT>;
   using MT = typename Tr::MT;
   constexpr bool kFp8 = Tr::kFp8;
-  constexpr int STAGES = Tr::kStages;
   constexpr int D = kTcD;
   constexpr int EB = sizeof(CT);
-  constexpr int ROWB = D * EB;            // 256 (16-bit) or 128 (e4m3) bytes per token row
-  constexpr int CPR = ROWB / 16;          // 16-byte chunks per row
+  constexpr int ROWB = D * EB;    // 256 (16-bit) or 128 (e4m3) bytes per token row
+  constexpr int CPR = ROWB / 16;  // 16-byte chunks per row
   constexpr int TILE_BYTES = kTcTile * ROWB;
   constexpr int STAGE_BYTES = 2 * TILE_BYTES;
   constexpr int ROWS_PER_PASS = kThreads / CPR;
   constexpr int PASSES = kTcTile / ROWS_PER_PASS;
+  constexpr size_t FRONT = tc_front_bytes<CT, NT, STAGES>();
 
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* valid = smem + STAGES * STAGE_BYTES;  // [STAGES][kTcTile]
+  uint8_t* valid = smem + FRONT;                                 // [STAGES][kTcTile]
+  int* bt_s = reinterpret_cast<int*>(valid + STAGES * kTcTile);  // [kMaxBtSmem]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
@@ -353,8 +463,9 @@ paged_decode_tc_kernel(const DecodeParams p) {
 
   const SplitRange rng = split_range(p, seq, split);
   if (split > 0 && rng.begin >= rng.end) return;
-  const int64_t span = rng.end > rng.begin ? rng.end - rng.begin : 0;
-  const int ntiles = (int)((span + kTcTile - 1) / kTcTile);
+  const int ntiles = (rng.end - rng.begin + kTcTile - 1) / kTcTile;  // 0 when empty
+  const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
+  __syncthreads();
 
   // ---- producer: all threads issue 16-byte cp.async for their rows/chunks
   const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
@@ -363,37 +474,34 @@ paged_decode_tc_kernel(const DecodeParams p) {
   const int ld_r0 = tid / CPR;
   // A tile never straddles a page when block_size is a power of two >= the tile.
   const bool one_page_per_tile = p.bs_shift >= 6;
-  const int end = (int)rng.end;
   auto load_tile = [&](int it) {
     const int stage = it % STAGES;
-    const int t0 = (int)rng.begin + it * kTcTile;
+    const int t0 = rng.begin + it * kTcTile;
     uint8_t* kd = smem + stage * STAGE_BYTES;
     uint8_t* vd = kd + TILE_BYTES;
-    int64_t tile_page = -1;
-    int tile_off = 0;
+    int tile_page = -1, tile_off = 0;
     if (one_page_per_tile) {
-      tile_page = page_of_block(p, seq, t0 >> p.bs_shift, count_invalid && tid == 0);
+      tile_page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
       tile_off = t0 & ((1 << p.bs_shift) - 1);
     }
 #pragma unroll
     for (int i = 0; i < PASSES; ++i) {
       const int r = ld_r0 + i * ROWS_PER_PASS;
       const int t = t0 + r;
-      int64_t page = -1;
-      int boff = 0;
-      if (t < end) {
+      int page = -1, boff = 0;
+      if (t < rng.end) {
         if (one_page_per_tile) {
           page = tile_page;
           boff = tile_off + r;
         } else {
           int blk;
           split_token(p, t, blk, boff);
-          page = page_of_block(p, seq, blk, count_invalid && ld_c == 0);
+          page = slice_page(p, seq, slice, bt_s, blk);
         }
       }
       const bool ok = page >= 0;
       const int64_t off =
-          ok ? (page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
+          ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
       const int soff = r * ROWB + ((ld_c ^ (r & 7)) << 4);
       cp_async_16(smem_u32(kd + soff), p.k_cache + off, ok ? 16 : 0);
       cp_async_16(smem_u32(vd + soff), p.v_cache + off, ok ? 16 : 0);
@@ -401,22 +509,22 @@ paged_decode_tc_kernel(const DecodeParams p) {
     }
   };
 
-  // prologue: put STAGES-1 tiles in flight before building the query fragments
+  // prologue: STAGES-1 tiles in flight before building the query fragments
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
     if (s < ntiles) load_tile(s);
     cp_async_commit();
   }
 
-  // ---- query fragments (A operand, rows = query heads of this CTA)
+  // ---- Q^T fragments (B operand: K = head_dim, N = query heads of this CTA)
   const QT* qp = reinterpret_cast<const QT*>(p.q);
   auto qval = [&](int row, int d) -> float {
     return row < nh ? to_f32(qp[(int64_t)seq * p.q_sb + (int64_t)(h0 + row) * p.q_sh + d]) : 0.0f;
   };
-  // column of element j (0..3) of row-fragment half `hi` for k-step ks
-  // 16-bit pages: a0 = cols 2tig,2tig+1; a2 = cols 8+2tig, 8+2tig+1 (PTX m16n8k16 layout)
-  // e4m3 pages: k index kappa -> d permuted so one ldmatrix word (4 bytes = d 4tig..4tig+3)
-  //             feeds b0 (kappa 2tig,2tig+1) and b1 (kappa 2tig+8, 2tig+9).
+  // head_dim index of B-fragment element (k-step ks, register half, element e).
+  // 16-bit pages: b0 = k 2tig,2tig+1; b1 = k 2tig+8,2tig+9 (PTX m16n8k16 layout).
+  // e4m3 pages: k is permuted so that one ldmatrix word (the 4 bytes d = 4tig..4tig+3)
+  // feeds both A registers of a k-step; Q uses the same permutation.
   auto qcol = [&](int ks, int half, int e) -> int {
     if (kFp8) return 16 * ks + 4 * tig + 2 * half + e;
     return 16 * ks + 8 * half + 2 * tig + e;
@@ -425,45 +533,42 @@ paged_decode_tc_kernel(const DecodeParams p) {
   if (kFp8 && std::is_same<QT, bf16>::value) {
     float mx = 0.0f;
 #pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int half = 0; half < 2; ++half)
+      for (int ks = 0; ks < D / 16; ++ks)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          mx = fmaxf(mx, fabsf(qval(g, qcol(ks, half, e))));
-          if (TWO_ROWS) mx = fmaxf(mx, fabsf(qval(g + 8, qcol(ks, half, e))));
-        }
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) mx = fmaxf(mx, fabsf(qval(nt * 8 + g, qcol(ks, half, e))));
     mx = warp_max(mx);
     if (mx > 0.0f && isfinite(mx)) {
       int ex;
-      frexpf(mx, &ex);            // mx = f * 2^ex, f in [0.5, 1)
+      frexpf(mx, &ex);                // mx = f * 2^ex, f in [0.5, 1)
       qpow2 = ldexpf(1.0f, 15 - ex);  // max |q| * qpow2 < 2^15 < f16 max
     }
   }
-  uint32_t qa[D / 16][4];
+  uint32_t qb[NT][D / 16][2];
 #pragma unroll
-  for (int ks = 0; ks < D / 16; ++ks) {
-    qa[ks][0] = pack2<MT>(qval(g, qcol(ks, 0, 0)) * qpow2, qval(g, qcol(ks, 0, 1)) * qpow2);
-    qa[ks][2] = pack2<MT>(qval(g, qcol(ks, 1, 0)) * qpow2, qval(g, qcol(ks, 1, 1)) * qpow2);
-    if (TWO_ROWS) {
-      qa[ks][1] =
-          pack2<MT>(qval(g + 8, qcol(ks, 0, 0)) * qpow2, qval(g + 8, qcol(ks, 0, 1)) * qpow2);
-      qa[ks][3] =
-          pack2<MT>(qval(g + 8, qcol(ks, 1, 0)) * qpow2, qval(g + 8, qcol(ks, 1, 1)) * qpow2);
-    } else {
-      qa[ks][1] = 0u;
-      qa[ks][3] = 0u;
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int row = nt * 8 + g;
+      qb[nt][ks][0] = pack2<MT>(qval(row, qcol(ks, 0, 0)) * qpow2, qval(row, qcol(ks, 0, 1)) * qpow2);
+      qb[nt][ks][1] = pack2<MT>(qval(row, qcol(ks, 1, 0)) * qpow2, qval(row, qcol(ks, 1, 1)) * qpow2);
     }
-  }
-  const float ks_scale = kFp8 ? __ldg(p.k_scale) : 1.0f;
-  const float vs_scale = kFp8 ? __ldg(p.v_scale) : 1.0f;
-  const float sc = p.qk_scale_log2 * ks_scale / qpow2;
+  const float ksc = kFp8 ? __ldg(p.k_scale) : 1.0f;
+  const float sc = p.qk_scale_log2 * ksc / qpow2;
 
-  // ---- per-warp softmax state (rows g and g+8) and output accumulators
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-  float o[D / 8][4];
+  // ---- per-warp softmax state for heads nt*8 + 2tig + e, and O^T accumulators
+  float m_run[NT][2], l_run[NT][2];
+  float o[NT][D / 16][4];
 #pragma unroll
-  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt][0] = m_run[nt][1] = -INFINITY;
+    l_run[nt][0] = l_run[nt][1] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.0f;
+  }
 
   const int lrow = lane & 7;   // ldmatrix: row within the 8x8 matrix this lane addresses
   const int lmat = lane >> 3;  // ldmatrix: which of the 4 matrices
@@ -474,131 +579,129 @@ paged_decode_tc_kernel(const DecodeParams p) {
     cp_async_commit();
 
     const int stage = it % STAGES;
-    const uint8_t* kt = smem + stage * STAGE_BYTES;
-    const uint8_t* vt = kt + TILE_BYTES;
+    const uint32_t kbase = smem_u32(smem + stage * STAGE_BYTES);
+    const uint32_t vbase = kbase + TILE_BYTES;
     const uint8_t* vld = valid + stage * kTcTile;
-    const uint32_t kbase = smem_u32(kt);
-    const uint32_t vbase = smem_u32(vt);
 
-    // ---- S = Q K^T for this warp's 16 tokens (two n8 tiles)
-    float s[2][4];
+    // ---- S^T = K Q^T: this warp's 16 tokens (M) x query heads (N)
+    float s[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-      const int r = warp * 16 + nt * 8 + lrow;
+    for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+    {
+      // matrices: 0 = tokens 0-7, 1 = tokens 8-15 (same chunk); 2/3 = next chunk
+      const int r = warp * 16 + ((lmat & 1) << 3) + lrow;
       if (!kFp8) {
+        // two independent accumulator chains (even / odd k-steps) halve the MMA
+        // dependency depth; summed after the loop
+        float s2[NT][4];
 #pragma unroll
-        for (int kp = 0; kp < D / 32; ++kp) {
-          const int lc = 4 * kp + lmat;
-          uint32_t b0, b1, b2, b3;
-          ldmatrix_x4(kbase + r * ROWB + ((lc ^ lrow) << 4), b0, b1, b2, b3);
-          Mma<MT>::run(s[nt], qa[2 * kp], b0, b1);
-          Mma<MT>::run(s[nt], qa[2 * kp + 1], b2, b3);
+        for (int nt = 0; nt < NT; ++nt) s2[nt][0] = s2[nt][1] = s2[nt][2] = s2[nt][3] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const int lc = 2 * ks + (lmat >> 1);
+          uint32_t a[4];
+          ldmatrix_x4(kbase + r * ROWB + ((lc ^ lrow) << 4), a[0], a[1], a[2], a[3]);
+          // a[0]: tokens 0-7, k 0-7; a[1]: tokens 8-15, k 0-7; a[2]/a[3]: k 8-15
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            Mma<MT>::run((ks & 1) ? s2[nt] : s[nt], a, qb[nt][ks][0], qb[nt][ks][1]);
         }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s[nt][i] += s2[nt][i];
       } else {
 #pragma unroll
-        for (int kq = 0; kq < D / 64; ++kq) {
-          const int lc = 4 * kq + lmat;
+        for (int kq = 0; kq < D / 32; ++kq) {
+          const int lc = 2 * kq + (lmat >> 1);
           uint32_t x[4];
           ldmatrix_x4(kbase + r * ROWB + ((lc ^ lrow) << 4), x[0], x[1], x[2], x[3]);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t b0 = e4m3x2_to_f16x2((uint16_t)(x[j] & 0xffffu));
-            const uint32_t b1 = e4m3x2_to_f16x2((uint16_t)(x[j] >> 16));
-            Mma<MT>::run(s[nt], qa[4 * kq + j], b0, b1);
+          for (int hc = 0; hc < 2; ++hc) {
+            uint32_t a[4];
+            a[0] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc] & 0xffffu));
+            a[1] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc + 1] & 0xffffu));
+            a[2] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc] >> 16));
+            a[3] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc + 1] >> 16));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              Mma<MT>::run(s[nt], a, qb[nt][2 * kq + hc][0], qb[nt][2 * kq + hc][1]);
           }
         }
       }
     }
 
-    // ---- online softmax (exp2 domain)
+    // ---- online softmax per query head (column of S^T), exp2 domain
+    const bool v0 = vld[warp * 16 + g] != 0, v1 = vld[warp * 16 + g + 8] != 0;
+    uint32_t pb[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int tok = warp * 16 + nt * 8 + 2 * tig;
-      const bool v0 = vld[tok] != 0, v1 = vld[tok + 1] != 0;
-      s[nt][0] = v0 ? s[nt][0] * sc : -INFINITY;
-      s[nt][1] = v1 ? s[nt][1] * sc : -INFINITY;
-      s[nt][2] = v0 ? s[nt][2] * sc : -INFINITY;
-      s[nt][3] = v1 ? s[nt][3] * sc : -INFINITY;
-    }
-    float p[2][4];
-    {
-      float mx = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m0, mx);
-      const float base = m_new == -INFINITY ? 0.0f : m_new;
-      const float alpha = exp2f(m0 - base);
-      m0 = m_new;
-      p[0][0] = exp2f(s[0][0] - base);
-      p[0][1] = exp2f(s[0][1] - base);
-      p[1][0] = exp2f(s[1][0] - base);
-      p[1][1] = exp2f(s[1][1] - base);
-      l0 = l0 * alpha + ((p[0][0] + p[0][1]) + (p[1][0] + p[1][1]));
-      if (alpha != 1.0f) {
+    for (int nt = 0; nt < NT; ++nt) {
+      float alpha[2];
 #pragma unroll
-        for (int n = 0; n < D / 8; ++n) {
-          o[n][0] *= alpha;
-          o[n][1] *= alpha;
+      for (int e = 0; e < 2; ++e) {
+        const float x0 = v0 ? s[nt][e] * sc : -INFINITY;      // token g
+        const float x1 = v1 ? s[nt][e + 2] * sc : -INFINITY;  // token g + 8
+        float mx = fmaxf(x0, x1);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[nt][e], mx);
+        const float base = m_new == -INFINITY ? 0.0f : m_new;
+        alpha[e] = exp2f(m_run[nt][e] - base);
+        m_run[nt][e] = m_new;
+        const float p0 = exp2f(x0 - base), p1 = exp2f(x1 - base);
+        l_run[nt][e] = fmaf(l_run[nt][e], alpha[e], p0 + p1);
+        s[nt][e] = p0;
+        s[nt][e + 2] = p1;
+      }
+      if (alpha[0] != 1.0f || alpha[1] != 1.0f) {
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+          o[nt][j][0] *= alpha[0];
+          o[nt][j][1] *= alpha[1];
+          o[nt][j][2] *= alpha[0];
+          o[nt][j][3] *= alpha[1];
         }
       }
-    }
-    if (TWO_ROWS) {
-      float mx = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m1, mx);
-      const float base = m_new == -INFINITY ? 0.0f : m_new;
-      const float alpha = exp2f(m1 - base);
-      m1 = m_new;
-      p[0][2] = exp2f(s[0][2] - base);
-      p[0][3] = exp2f(s[0][3] - base);
-      p[1][2] = exp2f(s[1][2] - base);
-      p[1][3] = exp2f(s[1][3] - base);
-      l1 = l1 * alpha + ((p[0][2] + p[0][3]) + (p[1][2] + p[1][3]));
-      if (alpha != 1.0f) {
-#pragma unroll
-        for (int n = 0; n < D / 8; ++n) {
-          o[n][2] *= alpha;
-          o[n][3] *= alpha;
-        }
-      }
-    } else {
-      p[0][2] = p[0][3] = p[1][2] = p[1][3] = 0.0f;
+      // P^T as the B operand (K = tokens, N = heads): transpose the 8x8 blocks
+      pb[nt][0] = movmatrix_trans(pack2<MT>(s[nt][0], s[nt][1]));  // tokens 0-7
+      pb[nt][1] = movmatrix_trans(pack2<MT>(s[nt][2], s[nt][3]));  // tokens 8-15
     }
 
-    // ---- O += P V (P as the A operand straight from the S accumulator layout)
-    uint32_t pa[4];
-    pa[0] = pack2<MT>(p[0][0], p[0][1]);
-    pa[1] = pack2<MT>(p[0][2], p[0][3]);
-    pa[2] = pack2<MT>(p[1][0], p[1][1]);
-    pa[3] = pack2<MT>(p[1][2], p[1][3]);
-    const int vr = warp * 16 + ((lmat & 1) << 3) + lrow;  // token row this lane addresses
+    // ---- O^T += V^T P^T, one 16-row (head_dim) M tile per MMA
     if (!kFp8) {
+      // matrices: 0 = (tokens 0-7, chunk 2c), 1 = (tokens 0-7, chunk 2c+1),
+      //           2 = (tokens 8-15, chunk 2c), 3 = (tokens 8-15, chunk 2c+1)
+      const int r = warp * 16 + ((lmat >> 1) << 3) + lrow;
 #pragma unroll
-      for (int cp = 0; cp < D / 16; ++cp) {
-        const int lc = 2 * cp + (lmat >> 1);
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(vbase + vr * ROWB + ((lc ^ lrow) << 4), b0, b1, b2, b3);
-        Mma<MT>::run(o[2 * cp], pa, b0, b1);
-        Mma<MT>::run(o[2 * cp + 1], pa, b2, b3);
+      for (int c = 0; c < D / 16; ++c) {
+        const int lc = 2 * c + (lmat & 1);
+        uint32_t a[4];
+        ldmatrix_x4_trans(vbase + r * ROWB + ((lc ^ lrow) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[nt][c], a, pb[nt][0], pb[nt][1]);
       }
     } else {
-      // ldmatrix.trans over e4m3 rows gives, per register, tokens (2tig, 2tig+1) x
-      // d (2g, 2g+1) of a 16-column chunk; a byte permute splits even and odd d.
+      // ldmatrix.trans over e4m3 rows: a register holds tokens (2tig, 2tig+1) x
+      // d (2g, 2g+1) of a 16-column chunk; a byte permute separates even d (M rows
+      // 0-7 of the tile) from odd d (M rows 8-15).
+      const int r = warp * 16 + ((lmat & 1) << 3) + lrow;
 #pragma unroll
       for (int cq = 0; cq < D / 32; ++cq) {
         const int lc = 2 * cq + (lmat >> 1);
         uint32_t x[4];
-        ldmatrix_x4_trans(vbase + vr * ROWB + ((lc ^ lrow) << 4), x[0], x[1], x[2], x[3]);
+        ldmatrix_x4_trans(vbase + r * ROWB + ((lc ^ lrow) << 4), x[0], x[1], x[2], x[3]);
 #pragma unroll
-        for (int hc = 0; hc < 2; ++hc) {  // chunk 2cq + hc: x[2hc] tokens 0-7, x[2hc+1] tokens 8-15
-          const uint32_t lo = __byte_perm(x[2 * hc], 0u, 0x3120);
-          const uint32_t hi = __byte_perm(x[2 * hc + 1], 0u, 0x3120);
-          Mma<MT>::run(o[4 * cq + 2 * hc + 0], pa, e4m3x2_to_f16x2((uint16_t)(lo & 0xffffu)),
-                       e4m3x2_to_f16x2((uint16_t)(hi & 0xffffu)));
-          Mma<MT>::run(o[4 * cq + 2 * hc + 1], pa, e4m3x2_to_f16x2((uint16_t)(lo >> 16)),
-                       e4m3x2_to_f16x2((uint16_t)(hi >> 16)));
+        for (int hc = 0; hc < 2; ++hc) {
+          const uint32_t ya = __byte_perm(x[2 * hc], 0u, 0x3120);      // tokens 0-7
+          const uint32_t yb = __byte_perm(x[2 * hc + 1], 0u, 0x3120);  // tokens 8-15
+          uint32_t a[4];
+          a[0] = e4m3x2_to_f16x2((uint16_t)(ya & 0xffffu));
+          a[1] = e4m3x2_to_f16x2((uint16_t)(ya >> 16));
+          a[2] = e4m3x2_to_f16x2((uint16_t)(yb & 0xffffu));
+          a[3] = e4m3x2_to_f16x2((uint16_t)(yb >> 16));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[nt][2 * cq + hc], a, pb[nt][0], pb[nt][1]);
         }
       }
     }
@@ -607,114 +710,62 @@ paged_decode_tc_kernel(const DecodeParams p) {
   __syncthreads();
 
   // ---- merge the 4 warps' states through shared memory (reusing the ring)
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  if (TWO_ROWS) {
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  }
-  constexpr int RP = D + 4;  // padded row pitch (floats)
-  float* red_acc = reinterpret_cast<float*>(smem);               // [4][16][RP]
-  float* red_m = red_acc + 4 * kMaxHeadsPerCta * RP;             // [4][16]
-  float* red_l = red_m + 4 * kMaxHeadsPerCta;                    // [4][16]
-  static_assert((4 * kMaxHeadsPerCta * RP + 8 * kMaxHeadsPerCta) * 4 <= STAGES * STAGE_BYTES,
-                "merge buffer fits in the ring");
-  auto out_col = [&](int n, int e) -> int {  // column of accumulator o[n][e] / o[n][e+2]
-    if (kFp8) {
-      const int chunk = n >> 1, odd = n & 1;
-      return 16 * chunk + 4 * tig + 2 * e + odd;
-    }
-    return 8 * n + 2 * tig + e;
-  };
-  {
-    float* ra = red_acc + (warp * kMaxHeadsPerCta + g) * RP;
+  constexpr int RP = D + 4;     // padded row pitch (floats)
+  constexpr int HC = 8 * NT;    // head slots of this CTA
+  float* red_acc = reinterpret_cast<float*>(smem);  // [4][HC][RP]; slot 0 becomes the merged O
+  float* red_m = red_acc + 4 * HC * RP;             // [4][HC]
+  float* red_l = red_m + 4 * HC;                    // [4][HC]
+  float* m_s = red_l + 4 * HC;                      // [HC]
+  float* l_s = m_s + HC;                            // [HC]
+  float* wts = l_s + HC;                            // [(kMaxSplits + 1) * HC]
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n) {
-      ra[out_col(n, 0)] = o[n][0];
-      ra[out_col(n, 1)] = o[n][1];
-    }
-    if (tig == 0) {
-      red_m[warp * kMaxHeadsPerCta + g] = m0;
-      red_l[warp * kMaxHeadsPerCta + g] = l0;
-    }
-    if (TWO_ROWS) {
-      float* rb = red_acc + (warp * kMaxHeadsPerCta + g + 8) * RP;
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        rb[out_col(n, 0)] = o[n][2];
-        rb[out_col(n, 1)] = o[n][3];
+    for (int e = 0; e < 2; ++e) {
+      float l = l_run[nt][e];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      const int head = nt * 8 + 2 * tig + e;
+      float* ra = red_acc + (warp * HC + head) * RP;
+#pragma unroll
+      for (int j = 0; j < D / 16; ++j) {
+        // O^T rows: 16-bit pages d = 16j + g / 16j + 8 + g; e4m3 pages d = 16j + 2g / + 1
+        const int d0 = kFp8 ? 16 * j + 2 * g : 16 * j + g;
+        const int d1 = kFp8 ? d0 + 1 : d0 + 8;
+        ra[d0] = o[nt][j][e];
+        ra[d1] = o[nt][j][e + 2];
       }
-      if (tig == 0) {
-        red_m[warp * kMaxHeadsPerCta + g + 8] = m1;
-        red_l[warp * kMaxHeadsPerCta + g + 8] = l1;
+      if (g == 0) {
+        red_m[warp * HC + head] = m_run[nt][e];
+        red_l[warp * HC + head] = l;
       }
     }
-  }
   __syncthreads();
-
-  const bool direct = rng.active == 1;
-  for (int idx = tid; idx < nh * D; idx += kThreads) {
-    const int h = idx / D, d = idx - h * D;
+  if (tid < nh) {
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, red_m[w * kMaxHeadsPerCta + h]);
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red_m[w * HC + tid]);
     const float base = M == -INFINITY ? 0.0f : M;
-    float O = 0.0f, L = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float wgt = exp2f(red_m[w * kMaxHeadsPerCta + h] - base);
-      O = fmaf(wgt, red_acc[(w * kMaxHeadsPerCta + h) * RP + d], O);
-      L = fmaf(wgt, red_l[w * kMaxHeadsPerCta + h], L);
-    }
-    const int head = h0 + h;
-    if (direct) {
-      QT* op = reinterpret_cast<QT*>(p.out);
-      op[(int64_t)seq * p.o_sb + (int64_t)head * p.o_sh + d] = from_f32<QT>(O * vs_scale / L);
-    } else {
-      const int64_t b = ((int64_t)seq * p.num_heads + head) * p.num_splits + split;
-      p.part_acc[b * D + d] = O;
-      if (d == 0) {
-        p.part_ml[b * 2 + 0] = M;
-        p.part_ml[b * 2 + 1] = L;
-      }
-    }
-  }
-}
-
-// ============================================================ split merge
-// One CTA per (head, sequence): combines the active splits' (m, l, acc) and writes
-// out = (sum_s 2^(m_s - M) acc_s) * v_scale / (sum_s 2^(m_s - M) l_s).
-template <typename QT>
-__global__ void __launch_bounds__(kThreads) split_merge_kernel(const DecodeParams p) {
-  const int head = blockIdx.x, seq = blockIdx.y;
-  const SplitRange rng = split_range(p, seq, 0);
-  if (rng.active <= 1) return;  // written directly by the split kernel
-  const int64_t base = ((int64_t)seq * p.num_heads + head) * p.num_splits;
-  __shared__ float wts[512];
-  __shared__ float sh_l;
-  float M = -INFINITY;
-  for (int s = 0; s < rng.active; ++s) M = fmaxf(M, p.part_ml[(base + s) * 2]);
-  const float mb = M == -INFINITY ? 0.0f : M;
-  for (int s = threadIdx.x; s < rng.active; s += blockDim.x)
-    wts[s] = exp2f(p.part_ml[(base + s) * 2] - mb);
-  __syncthreads();
-  if (threadIdx.x == 0) {
     float L = 0.0f;
-    for (int s = 0; s < rng.active; ++s) L = fmaf(wts[s], p.part_ml[(base + s) * 2 + 1], L);
-    sh_l = L;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) L = fmaf(exp2f(red_m[w * HC + tid] - base), red_l[w * HC + tid], L);
+    m_s[tid] = M;
+    l_s[tid] = L;
   }
   __syncthreads();
-  const float vs = p.v_scale != nullptr ? __ldg(p.v_scale) : 1.0f;
-  const float L = sh_l;
-  QT* op = reinterpret_cast<QT*>(p.out);
-  for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
+  for (int idx = tid; idx < nh * D; idx += kThreads) {
+    const int h = idx / D, d = idx - h * D;
+    const float base = m_s[h] == -INFINITY ? 0.0f : m_s[h];
     float O = 0.0f;
-    for (int s = 0; s < rng.active; ++s) O = fmaf(wts[s], p.part_acc[(base + s) * p.head_dim + d], O);
-    op[(int64_t)seq * p.o_sb + (int64_t)head * p.o_sh + d] = from_f32<QT>(O * vs / L);
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+      O = fmaf(exp2f(red_m[w * HC + h] - base), red_acc[(w * HC + h) * RP + d], O);
+    red_acc[h * RP + d] = O;  // in place: this thread alone reads and writes (h, d)
   }
+  __syncthreads();
+  finish_cta<QT>(p, seq, blockIdx.y, h0, nh, split, rng.active, red_acc, RP, m_s, l_s, wts);
 }
-
-constexpr int kMaxSplits = 512;  // split_merge_kernel's weight buffer
 
 // ============================================================ host side
 struct SplitPlan {
@@ -758,11 +809,22 @@ SplitPlan plan_splits(int num_seqs, int num_kv_heads, int head_groups, int block
 
 int head_groups_for(int group) { return (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta; }
 
-size_t workspace_bytes_for(int num_seqs, int num_heads, int head_dim, int num_splits) {
-  if (num_splits <= 1) return 0;
+// Workspace layout (each part 256-byte aligned): partial accumulators, partial (m, l),
+// arrival counters.
+struct WorkspaceLayout {
+  size_t acc, ml, ctr, total;
+};
+WorkspaceLayout workspace_layout(int num_seqs, int num_heads, int num_kv_heads, int head_dim,
+                                 int num_splits) {
+  WorkspaceLayout w{0, 0, 0, 0};
+  if (num_splits <= 1) return w;
   const size_t n = (size_t)num_seqs * num_heads * num_splits;
-  const size_t acc = round_up((int64_t)(n * head_dim * sizeof(float)), 256);
-  return acc + n * 2 * sizeof(float);
+  const size_t groups = (size_t)num_seqs * num_kv_heads * head_groups_for(num_heads / num_kv_heads);
+  w.acc = 0;
+  w.ml = round_up((int64_t)(n * head_dim * sizeof(float)), 256);
+  w.ctr = w.ml + round_up((int64_t)(n * 2 * sizeof(float)), 256);
+  w.total = w.ctr + round_up((int64_t)(groups * sizeof(unsigned int)), 256);
+  return w;
 }
 
 // One cudaFuncSetAttribute per kernel instantiation and device.
@@ -790,26 +852,37 @@ int launch_generic(const DecodeParams& p, dim3 grid, cudaStream_t stream, int de
   return cuda_status(cudaGetLastError(), "paged_decode_generic launch");
 }
 
-template <typename QT, typename CT>
-int launch_tc(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
-  constexpr size_t smem = tc_smem_bytes<CT>();
-  if (p.heads_per_cta > 8) {
-    int st = ensure_smem<paged_decode_tc_kernel<QT, CT, true>>(smem, device);
-    if (st != MKV_OK) return st;
-    paged_decode_tc_kernel<QT, CT, true><<<grid, kThreads, smem, stream>>>(p);
-  } else {
-    int st = ensure_smem<paged_decode_tc_kernel<QT, CT, false>>(smem, device);
-    if (st != MKV_OK) return st;
-    paged_decode_tc_kernel<QT, CT, false><<<grid, kThreads, smem, stream>>>(p);
-  }
+// Pipeline depth and CTAs per SM: 16-bit pages 2 stages x 32 KB (3 CTAs/SM), e4m3
+// pages 3 stages x 16 KB (4 CTAs/SM).
+// Measured on B200 (config 3, bf16): 2 stages x 3 CTAs/SM 6.05 TB/s, 3 x 2 5.29 TB/s,
+// 4 x 1 2.99 TB/s -- the decode is bound by resident warps, not by ring depth.
+#ifndef MKV_TC16_STAGES
+#define MKV_TC16_STAGES 2
+#define MKV_TC16_MINB 3
+#endif
+#ifndef MKV_TC8_STAGES
+#define MKV_TC8_STAGES 3
+#define MKV_TC8_MINB 4
+#endif
+template <typename CT> struct TcConfig;
+template <> struct TcConfig<bf16> { static constexpr int kStages = MKV_TC16_STAGES, kMinBlocks = MKV_TC16_MINB; };
+template <> struct TcConfig<f16> { static constexpr int kStages = MKV_TC16_STAGES, kMinBlocks = MKV_TC16_MINB; };
+template <> struct TcConfig<fp8> { static constexpr int kStages = MKV_TC8_STAGES, kMinBlocks = MKV_TC8_MINB; };
+
+template <typename QT, typename CT, int NT>
+int launch_tc_nt(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
+  constexpr int S = TcConfig<CT>::kStages, MB = TcConfig<CT>::kMinBlocks;
+  constexpr size_t smem = tc_smem_bytes<CT, NT, S>();
+  int st = ensure_smem<paged_decode_tc_kernel<QT, CT, NT, S, MB>>(smem, device);
+  if (st != MKV_OK) return st;
+  paged_decode_tc_kernel<QT, CT, NT, S, MB><<<grid, kThreads, smem, stream>>>(p);
   return cuda_status(cudaGetLastError(), "paged_decode_tc launch");
 }
 
-template <typename QT>
-int launch_merge(const DecodeParams& p, cudaStream_t stream) {
-  dim3 grid(p.num_heads, p.num_seqs);
-  split_merge_kernel<QT><<<grid, kThreads, 0, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "split_merge launch");
+template <typename QT, typename CT>
+int launch_tc(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
+  return p.heads_per_cta > 8 ? launch_tc_nt<QT, CT, 2>(p, grid, stream, device)
+                             : launch_tc_nt<QT, CT, 1>(p, grid, stream, device);
 }
 
 int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, int q_dtype,
@@ -840,8 +913,9 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
     return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
   if (num_seqs > 65535)
     return set_error(MKV_ERR_UNSUPPORTED, "%s: num_seqs > 65535", fn);
-  if ((int64_t)max_blocks * block_size >= ((int64_t)1 << 31))
-    return set_error(MKV_ERR_UNSUPPORTED, "%s: max_num_blocks * block_size must be < 2^31", fn);
+  if ((int64_t)max_blocks * block_size >= ((int64_t)1 << 31) || num_blocks >= ((int64_t)1 << 31))
+    return set_error(MKV_ERR_UNSUPPORTED,
+                     "%s: max_num_blocks * block_size and num_blocks must be < 2^31", fn);
   if (head_dim % 16 != 0 || head_dim > 256)
     return set_error(MKV_ERR_UNSUPPORTED,
                      "%s: head_dim must be a multiple of 16 and at most 256 (got %d)", fn,
@@ -864,11 +938,11 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   if ((int64_t)num_kv_heads * hgs > 65535)
     return set_error(MKV_ERR_UNSUPPORTED, "%s: too many kv heads", fn);
   const SplitPlan sp = plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_blocks, num_splits);
-  const size_t need = workspace_bytes_for(num_seqs, num_heads, head_dim, sp.num_splits);
-  if (need > 0 && (workspace == nullptr || ws_bytes < need))
-    return set_error(MKV_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, need,
-                     workspace ? ws_bytes : (size_t)0);
-  if (need > 0 && ((uintptr_t)workspace & 15u))
+  const WorkspaceLayout wl = workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits);
+  if (wl.total > 0 && (workspace == nullptr || ws_bytes < wl.total))
+    return set_error(MKV_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn,
+                     wl.total, workspace ? ws_bytes : (size_t)0);
+  if (wl.total > 0 && ((uintptr_t)workspace & 15u))
     return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
 
   DecodeParams p;
@@ -901,48 +975,38 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.o_sh = o_sh;
   p.num_splits = sp.num_splits;
   p.chunk = sp.chunk;
-  p.part_acc = need > 0 ? (float*)workspace : nullptr;
-  p.part_ml = need > 0 ? (float*)((uint8_t*)workspace +
-                                  round_up((int64_t)((size_t)num_seqs * num_heads * sp.num_splits *
-                                                     head_dim * sizeof(float)),
-                                           256))
-                       : nullptr;
+  uint8_t* ws = (uint8_t*)workspace;
+  p.part_acc = wl.total ? (float*)(ws + wl.acc) : nullptr;
+  p.part_ml = wl.total ? (float*)(ws + wl.ml) : nullptr;
+  p.arrivals = wl.total ? (unsigned int*)(ws + wl.ctr) : nullptr;
   p.invalid = invalid;
 
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
   cudaStream_t s = (cudaStream_t)stream;
+  if (wl.total) {  // arrival counters start at zero (the kernel leaves them at zero)
+    e = cudaMemsetAsync(ws + wl.ctr, 0, wl.total - wl.ctr, s);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(arrival counters)");
+  }
   dim3 grid(sp.num_splits, num_kv_heads * hgs, num_seqs);
 
   const bool tc_ok = head_dim == kTcD && q_dtype != MKV_DTYPE_F32;
-  int st;
-  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_BF16)
-    st = launch_tc<bf16, bf16>(p, grid, s, device);
-  else if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_F16)
-    st = launch_tc<f16, f16>(p, grid, s, device);
-  else if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16)
-    st = launch_tc<bf16, fp8>(p, grid, s, device);
-  else if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16)
-    st = launch_tc<f16, fp8>(p, grid, s, device);
-  else if (fp8_cache) {
+  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, bf16>(p, grid, s, device);
+  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, f16>(p, grid, s, device);
+  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, fp8>(p, grid, s, device);
+  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, fp8>(p, grid, s, device);
+  if (fp8_cache) {
     switch (q_dtype) {
-      case MKV_DTYPE_F32: st = launch_generic<float, fp8>(p, grid, s, device); break;
-      case MKV_DTYPE_F16: st = launch_generic<f16, fp8>(p, grid, s, device); break;
-      default: st = launch_generic<bf16, fp8>(p, grid, s, device); break;
-    }
-  } else {
-    switch (q_dtype) {
-      case MKV_DTYPE_F32: st = launch_generic<float, float>(p, grid, s, device); break;
-      case MKV_DTYPE_F16: st = launch_generic<f16, f16>(p, grid, s, device); break;
-      default: st = launch_generic<bf16, bf16>(p, grid, s, device); break;
+      case MKV_DTYPE_F32: return launch_generic<float, fp8>(p, grid, s, device);
+      case MKV_DTYPE_F16: return launch_generic<f16, fp8>(p, grid, s, device);
+      default: return launch_generic<bf16, fp8>(p, grid, s, device);
     }
   }
-  if (st != MKV_OK || sp.num_splits <= 1) return st;
   switch (q_dtype) {
-    case MKV_DTYPE_F32: return launch_merge<float>(p, s);
-    case MKV_DTYPE_F16: return launch_merge<f16>(p, s);
-    default: return launch_merge<bf16>(p, s);
+    case MKV_DTYPE_F32: return launch_generic<float, float>(p, grid, s, device);
+    case MKV_DTYPE_F16: return launch_generic<f16, f16>(p, grid, s, device);
+    default: return launch_generic<bf16, bf16>(p, grid, s, device);
   }
 }
 
@@ -970,7 +1034,7 @@ extern "C" size_t mkv_paged_decode_workspace_bytes(int32_t num_seqs, int32_t num
   const int hgs = head_groups_for(num_heads / num_kv_heads);
   const SplitPlan sp =
       plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, num_splits);
-  return workspace_bytes_for(num_seqs, num_heads, head_dim, sp.num_splits);
+  return workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits).total;
 }
 
 extern "C" int mkv_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_head,

@@ -60,9 +60,11 @@ def test_split_plan(B, H, KVH, BS, MAXB, expect):
 
 def test_workspace_bytes():
     lib = lib_mod.load()
-    n = 256 * 32 * 8
-    acc = (n * 128 * 4 + 255) // 256 * 256
-    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 0) == acc + n * 8
+    n = 256 * 32 * 8                      # (seq, head, split) partials
+    acc = (n * 128 * 4 + 255) // 256 * 256   # partial accumulators
+    ml = (n * 8 + 255) // 256 * 256          # partial (m, l)
+    ctr = (256 * 8 * 4 + 255) // 256 * 256   # one arrival counter per (seq, kv head)
+    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 0) == acc + ml + ctr
     assert lib.mkv_paged_decode_workspace_bytes(8, 8, 8, 128, 16, 1, 0) == 0
     # a forced split count overrides the plan
     assert lib.mkv_paged_decode_workspace_bytes(2, 4, 2, 64, 16, 8, 4) > 0
