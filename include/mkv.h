@@ -193,6 +193,39 @@ MKV_API int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq, int64_
                          void* workspace, size_t workspace_bytes, int32_t num_splits,
                          int32_t* invalid_count, void* stream);
 
+/*
+ * Paged-attention decode that allocates nothing and needs no workspace argument.
+ * This entry point has no counterpart in the reference; it exists for callers that
+ * cannot allocate device memory on their own: a host runtime that reserves all device
+ * memory up front and hands out no temporary buffers, a real-time serving loop where
+ * the device synchronisation of cudaMalloc is not allowed, or a foreign-language caller
+ * (cgo, JNI, a C application) that holds device pointers from another runtime but has
+ * no device allocator to create the decode workspace.
+ *
+ * It computes exactly what mkv_paged_decode computes (same arguments, minus the
+ * workspace; bf16/fp16/fp32 caches only). The split-KV scratch lives in an array built
+ * into the library, MKV_NOALLOC_SCRATCH_BYTES (16 MiB) per device, which every GPU
+ * that loads the library keeps until the process exits. A shape whose split scratch
+ * (mkv_paged_decode_workspace_bytes with the same num_splits) exceeds that size is
+ * rejected with MKV_ERR_WORKSPACE; num_splits = 1 needs no scratch at all.
+ * The first call on a device looks up the array's device address (once per device,
+ * with that device current); make that first call before any stream capture.
+ * All calls on a device share the one array: the part that must start at zero is
+ * cleared on the stream at each call, but calls that overlap on the GPU (other streams,
+ * other host threads) race on it and must be serialised by the caller.
+ */
+#define MKV_NOALLOC_SCRATCH_BYTES (16u << 20)
+MKV_API int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq, int64_t q_stride_head,
+                                     int32_t q_dtype, const void* k_cache, const void* v_cache,
+                                     int32_t cache_dtype, int64_t num_blocks, int32_t block_size,
+                                     const void* block_tables, int32_t block_table_index_type,
+                                     int64_t block_table_stride_seq, int32_t max_num_blocks,
+                                     const void* context_lens, int32_t context_lens_index_type,
+                                     int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                                     int32_t head_dim, float scale, void* out,
+                                     int64_t out_stride_seq, int64_t out_stride_head,
+                                     int32_t num_splits, int32_t* invalid_count, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

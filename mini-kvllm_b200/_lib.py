@@ -18,6 +18,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_FP8_E4M3 = 0, 1, 2, 3
 INDEX_I32, INDEX_I64 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 FP8_CALIB_WORK_BYTES = 16
+NOALLOC_SCRATCH_BYTES = 16 << 20
 
 # Every symbol include/mkv.h declares, with (restype, argtypes).
 _p, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -37,6 +38,9 @@ SIGNATURES: dict[str, tuple] = {
     "mkv_paged_decode": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),
+    "mkv_paged_decode_noalloc": (ctypes.c_int, [
+        _p, _i64, _i64, _i32, _p, _p, _i32, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
+        _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
     "mkv_paged_decode_fp8": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),

@@ -30,6 +30,7 @@
 //     counter; the last split to arrive merges them and writes the output, so there
 //     is no second kernel. The split count depends only on shapes (graph-safe).
 // A CUDA-core kernel with the same tiling and epilogue covers fp32 and other head dims.
+#include <mutex>
 #include <type_traits>
 
 #include "mkv_common.cuh"
@@ -1010,6 +1011,33 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   }
 }
 
+// ---------------------------------------------------------------- allocation-free entry
+// Built-in decode scratch for callers that cannot allocate device memory. Every device
+// that loads this library holds these MKV_NOALLOC_SCRATCH_BYTES until the process ends.
+// Host code only sees a shadow of this symbol: its device address is looked up once per
+// device below and passed to the kernels like any caller workspace.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MKV_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up on first use).
+int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return set_error(MKV_ERR_UNSUPPORTED, "mkv_paged_decode_noalloc: device id %d >= %d", device,
+                     kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[device] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(built-in decode scratch)");
+    g_noalloc_ptr[device] = ptr;
+  }
+  *out = g_noalloc_ptr[device];
+  return MKV_OK;
+}
+
 }  // namespace
 }  // namespace mkv
 
@@ -1076,4 +1104,46 @@ extern "C" int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
                      workspace_bytes, num_splits, invalid_count, stream);
+}
+
+extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
+                                        int64_t q_stride_head, int32_t q_dtype,
+                                        const void* k_cache, const void* v_cache,
+                                        int32_t cache_dtype, int64_t num_blocks,
+                                        int32_t block_size, const void* block_tables,
+                                        int32_t block_table_index_type,
+                                        int64_t block_table_stride_seq, int32_t max_num_blocks,
+                                        const void* context_lens, int32_t context_lens_index_type,
+                                        int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+                                        int32_t head_dim, float scale, void* out,
+                                        int64_t out_stride_seq, int64_t out_stride_head,
+                                        int32_t num_splits, int32_t* invalid_count,
+                                        void* stream) {
+  clear_error();
+  if (cache_dtype == MKV_DTYPE_FP8_E4M3)
+    return set_error(MKV_ERR_INVALID_ARGUMENT,
+                     "mkv_paged_decode_noalloc: FP8 caches go through mkv_paged_decode_fp8");
+  const size_t need = mkv_paged_decode_workspace_bytes(num_seqs, num_heads, num_kv_heads, head_dim,
+                                                       block_size, max_num_blocks, num_splits);
+  if (need > (size_t)MKV_NOALLOC_SCRATCH_BYTES)
+    return set_error(MKV_ERR_WORKSPACE,
+                     "mkv_paged_decode_noalloc: this shape needs %zu bytes of split scratch but the "
+                     "built-in scratch holds %zu; pass a smaller num_splits (1 needs none) or call "
+                     "mkv_paged_decode with a workspace",
+                     need, (size_t)MKV_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (need > 0) {
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+    int st = noalloc_scratch(device, &scratch);
+    if (st != MKV_OK) return st;
+  }
+  return decode_impl("mkv_paged_decode_noalloc", query, q_stride_seq, q_stride_head, q_dtype,
+                     k_cache, v_cache, cache_dtype, nullptr, nullptr, num_blocks, block_size,
+                     block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
+                     context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
+                     head_dim, scale, out, out_stride_seq, out_stride_head, scratch,
+                     scratch ? (size_t)MKV_NOALLOC_SCRATCH_BYTES : 0, num_splits, invalid_count,
+                     stream);
 }
