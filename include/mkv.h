@@ -6,7 +6,7 @@
  *     quantised to FP8 E4M3 with a per-tensor scale), and
  *   - the paged-attention decode (one query token per sequence, GQA head
  *     grouping, FP8 dequantisation fused into the page loads, online softmax,
- *     split-KV partitioning with a merge kernel).
+ *     split-KV partitioning with an in-kernel merge).
  *
  * Every entry point takes plain device pointers, element strides and sizes, and a
  * CUDA stream passed as `void*` (a `cudaStream_t`; NULL = legacy default stream).
@@ -136,15 +136,23 @@ MKV_API int mkv_store_kvcache_fp8(const void* key, const void* value,
                           int32_t dtype, int32_t* invalid_count, void* stream);
 
 /*
- * Number of KV splits the decode uses for this shape when num_splits = 0 (auto).
- * Host-only; depends on shapes, never on device data.
+ * Split count the decode uses for this shape when num_splits = 0 (auto). Returns 0
+ * when auto means the balanced schedule: the grid is the kernel's resident CTAs and
+ * each takes an equal share of all (sequence, kv head) token tiles, computed on the
+ * device from context_lens, so long units are split where CTA shares end. A positive
+ * value is a fixed split count (only for shapes beyond the balanced schedule's
+ * 64-bit work-item arithmetic). Host-only; depends on shapes, never on device data.
  */
 MKV_API int32_t mkv_paged_decode_num_splits(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
                                     int32_t head_dim, int32_t block_size, int32_t max_num_blocks);
 
 /*
- * Bytes of workspace the decode needs for this shape and split count
- * (num_splits = 0 means the automatic choice). 0 when no split is used.
+ * Bytes of workspace the decode needs for this shape and split count.
+ * num_splits = 0 (auto, balanced schedule): 2 partial slots per resident CTA
+ * (at most 148 x 4 CTAs) of min(H / KVH, 16) heads x (head_dim + 2) floats, plus one
+ * arrival counter per (sequence, kv head, head group); it does not grow with the
+ * context length. num_splits > 0: one partial per (sequence, head, split) plus the
+ * counters; 0 when num_splits = 1.
  */
 MKV_API size_t mkv_paged_decode_workspace_bytes(int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
                                         int32_t head_dim, int32_t block_size,

@@ -10,7 +10,7 @@
 // = softmax(scale * q.K) V in fp32, stored in the query dtype; no visible token -> NaN.
 //
 // B200 design (HBM-bound: ~2 * G FLOP per cache byte):
-//   * one CTA per (sequence, kv head, KV split) covers the whole GQA group, so each
+//   * a CTA works on (sequence, kv head) units and covers the whole GQA group, so each
 //     page row is read from HBM once, not G times as in the reference's (seq, head) grid;
 //   * pages stream through a multi-stage cp.async ring of 64-token tiles in shared
 //     memory (16-byte chunks, XOR-swizzled so ldmatrix reads are conflict-free); the
@@ -25,15 +25,21 @@
 //     scale and V's into the output;
 //   * online softmax in the exp2 domain; 4 warps split each tile and merge their
 //     (m, l, acc) through shared memory at the end;
-//   * long or ragged contexts are split into fixed-size token chunks (flash-decoding).
-//     Each split writes (m, l, acc) to the workspace and bumps a per-(seq, kv head)
-//     counter; the last split to arrive merges them and writes the output, so there
-//     is no second kernel. The split count depends only on shapes (graph-safe).
+//   * balanced persistent schedule (num_splits = 0): the grid is the kernel's resident
+//     CTAs (occupancy x SMs) and each CTA reads the context lengths once and takes an
+//     equal share of all (unit, tile) work items, so ragged batches and uniform long
+//     contexts both load every SM evenly, with no wave tail and no per-chunk restart.
+//     A unit that crosses a CTA boundary is finished by partials: each writes
+//     (m, l, acc) to the workspace and bumps the unit's counter; the last to arrive
+//     merges them and writes the output, so there is no second kernel. A forced
+//     num_splits > 0 instead splits every unit into fixed token chunks (flash-decoding)
+//     with the same epilogue. Nothing on the host depends on device data (graph-safe).
 // A CUDA-core kernel with the same tiling and epilogue covers fp32 and other head dims.
 #include <mutex>
 #include <type_traits>
 
 #include "mkv_common.cuh"
+#include "paged_decode_tc05.cuh"
 
 namespace mkv {
 namespace {
@@ -42,7 +48,7 @@ constexpr int kThreads = 128;        // 4 warps per CTA (both kernels)
 constexpr int kMaxHeadsPerCta = 16;  // query heads of one KV head handled by a CTA
 constexpr int kTcTile = 64;          // tokens per pipeline stage, tensor-core kernel
 constexpr int kGenTile = 32;         // tokens per pipeline stage, CUDA-core kernel
-constexpr int kChunkAlign = 64;      // split boundaries are multiples of both tiles
+constexpr int kChunkAlign = 128;     // split boundaries are multiples of every tile
 constexpr int kMaxSplits = 128;  // bounds the merge-weight buffer in shared memory
 constexpr int kMaxBtSmem = 128;      // block-table entries staged in shared memory
 constexpr float kLog2e = 1.4426950408889634f;
@@ -75,6 +81,11 @@ struct DecodeParams {
   unsigned int* arrivals;  // [num_seqs][num_kv_heads * head_groups], zero between launches
   int num_splits;
   int chunk;  // tokens per split, multiple of kChunkAlign
+  // Balanced schedule (num_splits = 0): the grid is sched_ctas resident CTAs and each
+  // takes an equal share of all (unit, tile) work items; every CTA gets >= min_tiles.
+  int balanced;
+  int sched_ctas;
+  int min_tiles;
   int32_t* invalid;
 };
 
@@ -121,12 +132,214 @@ __device__ __forceinline__ SplitRange split_range(const DecodeParams& p, int seq
   return r;
 }
 
-// Block-table slice of the split in shared memory (validated pages, -1 = none).
+// ---------------------------------------------------------------- work schedule
+// A unit is (sequence, KV head, head group): y = kv_head * head_groups + head group.
+// A segment is a contiguous token range of one unit processed by one CTA. With a fixed
+// split count (num_splits > 0) a CTA runs the single segment (split, y, seq) of its
+// grid coordinates. With the balanced schedule the tiles of all units are numbered
+// unit by unit (sequence-major) into W work items, CTA c of G takes items
+// [W*c/G, W*(c+1)/G), and so walks one or more segments; a unit that crosses a CTA
+// boundary is finished by partials. Partial k of a unit lives in slot
+// 2*(c_first + k) + (k == 0 ? first_off : 0): slot 2c holds CTA c's first segment,
+// 2c+1 its last, so every slot has one writer and the workspace is bounded by 2G slots.
+struct TokRange {
+  int begin, end;
+};
+struct Seg {
+  int seq, y;
+  int begin, end;  // token range [begin, end)
+  int nparts;      // partials of the unit (1 = this segment is the whole unit)
+  int part;        // this segment's index among them
+  int c_first, first_off;
+};
+
+__device__ __forceinline__ int eff_ctx(const DecodeParams& p, int seq) {
+  const int64_t ctx = load_ctx(p, seq);
+  const int64_t cap = (int64_t)p.max_blocks * p.block_size;
+  const int64_t eff = ctx < cap ? ctx : cap;
+  return eff > 0 ? (int)eff : 0;
+}
+// Tiles of one unit of the sequence; an empty context still takes one (empty) tile so
+// that its output (0/0 = NaN, as in the reference) is written.
+template <int TILE>
+__device__ __forceinline__ int unit_tiles(int eff) { return eff > 0 ? (eff + TILE - 1) / TILE : 1; }
+
+__device__ __forceinline__ long long warp_sum_ll(long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Schedule state, uniform across the CTA, kept in shared memory so the kernels' inner
+// loops carry none of it in registers. Thread 0 advances it between two barriers.
+struct SchedState {
+  long long w, w_end, unit_start, W, G;
+  int seq, y, nt, eff, U;
+  int has, fixed_pending;
+  Seg cur;
+};
+
+// CTA of work item x: the largest c with W*c/G <= x.
+__device__ __forceinline__ long long cta_of(const SchedState& st, long long x) {
+  return ((x + 1) * st.G - 1) / st.W;
+}
+
+// Block-collective (every thread calls it; it synchronises the block).
+template <int TILE>
+__device__ void sched_init(const DecodeParams& p, SchedState& st) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (!p.balanced) {
+    if (tid == 0) {
+      st.fixed_pending = 1;
+      st.U = p.num_kv_heads * p.head_groups;
+    }
+    __syncthreads();
+    return;
+  }
+  __shared__ long long red[kThreads / 32];
+  __shared__ long long found[2];
+  const int U = p.num_kv_heads * p.head_groups;
+  long long part = 0;
+  for (int s = tid; s < p.num_seqs; s += kThreads) part += unit_tiles<TILE>(eff_ctx(p, s));
+  part = warp_sum_ll(part);
+  if (lane == 0) red[warp] = part;
+  __syncthreads();
+  long long total = 0;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) total += red[i];
+  const long long W = total * U;
+  long long G = p.sched_ctas;
+  const long long by_work = W / p.min_tiles;  // every CTA gets >= min_tiles items
+  if (G > by_work) G = by_work > 0 ? by_work : 1;
+  const long long c = blockIdx.x;
+  long long w = 0, w_end = 0;
+  if (c < G) {  // uniform across the block
+    w = W * c / G;
+    w_end = W * (c + 1) / G;
+    // the sequence whose tile prefix P(s) satisfies P(s) <= w / U < P(s) + tiles(s)
+    const long long q = w / U;
+    long long carry = 0;
+    for (int base = 0; base < p.num_seqs; base += kThreads) {
+      const int s = base + tid;
+      const long long t = s < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, s)) : 0;
+      long long x = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long v = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += v;
+      }
+      __syncthreads();  // red is free again
+      if (lane == 31) red[warp] = x;
+      __syncthreads();
+      long long off = carry, chunk = 0;
+#pragma unroll
+      for (int i = 0; i < kThreads / 32; ++i) {
+        if (i < warp) off += red[i];
+        chunk += red[i];
+      }
+      const long long incl = off + x;
+      if (s < p.num_seqs && incl - t <= q && q < incl) {
+        found[0] = s;
+        found[1] = incl - t;
+      }
+      carry += chunk;
+      __syncthreads();
+      if (carry > q) break;
+    }
+  }
+  if (tid == 0) {
+    st.W = W;
+    st.G = G;
+    st.U = U;
+    st.w = w;
+    st.w_end = w_end;
+    st.fixed_pending = 0;
+    if (w < w_end) {
+      st.seq = (int)found[0];
+      st.eff = eff_ctx(p, st.seq);
+      st.nt = unit_tiles<TILE>(st.eff);
+      const long long r = w - found[1] * U;
+      st.y = (int)(r / st.nt);
+      st.unit_start = found[1] * U + (long long)st.y * st.nt;
+    }
+  }
+  __syncthreads();
+}
+
+// Block-collective: moves st.cur to the CTA's next segment; false when none is left.
+// Its first barrier also ends the previous segment's use of shared memory.
+template <int TILE>
+__device__ bool sched_next(const DecodeParams& p, SchedState& st) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Seg& sg = st.cur;
+    int has = 0;
+    if (!p.balanced) {
+      if (st.fixed_pending) {
+        st.fixed_pending = 0;
+        const SplitRange rng = split_range(p, blockIdx.z, blockIdx.x);
+        if (!(blockIdx.x > 0 && rng.begin >= rng.end)) {
+          has = 1;
+          sg.seq = blockIdx.z;
+          sg.y = blockIdx.y;
+          sg.begin = rng.begin;
+          sg.end = rng.end;
+          sg.nparts = rng.active;
+          sg.part = blockIdx.x;
+          sg.c_first = sg.first_off = 0;
+        }
+      }
+    } else if (st.w < st.w_end) {
+      has = 1;
+      const int nt = st.nt;
+      const int tb = (int)(st.w - st.unit_start);
+      const long long rem = st.w_end - st.unit_start;
+      const int te = rem < nt ? (int)rem : nt;
+      sg.seq = st.seq;
+      sg.y = st.y;
+      sg.begin = tb * TILE;
+      sg.end = min(te * TILE, st.eff);
+      const long long c_first = cta_of(st, st.unit_start);
+      const long long c_last = cta_of(st, st.unit_start + nt - 1);
+      sg.nparts = (int)(c_last - c_first + 1);
+      sg.part = (int)(blockIdx.x - c_first);
+      sg.c_first = (int)c_first;
+      sg.first_off = (st.W * c_first / st.G) < st.unit_start ? 1 : 0;
+      st.w = st.unit_start + te;
+      if (te == nt) {
+        st.unit_start += nt;
+        if (++st.y == st.U) {
+          st.y = 0;
+          ++st.seq;
+          if (st.w < st.w_end) {
+            st.eff = eff_ctx(p, st.seq);
+            st.nt = unit_tiles<TILE>(st.eff);
+          }
+        }
+      }
+    }
+    st.has = has;
+  }
+  __syncthreads();
+  return st.has != 0;
+}
+
+// Row (of head_dim floats in part_acc, of 2 floats in part_ml) of partial k, head h.
+__device__ __forceinline__ int64_t part_row(const DecodeParams& p, const Seg& sg, int h0, int k,
+                                            int h) {
+  if (p.balanced) {
+    const int slot = 2 * (sg.c_first + k) + (k == 0 ? sg.first_off : 0);
+    return (int64_t)slot * p.heads_per_cta + h;
+  }
+  return ((int64_t)sg.seq * p.num_heads + h0 + h) * p.num_splits + k;
+}
+
+// Block-table slice of the segment in shared memory (validated pages, -1 = none).
 struct BlockSlice {
   int lo, n;  // first logical block and count; n > kMaxBtSmem = not staged
 };
 __device__ __forceinline__ BlockSlice stage_block_table(const DecodeParams& p, int seq,
-                                                        const SplitRange& rng, int* bt_s,
+                                                        const TokRange& rng, int* bt_s,
                                                         bool count) {
   BlockSlice s{0, 0};
   if (rng.end > rng.begin) {
@@ -135,8 +348,11 @@ __device__ __forceinline__ BlockSlice stage_block_table(const DecodeParams& p, i
     split_token(p, rng.end - 1, hi, off);
     s.n = hi - s.lo + 1;
   }
-  if (s.n <= kMaxBtSmem)
+  if (s.n <= kMaxBtSmem) {
     for (int i = threadIdx.x; i < s.n; i += blockDim.x) bt_s[i] = page_of_block(p, seq, s.lo + i, count);
+  } else if (count) {  // not staged: the loads look pages up unchecked-for-counting, so count here
+    for (int i = threadIdx.x; i < s.n; i += blockDim.x) page_of_block(p, seq, s.lo + i, true);
+  }
   return s;
 }
 __device__ __forceinline__ int slice_page(const DecodeParams& p, int seq, const BlockSlice& s,
@@ -152,10 +368,11 @@ __device__ __forceinline__ int slice_page(const DecodeParams& p, int seq, const 
 // the output; it also zeroes the counter for the next launch. `wts` needs
 // (active + 1) * nh floats of shared memory.
 template <typename QT>
-__device__ void finish_cta(const DecodeParams& p, int seq, int cta_group, int h0, int nh,
-                           int split, int active, const float* o_s, int ld, const float* m_s,
-                           const float* l_s, float* wts) {
+__device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
+                           const float* o_s, int ld, const float* m_s, const float* l_s,
+                           float* wts) {
   const int D = p.head_dim;
+  const int seq = sg.seq, active = sg.nparts;
   const float vs = p.v_scale != nullptr ? __ldg(p.v_scale) : 1.0f;
   QT* op = reinterpret_cast<QT*>(p.out);
   if (active == 1) {
@@ -166,10 +383,9 @@ __device__ void finish_cta(const DecodeParams& p, int seq, int cta_group, int h0
     }
     return;
   }
-  const int64_t S = p.num_splits;
   for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
     const int h = idx / D, d = idx - h * D;
-    const int64_t b = ((int64_t)seq * p.num_heads + h0 + h) * S + split;
+    const int64_t b = part_row(p, sg, h0, sg.part, h);
     __stcg(p.part_acc + b * D + d, o_s[h * ld + d]);
     if (d == 0) {
       __stcg(p.part_ml + b * 2 + 0, m_s[h]);
@@ -179,32 +395,32 @@ __device__ void finish_cta(const DecodeParams& p, int seq, int cta_group, int h0
   __threadfence();
   __syncthreads();
   __shared__ bool last;
-  unsigned int* ctr = p.arrivals + (int64_t)seq * p.num_kv_heads * p.head_groups + cta_group;
+  unsigned int* ctr = p.arrivals + (int64_t)seq * p.num_kv_heads * p.head_groups + sg.y;
   if (threadIdx.x == 0) last = atomicAdd(ctr, 1u) == (unsigned)(active - 1);
   __syncthreads();
   if (!last) return;
   __threadfence();
   // merge weights: wts[s * nh + h] = 2^(m_s - M_h); wts[active * nh + h] = v_scale / L_h
   for (int h = threadIdx.x; h < nh; h += blockDim.x) {
-    const int64_t base = ((int64_t)seq * p.num_heads + h0 + h) * S;
     float M = -INFINITY;
-    for (int s = 0; s < active; ++s) M = fmaxf(M, __ldcg(p.part_ml + (base + s) * 2));
+    for (int s = 0; s < active; ++s) M = fmaxf(M, __ldcg(p.part_ml + part_row(p, sg, h0, s, h) * 2));
     const float mb = M == -INFINITY ? 0.0f : M;
     float L = 0.0f;
     for (int s = 0; s < active; ++s) {
-      const float w = exp2f(__ldcg(p.part_ml + (base + s) * 2) - mb);
+      const int64_t b = part_row(p, sg, h0, s, h);
+      const float w = exp2f(__ldcg(p.part_ml + b * 2) - mb);
       wts[s * nh + h] = w;
-      L = fmaf(w, __ldcg(p.part_ml + (base + s) * 2 + 1), L);
+      L = fmaf(w, __ldcg(p.part_ml + b * 2 + 1), L);
     }
     wts[active * nh + h] = vs / L;
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
     const int h = idx / D, d = idx - h * D;
-    const int64_t base = ((int64_t)seq * p.num_heads + h0 + h) * S;
     float O = 0.0f;
 #pragma unroll 4
-    for (int s = 0; s < active; ++s) O = fmaf(wts[s * nh + h], __ldcg(p.part_acc + (base + s) * D + d), O);
+    for (int s = 0; s < active; ++s)
+      O = fmaf(wts[s * nh + h], __ldcg(p.part_acc + part_row(p, sg, h0, s, h) * D + d), O);
     op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O * wts[active * nh + h]);
   }
   if (threadIdx.x == 0) *ctr = 0u;
@@ -239,16 +455,17 @@ paged_decode_generic_kernel(const DecodeParams p) {
   int* bt_s = reinterpret_cast<int*>(valid + 2 * kGenTile);        // [kMaxBtSmem]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y / p.head_groups;
-  const int hg = blockIdx.y - kvh * p.head_groups;
-  const int seq = blockIdx.z;
+  __shared__ SchedState sched;
+  sched_init<kGenTile>(p, sched);
+  while (sched_next<kGenTile>(p, sched)) {
+  const TokRange rng{sched.cur.begin, sched.cur.end};
+  const int seq = sched.cur.seq;
+  const int kvh = sched.cur.y / p.head_groups;
+  const int hg = sched.cur.y - kvh * p.head_groups;
   const int h0 = kvh * p.group + hg * p.heads_per_cta;
   const int nh = min(p.heads_per_cta, p.group - hg * p.heads_per_cta);
   const bool count_invalid = (kvh == 0 && hg == 0);
 
-  const SplitRange rng = split_range(p, seq, split);
-  if (split > 0 && rng.begin >= rng.end) return;
   const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
 
   const float ks = kFp8 ? __ldg(p.k_scale) : 1.0f;
@@ -376,7 +593,8 @@ paged_decode_generic_kernel(const DecodeParams p) {
   }
   __syncthreads();
   float* wts = o_s + kMaxHeadsPerCta * D;
-  finish_cta<QT>(p, seq, blockIdx.y, h0, nh, split, rng.active, o_s, D, m_s, l_s, wts);
+  finish_cta<QT>(p, sched.cur, h0, nh, o_s, D, m_s, l_s, wts);
+  }
 }
 
 size_t generic_smem_bytes(int head_dim, int elem_bytes) {
@@ -454,16 +672,17 @@ paged_decode_tc_kernel(const DecodeParams p) {
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
-  const int split = blockIdx.x;
-  const int kvh = blockIdx.y / p.head_groups;
-  const int hgrp = blockIdx.y - kvh * p.head_groups;
-  const int seq = blockIdx.z;
+  __shared__ SchedState sched;
+  sched_init<kTcTile>(p, sched);
+  while (sched_next<kTcTile>(p, sched)) {
+  const TokRange rng{sched.cur.begin, sched.cur.end};
+  const int seq = sched.cur.seq;
+  const int kvh = sched.cur.y / p.head_groups;
+  const int hgrp = sched.cur.y - kvh * p.head_groups;
   const int h0 = kvh * p.group + hgrp * p.heads_per_cta;
   const int nh = min(p.heads_per_cta, p.group - hgrp * p.heads_per_cta);
   const bool count_invalid = (kvh == 0 && hgrp == 0);
 
-  const SplitRange rng = split_range(p, seq, split);
-  if (split > 0 && rng.begin >= rng.end) return;
   const int ntiles = (rng.end - rng.begin + kTcTile - 1) / kTcTile;  // 0 when empty
   const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
   __syncthreads();
@@ -765,7 +984,384 @@ paged_decode_tc_kernel(const DecodeParams p) {
     red_acc[h * RP + d] = O;  // in place: this thread alone reads and writes (h, d)
   }
   __syncthreads();
-  finish_cta<QT>(p, seq, blockIdx.y, h0, nh, split, rng.active, red_acc, RP, m_s, l_s, wts);
+  finish_cta<QT>(p, sched.cur, h0, nh, red_acc, RP, m_s, l_s, wts);
+  }
+}
+
+// ============================================================ FP8 tensor-core kernel
+// head_dim = 128, e4m3 pages, bf16/f16 query. Both products run as FP8 MMAs
+// (mma.m16n8k32.e4m3, fp32 accumulate), so pages are never converted:
+//   * S^T = K Q^T: K's A fragments come straight out of ldmatrix; the query is split
+//     into e4m3 hi + lo parts (q ~ hi + lo to ~8 significant bits) and both are applied;
+//   * O^T = V^T P^T: V^T's A fragments are assembled from ldmatrix.trans words with one
+//     byte permute each, using a token permutation that P^T's fragments share;
+//     P is split into e4m3 hi + lo parts from f16. P is taken relative to the tile's
+//     own maximum (x 256), so small probabilities keep their precision: a warp keeps
+//     its accumulators relative to a per-head reference that follows the tile maxima
+//     (never more than 2^24 below the running maximum) and rescales them when it moves.
+// Each warp handles 32 tokens of a 128-token stage (two 16-token M tiles for S^T, one
+// k32 step for PV).
+__device__ __forceinline__ void mma_e4m3(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// f16x2 (x = low half) -> two e4m3 bytes (low byte from x), round to nearest even.
+__device__ __forceinline__ uint32_t f16x2_to_e4m3x2(uint32_t h) {
+  __half2_raw r;
+  r.x = (unsigned short)(h & 0xffffu);
+  r.y = (unsigned short)(h >> 16);
+  return (uint32_t)__nv_cvt_halfraw2_to_fp8x2(r, __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  const __half2 d = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&d);
+}
+
+// Four floats -> e4m3 hi bytes and e4m3 bytes of the residual x - hi (byte i = x[i]).
+__device__ __forceinline__ void split_e4m3x4(const float (&x)[4], uint32_t& hi, uint32_t& lo) {
+  hi = lo = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint8_t h = f32_to_e4m3(x[i]);
+    __nv_fp8_e4m3 hv;
+    hv.__x = h;
+    const uint8_t l = f32_to_e4m3(x[i] - to_f32(hv));
+    hi |= (uint32_t)h << (8 * i);
+    lo |= (uint32_t)l << (8 * i);
+  }
+}
+
+constexpr int kF8Tile = 128;  // tokens per stage: 4 warps x 32
+
+template <int NT>
+constexpr size_t f8_epilogue_bytes() { return tc_epilogue_bytes<NT>(); }
+template <int NT, int STAGES>
+constexpr size_t f8_front_bytes() {
+  constexpr size_t ring = (size_t)STAGES * 2 * kF8Tile * kTcD;
+  return ring > f8_epilogue_bytes<NT>() ? ring : f8_epilogue_bytes<NT>();
+}
+template <int NT, int STAGES>
+constexpr size_t f8_smem_bytes() {
+  return f8_front_bytes<NT, STAGES>() + (size_t)STAGES * kF8Tile + kMaxBtSmem * 4;
+}
+
+template <typename QT, int NT, int STAGES, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
+paged_decode_fp8mma_kernel(const DecodeParams p) {
+  constexpr int D = kTcD;
+  constexpr int ROWB = D;         // bytes per e4m3 token row
+  constexpr int CPR = ROWB / 16;  // 8 chunks per row
+  constexpr int TILE_BYTES = kF8Tile * ROWB;
+  constexpr int STAGE_BYTES = 2 * TILE_BYTES;
+  constexpr int ROWS_PER_PASS = kThreads / CPR;  // 16
+  constexpr int PASSES = kF8Tile / ROWS_PER_PASS;  // 8
+  constexpr size_t FRONT = f8_front_bytes<NT, STAGES>();
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* valid = smem + FRONT;                                  // [STAGES][kF8Tile]
+  int* bt_s = reinterpret_cast<int*>(valid + STAGES * kF8Tile);   // [kMaxBtSmem]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  __shared__ SchedState sched;
+  sched_init<kF8Tile>(p, sched);
+  while (sched_next<kF8Tile>(p, sched)) {
+  const TokRange rng{sched.cur.begin, sched.cur.end};
+  const int seq = sched.cur.seq;
+  const int kvh = sched.cur.y / p.head_groups;
+  const int hgrp = sched.cur.y - kvh * p.head_groups;
+  const int h0 = kvh * p.group + hgrp * p.heads_per_cta;
+  const int nh = min(p.heads_per_cta, p.group - hgrp * p.heads_per_cta);
+  const bool count_invalid = (kvh == 0 && hgrp == 0);
+
+  const int ntiles = (rng.end - rng.begin + kF8Tile - 1) / kF8Tile;
+  const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
+  __syncthreads();
+
+  const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
+  const int64_t head_off = (int64_t)kvh * ROWB;
+  const int ld_c = tid % CPR;
+  const int ld_r0 = tid / CPR;
+  const bool one_page_per_tile = p.bs_shift >= 7;  // power-of-two block_size >= 128
+  auto load_tile = [&](int it) {
+    const int stage = it % STAGES;
+    const int t0 = rng.begin + it * kF8Tile;
+    uint8_t* kd = smem + stage * STAGE_BYTES;
+    uint8_t* vd = kd + TILE_BYTES;
+    int tile_page = -1, tile_off = 0;
+    if (one_page_per_tile) {
+      tile_page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
+      tile_off = t0 & ((1 << p.bs_shift) - 1);
+    }
+#pragma unroll
+    for (int i = 0; i < PASSES; ++i) {
+      const int r = ld_r0 + i * ROWS_PER_PASS;
+      const int t = t0 + r;
+      int page = -1, boff = 0;
+      if (t < rng.end) {
+        if (one_page_per_tile) {
+          page = tile_page;
+          boff = tile_off + r;
+        } else {
+          int blk;
+          split_token(p, t, blk, boff);
+          page = slice_page(p, seq, slice, bt_s, blk);
+        }
+      }
+      const bool ok = page >= 0;
+      const int64_t off =
+          ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
+      const int soff = r * ROWB + ((ld_c ^ (r & 7)) << 4);
+      cp_async_16(smem_u32(kd + soff), p.k_cache + off, ok ? 16 : 0);
+      cp_async_16(smem_u32(vd + soff), p.v_cache + off, ok ? 16 : 0);
+      if (ld_c == 0) valid[stage * kF8Tile + r] = ok ? 1 : 0;
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < ntiles) load_tile(s);
+    cp_async_commit();
+  }
+
+  // ---- query as e4m3 hi + lo B fragments: b0 = d 32kq + 4tig + i, b1 = d 32kq + 16 + 4tig + i
+  const QT* qp = reinterpret_cast<const QT*>(p.q);
+  auto qval = [&](int row, int d) -> float {
+    return row < nh ? to_f32(qp[(int64_t)seq * p.q_sb + (int64_t)(h0 + row) * p.q_sh + d]) : 0.0f;
+  };
+  float qmax = 0.0f;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int kq = 0; kq < D / 32; ++kq)
+#pragma unroll
+      for (int half = 0; half < 2; ++half)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          qmax = fmaxf(qmax, fabsf(qval(nt * 8 + g, 32 * kq + 16 * half + 4 * tig + i)));
+  qmax = warp_max(qmax);
+  float qs = 1.0f;  // power of two: max |q| * qs in [128, 256), inside e4m3's range
+  if (qmax > 0.0f && isfinite(qmax)) {
+    int ex;
+    frexpf(qmax, &ex);
+    qs = ldexpf(1.0f, 8 - ex);
+  }
+  uint32_t qh[NT][D / 32][2], ql[NT][D / 32][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int kq = 0; kq < D / 32; ++kq)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = qval(nt * 8 + g, 32 * kq + 16 * half + 4 * tig + i) * qs;
+        split_e4m3x4(x, qh[nt][kq][half], ql[nt][kq][half]);
+      }
+  const float sc = p.qk_scale_log2 * __ldg(p.k_scale) / qs;
+
+  // per-warp state for heads nt*8 + 2tig + e: running max, accumulator reference, l
+  float m_run[NT][2], q_ref[NT][2], l_run[NT][2];
+  float o[NT][D / 16][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    m_run[nt][0] = m_run[nt][1] = -INFINITY;
+    q_ref[nt][0] = q_ref[nt][1] = -INFINITY;
+    l_run[nt][0] = l_run[nt][1] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.0f;
+  }
+
+  const int lrow = lane & 7;
+  const int lmat = lane >> 3;
+  for (int it = 0; it < ntiles; ++it) {
+    cp_async_wait<STAGES - 2>();
+    __syncthreads();
+    if (it + STAGES - 1 < ntiles) load_tile(it + STAGES - 1);
+    cp_async_commit();
+
+    const int stage = it % STAGES;
+    const uint32_t kbase = smem_u32(smem + stage * STAGE_BYTES);
+    const uint32_t vbase = kbase + TILE_BYTES;
+    const uint8_t* vld = valid + stage * kF8Tile;
+
+    // ---- S^T for the warp's two 16-token M tiles (independent chains); the hi and lo
+    // query parts accumulate into the same registers
+    float s[NT][2][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s[nt][mt][i] = 0.0f;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      // matrices: (tokens 0-7, chunk 2kq) (tokens 8-15, 2kq) (0-7, 2kq+1) (8-15, 2kq+1)
+      const int r = warp * 32 + mt * 16 + ((lmat & 1) << 3) + lrow;
+#pragma unroll
+      for (int kq = 0; kq < D / 32; ++kq) {
+        const int lc = 2 * kq + (lmat >> 1);
+        uint32_t a[4];
+        ldmatrix_x4(kbase + r * ROWB + ((lc ^ lrow) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_e4m3(s[nt][mt], a, qh[nt][kq][0], qh[nt][kq][1]);
+          mma_e4m3(s[nt][mt], a, ql[nt][kq][0], ql[nt][kq][1]);
+        }
+      }
+    }
+
+    // ---- softmax update and P^T (e4m3 hi + lo) B fragments
+    bool vt[2][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      vt[mt][0] = vld[warp * 32 + mt * 16 + g] != 0;
+      vt[mt][1] = vld[warp * 32 + mt * 16 + g + 8] != 0;
+    }
+    uint32_t ph[NT][2], pl[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float x[2][4];  // [mt][e + 2r], r = token g / g+8
+      float f[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int i = e + 2 * rr;
+            const float v = vt[mt][rr] ? s[nt][mt][i] * sc : -INFINITY;
+            x[mt][i] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[nt][e], mx);
+        const float q_new = mx == -INFINITY ? q_ref[nt][e] : fmaxf(mx, m_new - 24.0f);
+        f[e] = q_ref[nt][e] == -INFINITY ? 1.0f : exp2f(q_ref[nt][e] - q_new);
+        m_run[nt][e] = m_new;
+        q_ref[nt][e] = q_new;
+        float lsum = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int rr = 0; rr < 2; ++rr) {
+            const int i = e + 2 * rr;
+            const float pv = x[mt][i] == -INFINITY ? 0.0f : exp2f(x[mt][i] - q_new + 8.0f);
+            x[mt][i] = pv;
+            lsum += pv;
+          }
+        l_run[nt][e] = fmaf(l_run[nt][e], f[e], lsum);
+      }
+      if (f[0] != 1.0f || f[1] != 1.0f) {
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+          o[nt][j][0] *= f[0];
+          o[nt][j][1] *= f[1];
+          o[nt][j][2] *= f[0];
+          o[nt][j][3] *= f[1];
+        }
+      }
+      // P^T fragments: movmatrix gives (head g; tokens 2tig, 2tig+1) and (head g; tokens
+      // 8+2tig, 9+2tig) of an M tile; their bytes are the k order of the V^T fragments
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        const uint32_t x0 = movmatrix_trans(pack2<f16>(x[mt][0], x[mt][1]));
+        const uint32_t x1 = movmatrix_trans(pack2<f16>(x[mt][2], x[mt][3]));
+        const uint32_t h0 = f16x2_to_e4m3x2(x0), h1 = f16x2_to_e4m3x2(x1);
+        const uint32_t l0 = f16x2_to_e4m3x2(hsub2_u32(x0, e4m3x2_to_f16x2((uint16_t)h0)));
+        const uint32_t l1 = f16x2_to_e4m3x2(hsub2_u32(x1, e4m3x2_to_f16x2((uint16_t)h1)));
+        ph[nt][mt] = h0 | (h1 << 16);
+        pl[nt][mt] = l0 | (l1 << 16);
+      }
+    }
+
+    // ---- O^T += V^T P^T over the warp's 32 tokens, one 16-row head_dim chunk per MMA pair
+    {
+      const int r = warp * 32 + lmat * 8 + lrow;  // matrices: token groups 0-7 .. 24-31
+#pragma unroll
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t x[4];
+        ldmatrix_x4_trans(vbase + r * ROWB + ((c ^ lrow) << 4), x[0], x[1], x[2], x[3]);
+        // x[j]: tokens (8j + 2tig, 8j + 2tig + 1) x d (16c + 2g, 16c + 2g + 1)
+        uint32_t a[4];
+        a[0] = __byte_perm(x[0], x[1], 0x6420);  // d even, tokens 2tig,2tig+1,8+2tig,9+2tig
+        a[1] = __byte_perm(x[0], x[1], 0x7531);  // d odd
+        a[2] = __byte_perm(x[2], x[3], 0x6420);  // same for tokens 16-31
+        a[3] = __byte_perm(x[2], x[3], 0x7531);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_e4m3(o[nt][c], a, ph[nt][0], ph[nt][1]);
+          mma_e4m3(o[nt][c], a, pl[nt][0], pl[nt][1]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- merge the 4 warps (reference q_ref plays the role of m; the x256 cancels)
+  constexpr int RP = D + 4;
+  constexpr int HC = 8 * NT;
+  float* red_acc = reinterpret_cast<float*>(smem);
+  float* red_m = red_acc + 4 * HC * RP;
+  float* red_l = red_m + 4 * HC;
+  float* m_s = red_l + 4 * HC;
+  float* l_s = m_s + HC;
+  float* wts = l_s + HC;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float l = l_run[nt][e];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      const int head = nt * 8 + 2 * tig + e;
+      float* ra = red_acc + (warp * HC + head) * RP;
+#pragma unroll
+      for (int j = 0; j < D / 16; ++j) {
+        ra[16 * j + 2 * g] = o[nt][j][e];
+        ra[16 * j + 2 * g + 1] = o[nt][j][e + 2];
+      }
+      if (g == 0) {
+        red_m[warp * HC + head] = q_ref[nt][e];
+        red_l[warp * HC + head] = l;
+      }
+    }
+  __syncthreads();
+  if (tid < nh) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red_m[w * HC + tid]);
+    const float base = M == -INFINITY ? 0.0f : M;
+    float L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) L = fmaf(exp2f(red_m[w * HC + tid] - base), red_l[w * HC + tid], L);
+    m_s[tid] = M;
+    l_s[tid] = L;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < nh * D; idx += kThreads) {
+    const int h = idx / D, d = idx - h * D;
+    const float base = m_s[h] == -INFINITY ? 0.0f : m_s[h];
+    float O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+      O = fmaf(exp2f(red_m[w * HC + h] - base), red_acc[(w * HC + h) * RP + d], O);
+    red_acc[h * RP + d] = O;
+  }
+  __syncthreads();
+  finish_cta<QT>(p, sched.cur, h0, nh, red_acc, RP, m_s, l_s, wts);
+  }
 }
 
 // ============================================================ host side
@@ -776,9 +1372,10 @@ struct SplitPlan {
 
 inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
-// Shapes only: the number of CTAs per (seq, kv head) is sized so the grid covers
-// several waves of the 148 SMs at two resident CTAs each, with chunks of at most 1024
-// tokens (balanced work for ragged batches) and at least 128 tokens.
+// Fixed split plan, shapes only (used for a forced num_splits and when the balanced
+// schedule's arithmetic bound fails): the number of CTAs per (seq, kv head) is sized so
+// the grid covers several waves of the 148 SMs at two resident CTAs each, with chunks of
+// at most 1024 tokens and at least 128 tokens.
 SplitPlan plan_splits(int num_seqs, int num_kv_heads, int head_groups, int block_size,
                       int max_blocks, int forced) {
   SplitPlan sp;
@@ -810,17 +1407,45 @@ SplitPlan plan_splits(int num_seqs, int num_kv_heads, int head_groups, int block
 
 int head_groups_for(int group) { return (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta; }
 
+// Balanced schedule bounds: at most kMaxResident CTAs (B200: 148 SMs x 4), each with at
+// least kMinCtaTokens tokens of work.
+constexpr int kMaxResident = kNumSMs * 4;
+constexpr int kMinCtaTokens = 256;
+
+// The balanced schedule serves num_splits = 0 unless its work-item arithmetic
+// (W * G < 2^62 with W <= units * (cap / 32 + 1)) could overflow.
+bool use_balanced(int num_seqs, int num_kv_heads, int head_groups, int block_size,
+                  int max_blocks, int num_splits) {
+  if (num_splits != 0) return false;
+  const double units = (double)num_seqs * num_kv_heads * head_groups;
+  const double items = units * ((double)max_blocks * block_size / 32.0 + 1.0);
+  return items * kMaxResident < 4.0e18;
+}
+
+// Work items per CTA at least: enough tokens to amortise a pipeline fill, and few enough
+// CTAs per unit that a unit has at most kMaxSplits partials (the merge-weight buffer).
+int min_tiles_for(int tile, int block_size, int max_blocks) {
+  const int64_t cap_tiles = ((int64_t)max_blocks * block_size + tile - 1) / tile;
+  const int64_t by_merge = (cap_tiles + kMaxSplits - 3) / (kMaxSplits - 2);
+  const int64_t by_fill = (kMinCtaTokens + tile - 1) / tile;
+  return (int)(by_merge > by_fill ? by_merge : by_fill);
+}
+
 // Workspace layout (each part 256-byte aligned): partial accumulators, partial (m, l),
-// arrival counters.
+// arrival counters. Fixed splits: one partial per (sequence, head, split). Balanced:
+// 2 * kMaxResident slots of heads_per_cta partials.
 struct WorkspaceLayout {
   size_t acc, ml, ctr, total;
 };
 WorkspaceLayout workspace_layout(int num_seqs, int num_heads, int num_kv_heads, int head_dim,
-                                 int num_splits) {
+                                 int num_splits, bool balanced) {
   WorkspaceLayout w{0, 0, 0, 0};
-  if (num_splits <= 1) return w;
-  const size_t n = (size_t)num_seqs * num_heads * num_splits;
-  const size_t groups = (size_t)num_seqs * num_kv_heads * head_groups_for(num_heads / num_kv_heads);
+  if (!balanced && num_splits <= 1) return w;
+  const int group = num_heads / num_kv_heads;
+  const int hpc = group < kMaxHeadsPerCta ? group : kMaxHeadsPerCta;
+  const size_t n = balanced ? (size_t)2 * kMaxResident * hpc
+                            : (size_t)num_seqs * num_heads * num_splits;
+  const size_t groups = (size_t)num_seqs * num_kv_heads * head_groups_for(group);
   w.acc = 0;
   w.ml = round_up((int64_t)(n * head_dim * sizeof(float)), 256);
   w.ctr = w.ml + round_up((int64_t)(n * 2 * sizeof(float)), 256);
@@ -842,15 +1467,65 @@ int ensure_smem(size_t bytes, int device) {
   return MKV_OK;
 }
 
+// Resident CTAs of Kernel at `smem` bytes on `device` (occupancy x SMs), cached per device.
+constexpr int kMaxDevices = 64;
+template <auto Kernel>
+int resident_ctas(size_t smem, int device, int* out) {
+  static std::mutex mu;
+  static size_t key[kMaxDevices];
+  static int val[kMaxDevices];
+  const bool cacheable = device >= 0 && device < kMaxDevices;
+  if (cacheable) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (val[device] > 0 && key[device] == smem) {
+      *out = val[device];
+      return MKV_OK;
+    }
+  }
+  int occ = 0, sms = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, Kernel, kThreads, smem);
+  if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute(SM count)");
+  int g = occ * sms;
+  if (g > kMaxResident) g = kMaxResident;
+  if (g < 1) g = 1;
+  if (cacheable) {
+    std::lock_guard<std::mutex> lock(mu);
+    key[device] = smem;
+    val[device] = g;
+  }
+  *out = g;
+  return MKV_OK;
+}
+
+// Grid of the launch: (splits, units per sequence, sequences) for fixed splits, or the
+// resident CTAs of the kernel for the balanced schedule (which also fills p's fields).
+template <auto Kernel>
+int launch_decode(DecodeParams p, int tile, size_t smem, cudaStream_t stream, int device,
+                  const char* what) {
+  dim3 grid(p.num_splits, p.num_kv_heads * p.head_groups, p.num_seqs);
+  if (p.balanced) {
+    int g = 0;
+    int st = resident_ctas<Kernel>(smem, device, &g);
+    if (st != MKV_OK) return st;
+    p.sched_ctas = g;
+    p.min_tiles = min_tiles_for(tile, p.block_size, p.max_blocks);
+    grid = dim3(g, 1, 1);
+  }
+  Kernel<<<grid, kThreads, smem, stream>>>(p);
+  return cuda_status(cudaGetLastError(), what);
+}
+
 template <typename QT, typename CT>
-int launch_generic(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
+int launch_generic(const DecodeParams& p, cudaStream_t stream, int device) {
   const size_t smem = generic_smem_bytes(p.head_dim, sizeof(CT));
   // opt in once to the largest size this instantiation can use (head_dim 256)
   int st = ensure_smem<paged_decode_generic_kernel<QT, CT>>(generic_smem_bytes(256, sizeof(CT)),
                                                             device);
   if (st != MKV_OK) return st;
-  paged_decode_generic_kernel<QT, CT><<<grid, kThreads, smem, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "paged_decode_generic launch");
+  return launch_decode<paged_decode_generic_kernel<QT, CT>>(p, kGenTile, smem, stream, device,
+                                                            "paged_decode_generic launch");
 }
 
 // Pipeline depth and CTAs per SM: 16-bit pages 2 stages x 32 KB (3 CTAs/SM), e4m3
@@ -871,19 +1546,39 @@ template <> struct TcConfig<f16> { static constexpr int kStages = MKV_TC16_STAGE
 template <> struct TcConfig<fp8> { static constexpr int kStages = MKV_TC8_STAGES, kMinBlocks = MKV_TC8_MINB; };
 
 template <typename QT, typename CT, int NT>
-int launch_tc_nt(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
+int launch_tc_nt(const DecodeParams& p, cudaStream_t stream, int device) {
   constexpr int S = TcConfig<CT>::kStages, MB = TcConfig<CT>::kMinBlocks;
   constexpr size_t smem = tc_smem_bytes<CT, NT, S>();
   int st = ensure_smem<paged_decode_tc_kernel<QT, CT, NT, S, MB>>(smem, device);
   if (st != MKV_OK) return st;
-  paged_decode_tc_kernel<QT, CT, NT, S, MB><<<grid, kThreads, smem, stream>>>(p);
-  return cuda_status(cudaGetLastError(), "paged_decode_tc launch");
+  return launch_decode<paged_decode_tc_kernel<QT, CT, NT, S, MB>>(p, kTcTile, smem, stream, device,
+                                                                  "paged_decode_tc launch");
+}
+
+// e4m3 pages with FP8 MMAs: 2 stages x 32 KB (128-token tiles), 3 CTAs/SM.
+#ifndef MKV_F8_STAGES
+#define MKV_F8_STAGES 2
+#define MKV_F8_MINB 3
+#endif
+template <typename QT, int NT>
+int launch_fp8mma_nt(const DecodeParams& p, cudaStream_t stream, int device) {
+  constexpr int S = MKV_F8_STAGES, MB = MKV_F8_MINB;
+  constexpr size_t smem = f8_smem_bytes<NT, S>();
+  int st = ensure_smem<paged_decode_fp8mma_kernel<QT, NT, S, MB>>(smem, device);
+  if (st != MKV_OK) return st;
+  return launch_decode<paged_decode_fp8mma_kernel<QT, NT, S, MB>>(
+      p, kF8Tile, smem, stream, device, "paged_decode_fp8mma launch");
+}
+template <typename QT>
+int launch_fp8mma(const DecodeParams& p, cudaStream_t stream, int device) {
+  return p.heads_per_cta > 8 ? launch_fp8mma_nt<QT, 2>(p, stream, device)
+                             : launch_fp8mma_nt<QT, 1>(p, stream, device);
 }
 
 template <typename QT, typename CT>
-int launch_tc(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
-  return p.heads_per_cta > 8 ? launch_tc_nt<QT, CT, 2>(p, grid, stream, device)
-                             : launch_tc_nt<QT, CT, 1>(p, grid, stream, device);
+int launch_tc(const DecodeParams& p, cudaStream_t stream, int device) {
+  return p.heads_per_cta > 8 ? launch_tc_nt<QT, CT, 2>(p, stream, device)
+                             : launch_tc_nt<QT, CT, 1>(p, stream, device);
 }
 
 int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, int q_dtype,
@@ -938,8 +1633,11 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   const int hgs = head_groups_for(group);
   if ((int64_t)num_kv_heads * hgs > 65535)
     return set_error(MKV_ERR_UNSUPPORTED, "%s: too many kv heads", fn);
+  const bool balanced =
+      use_balanced(num_seqs, num_kv_heads, hgs, block_size, max_blocks, num_splits);
   const SplitPlan sp = plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_blocks, num_splits);
-  const WorkspaceLayout wl = workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits);
+  const WorkspaceLayout wl =
+      workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits, balanced);
   if (wl.total > 0 && (workspace == nullptr || ws_bytes < wl.total))
     return set_error(MKV_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn,
                      wl.total, workspace ? ws_bytes : (size_t)0);
@@ -976,6 +1674,9 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.o_sh = o_sh;
   p.num_splits = sp.num_splits;
   p.chunk = sp.chunk;
+  p.balanced = balanced ? 1 : 0;
+  p.sched_ctas = 0;  // set at launch from the kernel's occupancy
+  p.min_tiles = 1;
   uint8_t* ws = (uint8_t*)workspace;
   p.part_acc = wl.total ? (float*)(ws + wl.acc) : nullptr;
   p.part_ml = wl.total ? (float*)(ws + wl.ml) : nullptr;
@@ -990,24 +1691,45 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
     e = cudaMemsetAsync(ws + wl.ctr, 0, wl.total - wl.ctr, s);
     if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(arrival counters)");
   }
-  dim3 grid(sp.num_splits, num_kv_heads * hgs, num_seqs);
+
+  // The tcgen05 kernel (compiled in with MKV_ENABLE_TC05) runs fixed split plans only.
+  if (!balanced && tc05::supported(q_dtype, cache_dtype, head_dim, block_size, hpc)) {
+    tc05::Params t;
+    t.q = query; t.q_sb = q_sb; t.q_sh = q_sh;
+    t.num_blocks = num_blocks; t.block_size = block_size; t.bs_shift = p.bs_shift;
+    t.bt = bt; t.bt_sb = bt_sb; t.max_blocks = max_blocks; t.bt_i64 = p.bt_i64;
+    t.ctx = ctx; t.ctx_i64 = p.ctx_i64;
+    t.num_seqs = num_seqs; t.num_heads = num_heads; t.num_kv_heads = num_kv_heads;
+    t.group = group; t.heads_per_cta = hpc; t.head_groups = hgs;
+    t.qk_scale_log2 = p.qk_scale_log2; t.k_scale = p.k_scale; t.v_scale = p.v_scale;
+    t.out = out; t.o_sb = o_sb; t.o_sh = o_sh;
+    t.part_acc = p.part_acc; t.part_ml = p.part_ml; t.arrivals = p.arrivals;
+    t.num_splits = sp.num_splits; t.chunk = sp.chunk;
+    t.num_units = (int64_t)num_seqs * num_kv_heads * hgs * sp.num_splits;
+    t.invalid = invalid;
+    return tc05::launch(t, q_dtype, cache_dtype, k_cache, v_cache, s, device);
+  }
 
   const bool tc_ok = head_dim == kTcD && q_dtype != MKV_DTYPE_F32;
-  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, bf16>(p, grid, s, device);
-  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, f16>(p, grid, s, device);
-  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, fp8>(p, grid, s, device);
-  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, fp8>(p, grid, s, device);
+  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, bf16>(p, s, device);
+  if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, f16>(p, s, device);
+#ifdef MKV_FP8_CONVERT_PATH
+  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, fp8>(p, s, device);
+  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, fp8>(p, s, device);
+#endif
+  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_fp8mma<bf16>(p, s, device);
+  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_fp8mma<f16>(p, s, device);
   if (fp8_cache) {
     switch (q_dtype) {
-      case MKV_DTYPE_F32: return launch_generic<float, fp8>(p, grid, s, device);
-      case MKV_DTYPE_F16: return launch_generic<f16, fp8>(p, grid, s, device);
-      default: return launch_generic<bf16, fp8>(p, grid, s, device);
+      case MKV_DTYPE_F32: return launch_generic<float, fp8>(p, s, device);
+      case MKV_DTYPE_F16: return launch_generic<f16, fp8>(p, s, device);
+      default: return launch_generic<bf16, fp8>(p, s, device);
     }
   }
   switch (q_dtype) {
-    case MKV_DTYPE_F32: return launch_generic<float, float>(p, grid, s, device);
-    case MKV_DTYPE_F16: return launch_generic<f16, f16>(p, grid, s, device);
-    default: return launch_generic<bf16, bf16>(p, grid, s, device);
+    case MKV_DTYPE_F32: return launch_generic<float, float>(p, s, device);
+    case MKV_DTYPE_F16: return launch_generic<f16, f16>(p, s, device);
+    default: return launch_generic<bf16, bf16>(p, s, device);
   }
 }
 
@@ -1018,7 +1740,6 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
 // device below and passed to the kernels like any caller workspace.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MKV_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
 
@@ -1049,6 +1770,7 @@ extern "C" int32_t mkv_paged_decode_num_splits(int32_t num_seqs, int32_t num_hea
   (void)head_dim;
   if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads != 0) return 1;
   const int hgs = head_groups_for(num_heads / num_kv_heads);
+  if (use_balanced(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, 0)) return 0;
   return plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, 0).num_splits;
 }
 
@@ -1062,7 +1784,10 @@ extern "C" size_t mkv_paged_decode_workspace_bytes(int32_t num_seqs, int32_t num
   const int hgs = head_groups_for(num_heads / num_kv_heads);
   const SplitPlan sp =
       plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, num_splits);
-  return workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits).total;
+  const bool balanced =
+      use_balanced(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, num_splits);
+  return workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits, balanced)
+      .total;
 }
 
 extern "C" int mkv_paged_decode(const void* query, int64_t q_stride_seq, int64_t q_stride_head,

@@ -47,27 +47,47 @@ def test_version_and_status_strings():
 
 
 @pytest.mark.parametrize("B,H,KVH,BS,MAXB,expect", [
-    (256, 32, 8, 256, 32, 8),     # config 3: 1024-token chunks of an 8192-token table
-    (64, 32, 8, 256, 128, 32),    # config 4: 32768 tokens
-    (4, 16, 8, 16, 32, 4),        # config 1: small batch -> 128-token chunks
-    (256, 4, 1, 256, 32, 16),     # config 3 on one of 8 ranks (1 KV head): 512-token chunks
-    (8, 8, 8, 16, 1, 1),          # table fits one chunk -> no split
+    (256, 32, 8, 256, 32, 0),     # config 3: balanced schedule (0 = chosen on the device)
+    (64, 32, 8, 256, 128, 0),     # config 4
+    (4, 16, 8, 16, 32, 0),        # config 1
+    (1, 8, 8, 16, 1, 0),          # tiny
+    (65535, 65535, 65535, 256, 1 << 22, 128),  # work-item bound exceeded: fixed plan
 ])
 def test_split_plan(B, H, KVH, BS, MAXB, expect):
     lib = lib_mod.load()
     assert lib.mkv_paged_decode_num_splits(B, H, KVH, 128, BS, MAXB) == expect
 
 
-def test_workspace_bytes():
+RESIDENT = 148 * 4  # balanced schedule: at most 4 CTAs per SM on 148 SMs
+
+
+def test_workspace_bytes_balanced():
+    """Auto (num_splits = 0): 2 partial slots per resident CTA, heads_per_cta heads each,
+    plus one arrival counter per (seq, kv head)."""
+    lib = lib_mod.load()
+    n = 2 * RESIDENT * 4                   # slots x heads per CTA (group of 4)
+    acc = (n * 128 * 4 + 255) // 256 * 256
+    ml = (n * 8 + 255) // 256 * 256
+    ctr = (256 * 8 * 4 + 255) // 256 * 256
+    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 0) == acc + ml + ctr
+    # independent of the context length: the same bound serves any table width
+    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 4096, 0) == acc + ml + ctr
+    # group of 32 query heads -> two head groups of 16
+    n16 = 2 * RESIDENT * 16
+    ctr16 = (4 * 2 * 2 * 4 + 255) // 256 * 256
+    assert lib.mkv_paged_decode_workspace_bytes(4, 64, 2, 128, 16, 8, 0) == \
+        (n16 * 128 * 4 + 255) // 256 * 256 + (n16 * 8 + 255) // 256 * 256 + ctr16
+
+
+def test_workspace_bytes_fixed_splits():
     lib = lib_mod.load()
     n = 256 * 32 * 8                      # (seq, head, split) partials
-    acc = (n * 128 * 4 + 255) // 256 * 256   # partial accumulators
-    ml = (n * 8 + 255) // 256 * 256          # partial (m, l)
-    ctr = (256 * 8 * 4 + 255) // 256 * 256   # one arrival counter per (seq, kv head)
-    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 0) == acc + ml + ctr
-    assert lib.mkv_paged_decode_workspace_bytes(8, 8, 8, 128, 16, 1, 0) == 0
-    # a forced split count overrides the plan
-    assert lib.mkv_paged_decode_workspace_bytes(2, 4, 2, 64, 16, 8, 4) > 0
+    acc = (n * 128 * 4 + 255) // 256 * 256
+    ml = (n * 8 + 255) // 256 * 256
+    ctr = (256 * 8 * 4 + 255) // 256 * 256
+    assert lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 8) == acc + ml + ctr
+    assert lib.mkv_paged_decode_workspace_bytes(8, 8, 8, 128, 16, 1, 1) == 0   # one split: none
+    assert lib.mkv_paged_decode_workspace_bytes(2, 4, 2, 64, 16, 64, 4) > 0
 
 
 def _decode_call(lib, **kw):
@@ -90,6 +110,7 @@ def _decode_call(lib, **kw):
     (dict(btt=7), 1, b"block_table_index_type"),
     (dict(k=(1 << 21) + 8), 1, b"16-byte aligned"),
     (dict(maxb=64, ns=0, B=512), 3, b"workspace"),
+    (dict(maxb=64, ns=8, B=512), 3, b"workspace"),
     (dict(q=None), 1, b"null pointer"),
     (dict(bs=0), 1, b"bad sizes"),
 ])

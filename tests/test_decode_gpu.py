@@ -258,3 +258,67 @@ def test_decode_step_in_cuda_graph():
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(static_out, eager)
+
+
+# ------------------------------------------------------------------ balanced schedule
+def _balanced_case(case, fp8):
+    g = torch.Generator().manual_seed(11)
+    if case == "one_long":        # one unit per kv head, each shared by ~80 CTAs
+        return wl.decode_workload(case, 1, 32, 8, 128, 16, [20000], fp8=fp8, seed=21, with_append=False)
+    if case == "many_ragged":     # 600 sequences, 10% empty, segments beyond the staged table
+        lens = torch.randint(0, 3000, (600,), generator=g)
+        lens[torch.rand(600, generator=g) < 0.1] = 0
+        return wl.decode_workload(case, 600, 32, 8, 128, 16, lens.tolist(), fp8=fp8, seed=22,
+                                  with_append=False)
+    if case == "wide_group":      # 32 query heads per kv head: two head groups per unit
+        return wl.decode_workload(case, 7, 64, 2, 128, 256, [9000, 1, 0, 4097, 128, 65, 30000],
+                                  fp8=fp8, seed=23, with_append=False)
+    # a table wide enough that the merge bound (128 partials per unit) sets the CTA share
+    return wl.decode_workload(case, 2, 8, 1, 128, 256, [100000, 3], fp8=fp8, seed=24, with_append=False)
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("case", ["one_long", "many_ragged", "wide_group", "very_long"])
+def test_balanced_schedule(case, fp8):
+    """The automatic (balanced, persistent) schedule against a float32 torch reference on
+    every sequence, and against the one-split plan over the whole batch."""
+    w = _balanced_case(case, fp8)
+    out = _decode_w(w)
+    torch.cuda.synchronize()
+    atol, rtol = TOL[torch.bfloat16]
+    lens = w.context_lens.tolist()
+    live = [b for b, n in enumerate(lens) if n > 0]
+    empty = [b for b, n in enumerate(lens) if n == 0]
+    assert torch.isnan(out[empty]).all() if empty else True
+    assert not torch.isnan(out[live]).any()
+    for i in range(0, len(live), 64):
+        seqs = live[i:i + 64]
+        assert torch.allclose(out[seqs].float(), torch_reference(w, seqs), atol=atol, rtol=rtol)
+    one = _decode_w(w, splits=1)
+    assert torch.allclose(one[live].float(), out[live].float(), atol=atol, rtol=rtol)
+    again = _decode_w(w)  # counters were left at zero: a second launch agrees bit for bit
+    assert torch.equal(torch.nan_to_num(again, nan=7.0), torch.nan_to_num(out, nan=7.0))
+
+
+def test_balanced_schedule_counts_invalid_pages_once():
+    """Out-of-range page entries are counted once per (sequence, entry) whatever the
+    schedule, here on segments longer than the staged block-table slice."""
+    lib = mkv_module("_lib").load()
+    w = wl.decode_workload("inv", 3, 8, 2, 128, 16, [4000, 2500, 700], seed=31, with_append=False)
+    w.block_tables[0, 5] = 10 ** 6
+    w.block_tables[0, 200] = -7
+    w.block_tables[1, 3] = 10 ** 6
+    for splits in (0, 1, 5):
+        cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+        out = torch.empty_like(w.query)
+        n = lib.mkv_paged_decode_workspace_bytes(3, 8, 2, 128, 16, w.block_tables.shape[1], splits)
+        ws = torch.empty(max(n, 1), dtype=torch.uint8, device="cuda")
+        st = lib.mkv_paged_decode(
+            w.query.data_ptr(), w.query.stride(0), w.query.stride(1), 2, w.k_cache.data_ptr(),
+            w.v_cache.data_ptr(), 2, w.k_cache.shape[0], 16, w.block_tables.data_ptr(), 0,
+            w.block_tables.stride(0), w.block_tables.shape[1], w.context_lens.data_ptr(), 1, 3, 8, 2,
+            128, w.scale, out.data_ptr(), out.stride(0), out.stride(1), ws.data_ptr(), n, splits,
+            cnt.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert st == 0, lib.mkv_last_error()
+        torch.cuda.synchronize()
+        assert int(cnt) == 3, (splits, int(cnt))

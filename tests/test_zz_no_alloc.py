@@ -90,14 +90,14 @@ def test_no_alloc_matches_workspace_entry_twice(dtype, splits):
 
 def test_no_alloc_rejects_shapes_beyond_its_scratch():
     lib = lib_mod.load()
-    # config-3 sized batch with the automatic split plan needs ~34 MB > 16 MiB
-    need = lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 0)
+    # config-3 sized batch with 8 fixed splits per sequence needs ~34 MB > 16 MiB
+    need = lib.mkv_paged_decode_workspace_bytes(256, 32, 8, 128, 256, 32, 8)
     assert need > lib_mod.NOALLOC_SCRATCH_BYTES
     dummy = torch.zeros(16, dtype=torch.bfloat16, device="cuda")
     p = dummy.data_ptr()
     st = lib.mkv_paged_decode_noalloc(p, 4096, 128, lib_mod.DTYPE_BF16, p, p, lib_mod.DTYPE_BF16, 1,
                                       256, p, lib_mod.INDEX_I32, 32, 32, p, lib_mod.INDEX_I64, 256, 32,
-                                      8, 128, 0.1, p, 4096, 128, 0, None,
+                                      8, 128, 0.1, p, 4096, 128, 8, None,
                                       torch.cuda.current_stream().cuda_stream)
     assert st == lib_mod.ERR_WORKSPACE
     assert b"built-in scratch" in lib.mkv_last_error()
