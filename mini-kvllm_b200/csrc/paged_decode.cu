@@ -136,12 +136,20 @@ __device__ __forceinline__ SplitRange split_range(const DecodeParams& p, int seq
 // A unit is (sequence, KV head, head group): y = kv_head * head_groups + head group.
 // A segment is a contiguous token range of one unit processed by one CTA. With a fixed
 // split count (num_splits > 0) a CTA runs the single segment (split, y, seq) of its
-// grid coordinates. With the balanced schedule the tiles of all units are numbered
-// unit by unit (sequence-major) into W work items, CTA c of G takes items
-// [W*c/G, W*(c+1)/G), and so walks one or more segments; a unit that crosses a CTA
-// boundary is finished by partials. Partial k of a unit lives in slot
-// 2*(c_first + k) + (k == 0 ? first_off : 0): slot 2c holds CTA c's first segment,
-// 2c+1 its last, so every slot has one writer and the workspace is bounded by 2G slots.
+// grid coordinates. With the balanced schedule the work items (token tiles) are split
+// evenly over the CTAs, each taking a contiguous range and so walking one or more
+// segments; a unit that crosses a CTA boundary is finished by partials.
+//   * Lanes (the U = kv_heads * head_groups values of y share the grid evenly): CTA
+//     c = y + U * r is rank r of lane y; lane y's items are the tiles of units (s, y) for
+//     s = 0, 1, ... and its G/U ranks split them evenly. All lanes walk the same token
+//     ranges at the same pace, so the KV heads of a token row (adjacent in HBM) are read
+//     together, as with a fixed (split, head, seq) grid.
+//   * Otherwise (U does not divide the grid closely enough) one sequence of W items over
+//     all units, sequence-major, split over the G CTAs.
+// Rank r's range is [W*r/G, W*(r+1)/G) in its item sequence. Partial k of a unit is
+// written by rank r_first + k, i.e. CTA cta_base + cta_stride*(r_first + k), into slot
+// 2*cta + (k == 0 ? first_off : 0): slot 2c holds CTA c's first segment, 2c+1 its last,
+// so every slot has one writer and the workspace is bounded by 2 * grid slots.
 struct TokRange {
   int begin, end;
 };
@@ -150,7 +158,8 @@ struct Seg {
   int begin, end;  // token range [begin, end)
   int nparts;      // partials of the unit (1 = this segment is the whole unit)
   int part;        // this segment's index among them
-  int c_first, first_off;
+  int c_first, first_off;   // rank of partial 0's writer; partial 0 in its last-segment slot
+  int cta_base, cta_stride; // CTA index of rank r: cta_base + cta_stride * r
 };
 
 __device__ __forceinline__ int eff_ctx(const DecodeParams& p, int seq) {
@@ -173,8 +182,9 @@ __device__ __forceinline__ long long warp_sum_ll(long long v) {
 // Schedule state, uniform across the CTA, kept in shared memory so the kernels' inner
 // loops carry none of it in registers. Thread 0 advances it between two barriers.
 struct SchedState {
-  long long w, w_end, unit_start, W, G;
+  long long w, w_end, unit_start, W, G;  // item range of this rank; items and ranks in its sequence
   int seq, y, nt, eff, U;
+  int lanes, rank;
   int has, fixed_pending;
   Seg cur;
 };
@@ -207,17 +217,22 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
   long long total = 0;
 #pragma unroll
   for (int i = 0; i < kThreads / 32; ++i) total += red[i];
-  const long long W = total * U;
-  long long G = p.sched_ctas;
-  const long long by_work = W / p.min_tiles;  // every CTA gets >= min_tiles items
+  // lanes when U divides the grid with at most 1/32 of it idle
+  const long long grid = p.sched_ctas;
+  const bool lanes = (long long)U <= grid && (grid - grid / U * U) * 32 <= grid;
+  const long long W = lanes ? total : total * U;
+  long long G = lanes ? grid / U : grid;
+  const long long by_work = W / p.min_tiles;  // every rank gets >= min_tiles items
   if (G > by_work) G = by_work > 0 ? by_work : 1;
   const long long c = blockIdx.x;
+  const long long rank = lanes ? c / U : c;
   long long w = 0, w_end = 0;
-  if (c < G) {  // uniform across the block
-    w = W * c / G;
-    w_end = W * (c + 1) / G;
-    // the sequence whose tile prefix P(s) satisfies P(s) <= w / U < P(s) + tiles(s)
-    const long long q = w / U;
+  if (rank < G) {  // uniform across the block
+    w = W * rank / G;
+    w_end = W * (rank + 1) / G;
+    // the sequence whose tile prefix P(s) satisfies P(s) <= w' < P(s) + tiles(s), with
+    // w' = w for lanes and w / U for the unit-major order
+    const long long q = lanes ? w : w / U;
     long long carry = 0;
     for (int base = 0; base < p.num_seqs; base += kThreads) {
       const int s = base + tid;
@@ -253,14 +268,21 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
     st.U = U;
     st.w = w;
     st.w_end = w_end;
+    st.lanes = lanes ? 1 : 0;
+    st.rank = (int)rank;
     st.fixed_pending = 0;
     if (w < w_end) {
       st.seq = (int)found[0];
       st.eff = eff_ctx(p, st.seq);
       st.nt = unit_tiles<TILE>(st.eff);
-      const long long r = w - found[1] * U;
-      st.y = (int)(r / st.nt);
-      st.unit_start = found[1] * U + (long long)st.y * st.nt;
+      if (lanes) {
+        st.y = (int)(c % U);
+        st.unit_start = found[1];
+      } else {
+        const long long r = w - found[1] * U;
+        st.y = (int)(r / st.nt);
+        st.unit_start = found[1] * U + (long long)st.y * st.nt;
+      }
     }
   }
   __syncthreads();
@@ -287,6 +309,8 @@ __device__ bool sched_next(const DecodeParams& p, SchedState& st) {
           sg.nparts = rng.active;
           sg.part = blockIdx.x;
           sg.c_first = sg.first_off = 0;
+          sg.cta_base = 0;
+          sg.cta_stride = 1;
         }
       }
     } else if (st.w < st.w_end) {
@@ -302,14 +326,17 @@ __device__ bool sched_next(const DecodeParams& p, SchedState& st) {
       const long long c_first = cta_of(st, st.unit_start);
       const long long c_last = cta_of(st, st.unit_start + nt - 1);
       sg.nparts = (int)(c_last - c_first + 1);
-      sg.part = (int)(blockIdx.x - c_first);
+      sg.part = (int)(st.rank - c_first);
       sg.c_first = (int)c_first;
       sg.first_off = (st.W * c_first / st.G) < st.unit_start ? 1 : 0;
+      sg.cta_base = st.lanes ? st.y : 0;
+      sg.cta_stride = st.lanes ? st.U : 1;
       st.w = st.unit_start + te;
       if (te == nt) {
         st.unit_start += nt;
-        if (++st.y == st.U) {
-          st.y = 0;
+        const bool next_seq = st.lanes || ++st.y == st.U;
+        if (next_seq) {
+          if (!st.lanes) st.y = 0;
           ++st.seq;
           if (st.w < st.w_end) {
             st.eff = eff_ctx(p, st.seq);
@@ -328,7 +355,8 @@ __device__ bool sched_next(const DecodeParams& p, SchedState& st) {
 __device__ __forceinline__ int64_t part_row(const DecodeParams& p, const Seg& sg, int h0, int k,
                                             int h) {
   if (p.balanced) {
-    const int slot = 2 * (sg.c_first + k) + (k == 0 ? sg.first_off : 0);
+    const int cta = sg.cta_base + sg.cta_stride * (sg.c_first + k);
+    const int slot = 2 * cta + (k == 0 ? sg.first_off : 0);
     return (int64_t)slot * p.heads_per_cta + h;
   }
   return ((int64_t)sg.seq * p.num_heads + h0 + h) * p.num_splits + k;
@@ -424,6 +452,74 @@ __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
     op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O * wts[active * nh + h]);
   }
   if (threadIdx.x == 0) *ctr = 0u;
+}
+
+// ---------------------------------------------------------------- tensor-core tile loads
+// Issues the cp.async copies of one K/V tile (TILE token rows of ROWB bytes of one kv
+// head, starting at token t0) into the stage's buffers, 16-byte chunks XOR-swizzled by
+// row (chunk ^ (row & 7)), and writes the stage's per-row valid flags. Rows past the
+// segment or on a missing page are zero-filled (src-size 0) and flagged invalid.
+// When the tile lies inside one page (power-of-two block_size >= TILE) the thread's
+// rows are one base address plus a constant stride, so a full tile costs two cp.async
+// and one address add per pass.
+template <int TILE, int ROWB>
+__device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
+                                             const BlockSlice& slice, const int* bt_s,
+                                             const TokRange& rng, int t0, uint8_t* kd,
+                                             uint8_t* vd, uint8_t* valid, int64_t row_stride,
+                                             int64_t head_off, bool one_page_per_tile) {
+  constexpr int CPR = ROWB / 16;         // 16-byte chunks per row
+  constexpr int RPP = kThreads / CPR;    // rows per pass (a multiple of 8)
+  constexpr int PASSES = TILE / RPP;
+  static_assert(RPP % 8 == 0 && TILE % RPP == 0 && TILE <= kThreads, "tile geometry");
+  const int tid = threadIdx.x, ld_c = tid % CPR, ld_r0 = tid / CPR;
+  // (r & 7) is the same for all of this thread's rows r = ld_r0 + i * RPP
+  const uint32_t soff0 = ld_r0 * ROWB + ((ld_c ^ (ld_r0 & 7)) << 4);
+  const uint32_t kd0 = smem_u32(kd) + soff0, vd0 = smem_u32(vd) + soff0;
+  if (one_page_per_tile) {
+    const int page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
+    const int nrows = page >= 0 ? min(TILE, rng.end - t0) : 0;
+    const int64_t base =
+        page >= 0 ? ((int64_t)page * p.block_size + (t0 & ((1 << p.bs_shift) - 1)) + ld_r0) *
+                            row_stride + head_off + ld_c * 16
+                  : 0;
+    const uint8_t* kp = p.k_cache + base;
+    const uint8_t* vp = p.v_cache + base;
+    const int64_t step = (int64_t)RPP * row_stride;
+    if (nrows == TILE) {
+#pragma unroll
+      for (int i = 0; i < PASSES; ++i) {
+        cp_async_16(kd0 + i * RPP * ROWB, kp + i * step, 16);
+        cp_async_16(vd0 + i * RPP * ROWB, vp + i * step, 16);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < PASSES; ++i) {
+        const bool ok = ld_r0 + i * RPP < nrows;
+        cp_async_16(kd0 + i * RPP * ROWB, ok ? kp + i * step : p.k_cache, ok ? 16 : 0);
+        cp_async_16(vd0 + i * RPP * ROWB, ok ? vp + i * step : p.v_cache, ok ? 16 : 0);
+      }
+    }
+    if (tid < TILE) valid[tid] = tid < nrows ? 1 : 0;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < PASSES; ++i) {
+    const int r = ld_r0 + i * RPP;
+    const int t = t0 + r;
+    int page = -1, boff = 0;
+    if (t < rng.end) {
+      int blk;
+      split_token(p, t, blk, boff);
+      page = slice_page(p, seq, slice, bt_s, blk);
+    }
+    const bool ok = page >= 0;
+    const int64_t off =
+        ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
+    cp_async_16(kd0 + i * RPP * ROWB, p.k_cache + off, ok ? 16 : 0);
+    cp_async_16(vd0 + i * RPP * ROWB, p.v_cache + off, ok ? 16 : 0);
+    if (ld_c == 0) valid[r] = ok ? 1 : 0;
+  }
 }
 
 // ============================================================ CUDA-core kernel
@@ -659,11 +755,8 @@ paged_decode_tc_kernel(const DecodeParams p) {
   constexpr int D = kTcD;
   constexpr int EB = sizeof(CT);
   constexpr int ROWB = D * EB;    // 256 (16-bit) or 128 (e4m3) bytes per token row
-  constexpr int CPR = ROWB / 16;  // 16-byte chunks per row
   constexpr int TILE_BYTES = kTcTile * ROWB;
   constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  constexpr int ROWS_PER_PASS = kThreads / CPR;
-  constexpr int PASSES = kTcTile / ROWS_PER_PASS;
   constexpr size_t FRONT = tc_front_bytes<CT, NT, STAGES>();
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -690,43 +783,14 @@ paged_decode_tc_kernel(const DecodeParams p) {
   // ---- producer: all threads issue 16-byte cp.async for their rows/chunks
   const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
   const int64_t head_off = (int64_t)kvh * ROWB;
-  const int ld_c = tid % CPR;
-  const int ld_r0 = tid / CPR;
   // A tile never straddles a page when block_size is a power of two >= the tile.
   const bool one_page_per_tile = p.bs_shift >= 6;
   auto load_tile = [&](int it) {
     const int stage = it % STAGES;
-    const int t0 = rng.begin + it * kTcTile;
     uint8_t* kd = smem + stage * STAGE_BYTES;
-    uint8_t* vd = kd + TILE_BYTES;
-    int tile_page = -1, tile_off = 0;
-    if (one_page_per_tile) {
-      tile_page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
-      tile_off = t0 & ((1 << p.bs_shift) - 1);
-    }
-#pragma unroll
-    for (int i = 0; i < PASSES; ++i) {
-      const int r = ld_r0 + i * ROWS_PER_PASS;
-      const int t = t0 + r;
-      int page = -1, boff = 0;
-      if (t < rng.end) {
-        if (one_page_per_tile) {
-          page = tile_page;
-          boff = tile_off + r;
-        } else {
-          int blk;
-          split_token(p, t, blk, boff);
-          page = slice_page(p, seq, slice, bt_s, blk);
-        }
-      }
-      const bool ok = page >= 0;
-      const int64_t off =
-          ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
-      const int soff = r * ROWB + ((ld_c ^ (r & 7)) << 4);
-      cp_async_16(smem_u32(kd + soff), p.k_cache + off, ok ? 16 : 0);
-      cp_async_16(smem_u32(vd + soff), p.v_cache + off, ok ? 16 : 0);
-      if (ld_c == 0) valid[stage * kTcTile + r] = ok ? 1 : 0;
-    }
+    load_kv_tile<kTcTile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kTcTile, kd,
+                                kd + TILE_BYTES, valid + stage * kTcTile, row_stride, head_off,
+                                one_page_per_tile);
   };
 
   // prologue: STAGES-1 tiles in flight before building the query fragments
@@ -1056,11 +1120,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
 paged_decode_fp8mma_kernel(const DecodeParams p) {
   constexpr int D = kTcD;
   constexpr int ROWB = D;         // bytes per e4m3 token row
-  constexpr int CPR = ROWB / 16;  // 8 chunks per row
   constexpr int TILE_BYTES = kF8Tile * ROWB;
   constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  constexpr int ROWS_PER_PASS = kThreads / CPR;  // 16
-  constexpr int PASSES = kF8Tile / ROWS_PER_PASS;  // 8
   constexpr size_t FRONT = f8_front_bytes<NT, STAGES>();
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -1086,42 +1147,13 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
 
   const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
   const int64_t head_off = (int64_t)kvh * ROWB;
-  const int ld_c = tid % CPR;
-  const int ld_r0 = tid / CPR;
   const bool one_page_per_tile = p.bs_shift >= 7;  // power-of-two block_size >= 128
   auto load_tile = [&](int it) {
     const int stage = it % STAGES;
-    const int t0 = rng.begin + it * kF8Tile;
     uint8_t* kd = smem + stage * STAGE_BYTES;
-    uint8_t* vd = kd + TILE_BYTES;
-    int tile_page = -1, tile_off = 0;
-    if (one_page_per_tile) {
-      tile_page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
-      tile_off = t0 & ((1 << p.bs_shift) - 1);
-    }
-#pragma unroll
-    for (int i = 0; i < PASSES; ++i) {
-      const int r = ld_r0 + i * ROWS_PER_PASS;
-      const int t = t0 + r;
-      int page = -1, boff = 0;
-      if (t < rng.end) {
-        if (one_page_per_tile) {
-          page = tile_page;
-          boff = tile_off + r;
-        } else {
-          int blk;
-          split_token(p, t, blk, boff);
-          page = slice_page(p, seq, slice, bt_s, blk);
-        }
-      }
-      const bool ok = page >= 0;
-      const int64_t off =
-          ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + ld_c * 16 : 0;
-      const int soff = r * ROWB + ((ld_c ^ (r & 7)) << 4);
-      cp_async_16(smem_u32(kd + soff), p.k_cache + off, ok ? 16 : 0);
-      cp_async_16(smem_u32(vd + soff), p.v_cache + off, ok ? 16 : 0);
-      if (ld_c == 0) valid[stage * kF8Tile + r] = ok ? 1 : 0;
-    }
+    load_kv_tile<kF8Tile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kF8Tile, kd,
+                                kd + TILE_BYTES, valid + stage * kF8Tile, row_stride, head_off,
+                                one_page_per_tile);
   };
 
 #pragma unroll

@@ -273,12 +273,15 @@ def _balanced_case(case, fp8):
     if case == "wide_group":      # 32 query heads per kv head: two head groups per unit
         return wl.decode_workload(case, 7, 64, 2, 128, 256, [9000, 1, 0, 4097, 128, 65, 30000],
                                   fp8=fp8, seed=23, with_append=False)
+    if case == "unit_major":      # 32 kv heads do not divide a 444-CTA grid: unit-major order
+        lens = torch.randint(0, 2500, (40,), generator=g).tolist()
+        return wl.decode_workload(case, 40, 32, 32, 128, 16, lens, fp8=fp8, seed=25, with_append=False)
     # a table wide enough that the merge bound (128 partials per unit) sets the CTA share
     return wl.decode_workload(case, 2, 8, 1, 128, 256, [100000, 3], fp8=fp8, seed=24, with_append=False)
 
 
 @pytest.mark.parametrize("fp8", [False, True])
-@pytest.mark.parametrize("case", ["one_long", "many_ragged", "wide_group", "very_long"])
+@pytest.mark.parametrize("case", ["one_long", "many_ragged", "wide_group", "unit_major", "very_long"])
 def test_balanced_schedule(case, fp8):
     """The automatic (balanced, persistent) schedule against a float32 torch reference on
     every sequence, and against the one-split plan over the whole batch."""
