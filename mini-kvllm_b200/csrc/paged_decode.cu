@@ -49,8 +49,9 @@ constexpr int kMaxHeadsPerCta = 16;  // query heads of one KV head handled by a 
 constexpr int kTcTile = 64;          // tokens per pipeline stage, tensor-core kernel
 constexpr int kGenTile = 32;         // tokens per pipeline stage, CUDA-core kernel
 constexpr int kChunkAlign = 128;     // split boundaries are multiples of every tile
-constexpr int kMaxSplits = 128;  // bounds the merge-weight buffer in shared memory
+constexpr int kMaxSplits = 128;     // bounds the partials a unit is merged from
 constexpr int kMaxBtSmem = 128;      // block-table entries staged in shared memory
+constexpr int kTcD = 128;           // head_dim of the tensor-core kernels
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
@@ -86,6 +87,7 @@ struct DecodeParams {
   int balanced;
   int sched_ctas;
   int min_tiles;
+  int q_vec16;  // query rows start on 16-byte boundaries (base and both strides)
   int32_t* invalid;
 };
 
@@ -131,6 +133,26 @@ __device__ __forceinline__ SplitRange split_range(const DecodeParams& p, int seq
   r.end = (int)((int64_t)r.begin + p.chunk < eff ? (int64_t)r.begin + p.chunk : eff);
   return r;
 }
+
+// Optional per-CTA event timestamps (globaltimer, ns) for studying the schedule; compiled
+// only with -DMKV_DECODE_TRACE and read back with mkv_debug_decode_trace.
+#ifdef MKV_DECODE_TRACE
+constexpr int kTraceEvents = 96;
+__device__ unsigned long long g_dtrace[kNumSMs * 4][kTraceEvents];
+#define MKV_DTRACE(ev)                                                              \
+  do {                                                                              \
+    if (threadIdx.x == 0 && (ev) < kTraceEvents && blockIdx.x < kNumSMs * 4) {      \
+      unsigned long long t_;                                                        \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                        \
+      g_dtrace[blockIdx.x][(ev)] = t_;                                              \
+    }                                                                               \
+  } while (0)
+constexpr int kTraceEventsLast = kTraceEvents - 1;
+#else
+#define MKV_DTRACE(ev) \
+  do {                 \
+  } while (0)
+#endif
 
 // ---------------------------------------------------------------- work schedule
 // A unit is (sequence, KV head, head group): y = kv_head * head_groups + head group.
@@ -209,14 +231,39 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
   __shared__ long long red[kThreads / 32];
   __shared__ long long found[2];
   const int U = p.num_kv_heads * p.head_groups;
+  // Up to kScanCache sequences per thread are kept in registers (thread t holds the
+  // sequences [t * kScanCache, (t + 1) * kScanCache)), so that for num_seqs <=
+  // kThreads * kScanCache the lengths are read once and one block scan finds the start.
+  constexpr int kScanCache = 8;
+  const bool cached = p.num_seqs <= kThreads * kScanCache;
+  int tl[kScanCache];
   long long part = 0;
-  for (int s = tid; s < p.num_seqs; s += kThreads) part += unit_tiles<TILE>(eff_ctx(p, s));
-  part = warp_sum_ll(part);
-  if (lane == 0) red[warp] = part;
-  __syncthreads();
-  long long total = 0;
+  if (cached) {
 #pragma unroll
-  for (int i = 0; i < kThreads / 32; ++i) total += red[i];
+    for (int j = 0; j < kScanCache; ++j) {
+      const int sq = tid * kScanCache + j;
+      tl[j] = sq < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, sq)) : 0;
+      part += tl[j];
+    }
+  } else {
+    for (int sq = tid; sq < p.num_seqs; sq += kThreads) part += unit_tiles<TILE>(eff_ctx(p, sq));
+  }
+  // inclusive block scan of the per-thread sums (cached layout: sequence order)
+  long long x = part;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long v = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += v;
+  }
+  if (lane == 31) red[warp] = x;
+  __syncthreads();
+  long long total = 0, before = 0;
+#pragma unroll
+  for (int i = 0; i < kThreads / 32; ++i) {
+    if (i < warp) before += red[i];
+    total += red[i];
+  }
+  const long long excl = before + x - part;  // items before this thread's sequences
   // lanes when U divides the grid with at most 1/32 of it idle
   const long long grid = p.sched_ctas;
   const bool lanes = (long long)U <= grid && (grid - grid / U * U) * 32 <= grid;
@@ -233,33 +280,48 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
     // the sequence whose tile prefix P(s) satisfies P(s) <= w' < P(s) + tiles(s), with
     // w' = w for lanes and w / U for the unit-major order
     const long long q = lanes ? w : w / U;
-    long long carry = 0;
-    for (int base = 0; base < p.num_seqs; base += kThreads) {
-      const int s = base + tid;
-      const long long t = s < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, s)) : 0;
-      long long x = t;
+    if (cached) {
+      if (excl <= q && q < excl + part) {
+        long long pre = excl;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const long long v = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += v;
+        for (int j = 0; j < kScanCache; ++j) {
+          if (pre <= q && q < pre + tl[j]) {
+            found[0] = tid * kScanCache + j;
+            found[1] = pre;
+          }
+          pre += tl[j];
+        }
       }
-      __syncthreads();  // red is free again
-      if (lane == 31) red[warp] = x;
       __syncthreads();
-      long long off = carry, chunk = 0;
+    } else {
+      long long carry = 0;
+      for (int base = 0; base < p.num_seqs; base += kThreads) {
+        const int sq = base + tid;
+        const long long t = sq < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, sq)) : 0;
+        long long y = t;
 #pragma unroll
-      for (int i = 0; i < kThreads / 32; ++i) {
-        if (i < warp) off += red[i];
-        chunk += red[i];
+        for (int o = 1; o < 32; o <<= 1) {
+          const long long v = __shfl_up_sync(0xffffffffu, y, o);
+          if (lane >= o) y += v;
+        }
+        __syncthreads();  // red is free again
+        if (lane == 31) red[warp] = y;
+        __syncthreads();
+        long long off = carry, chunk = 0;
+#pragma unroll
+        for (int i = 0; i < kThreads / 32; ++i) {
+          if (i < warp) off += red[i];
+          chunk += red[i];
+        }
+        const long long incl = off + y;
+        if (sq < p.num_seqs && incl - t <= q && q < incl) {
+          found[0] = sq;
+          found[1] = incl - t;
+        }
+        carry += chunk;
+        __syncthreads();
+        if (carry > q) break;
       }
-      const long long incl = off + x;
-      if (s < p.num_seqs && incl - t <= q && q < incl) {
-        found[0] = s;
-        found[1] = incl - t;
-      }
-      carry += chunk;
-      __syncthreads();
-      if (carry > q) break;
     }
   }
   if (tid == 0) {
@@ -389,16 +451,25 @@ __device__ __forceinline__ int slice_page(const DecodeParams& p, int seq, const 
 }
 
 // ---------------------------------------------------------------- shared epilogue
+// Arrival on a unit's counter: thread 0's release/acquire add at gpu scope, after a
+// barrier that orders every thread's partial stores before it (the split-K semaphore
+// pattern). The last to arrive then reads the others' partials after a second barrier.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* ctr, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(ctr), "r"(v)
+               : "memory");
+  return old;
+}
+
 // The CTA's result for its nh heads is staged in shared memory: o_s[h * ld + d]
-// (unnormalised), m_s[h] (log2 units), l_s[h]. A sequence with one active split writes
-// out = o * v_scale / l directly. Otherwise the split stores its (m, l, o) partial and
-// the last split to arrive (per-(seq, kv head) counter) merges all partials and writes
-// the output; it also zeroes the counter for the next launch. `wts` needs
-// (active + 1) * nh floats of shared memory.
+// (unnormalised), m_s[h] (log2 units), l_s[h]. A unit finished by one segment writes
+// out = o * v_scale / l directly. Otherwise the segment stores its (m, l, o) partial and
+// the last to arrive (per-unit counter) merges all partials in one online pass (running
+// maximum with rescaling, the same arithmetic as the softmax) and writes the output; it
+// also zeroes the counter for the next launch.
 template <typename QT>
 __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
-                           const float* o_s, int ld, const float* m_s, const float* l_s,
-                           float* wts) {
+                           const float* o_s, int ld, const float* m_s, const float* l_s) {
   const int D = p.head_dim;
   const int seq = sg.seq, active = sg.nparts;
   const float vs = p.v_scale != nullptr ? __ldg(p.v_scale) : 1.0f;
@@ -420,36 +491,45 @@ __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
       __stcg(p.part_ml + b * 2 + 1, l_s[h]);
     }
   }
-  __threadfence();
   __syncthreads();
   __shared__ bool last;
   unsigned int* ctr = p.arrivals + (int64_t)seq * p.num_kv_heads * p.head_groups + sg.y;
-  if (threadIdx.x == 0) last = atomicAdd(ctr, 1u) == (unsigned)(active - 1);
+  if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(ctr, 1u) == (unsigned)(active - 1);
   __syncthreads();
   if (!last) return;
-  __threadfence();
-  // merge weights: wts[s * nh + h] = 2^(m_s - M_h); wts[active * nh + h] = v_scale / L_h
-  for (int h = threadIdx.x; h < nh; h += blockDim.x) {
-    float M = -INFINITY;
-    for (int s = 0; s < active; ++s) M = fmaxf(M, __ldcg(p.part_ml + part_row(p, sg, h0, s, h) * 2));
-    const float mb = M == -INFINITY ? 0.0f : M;
-    float L = 0.0f;
+  // OUT outputs per thread at a time, so that their partial loads are in flight together
+  constexpr int OUT = 4;
+  for (int base = threadIdx.x; base < nh * D; base += OUT * blockDim.x) {
+    float M[OUT], L[OUT], O[OUT];
+#pragma unroll
+    for (int i = 0; i < OUT; ++i) M[i] = -INFINITY, L[i] = 0.0f, O[i] = 0.0f;
+#pragma unroll 2
     for (int s = 0; s < active; ++s) {
-      const int64_t b = part_row(p, sg, h0, s, h);
-      const float w = exp2f(__ldcg(p.part_ml + b * 2) - mb);
-      wts[s * nh + h] = w;
-      L = fmaf(w, __ldcg(p.part_ml + b * 2 + 1), L);
+#pragma unroll
+      for (int i = 0; i < OUT; ++i) {
+        const int idx = base + i * blockDim.x;
+        if (idx < nh * D) {
+          const int h = idx / D, d = idx - h * D;
+          const int64_t b = part_row(p, sg, h0, s, h);
+          const float m = __ldcg(p.part_ml + b * 2), l = __ldcg(p.part_ml + b * 2 + 1);
+          const float a = __ldcg(p.part_acc + b * D + d);
+          const float mn = fmaxf(M[i], m);
+          const float ref = mn == -INFINITY ? 0.0f : mn;
+          const float c_old = exp2f(M[i] - ref), c_new = exp2f(m - ref);
+          O[i] = fmaf(O[i], c_old, a * c_new);
+          L[i] = fmaf(L[i], c_old, l * c_new);
+          M[i] = mn;
+        }
+      }
     }
-    wts[active * nh + h] = vs / L;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < nh * D; idx += blockDim.x) {
-    const int h = idx / D, d = idx - h * D;
-    float O = 0.0f;
-#pragma unroll 4
-    for (int s = 0; s < active; ++s)
-      O = fmaf(wts[s * nh + h], __ldcg(p.part_acc + part_row(p, sg, h0, s, h) * D + d), O);
-    op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O * wts[active * nh + h]);
+#pragma unroll
+    for (int i = 0; i < OUT; ++i) {
+      const int idx = base + i * blockDim.x;
+      if (idx < nh * D) {
+        const int h = idx / D, d = idx - h * D;
+        op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O[i] * vs / L[i]);
+      }
+    }
   }
   if (threadIdx.x == 0) *ctr = 0u;
 }
@@ -522,6 +602,29 @@ __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
   }
 }
 
+// The nh query rows (seq, h0 .. h0 + nh - 1) of a segment into q_s (pitch kTcD elements):
+// 16-byte cp.async chunks when the rows are 16-byte aligned (joining the caller's next
+// cp.async group), else element copies.
+template <typename QT>
+__device__ __forceinline__ void load_q_rows(const DecodeParams& p, int seq, int h0, int nh,
+                                            QT* q_s) {
+  constexpr int D = kTcD;
+  constexpr int PER = 16 / (int)sizeof(QT);  // elements per 16-byte chunk
+  constexpr int CPR = D / PER;
+  const QT* qp = reinterpret_cast<const QT*>(p.q) + (int64_t)seq * p.q_sb + (int64_t)h0 * p.q_sh;
+  if (p.q_vec16) {
+    for (int c = threadIdx.x; c < nh * CPR; c += kThreads) {
+      const int r = c / CPR, k = c - r * CPR;
+      cp_async_16(smem_u32(q_s + r * D + k * PER), qp + (int64_t)r * p.q_sh + k * PER, 16);
+    }
+  } else {
+    for (int i = threadIdx.x; i < nh * D; i += kThreads) {
+      const int r = i / D, d = i - r * D;
+      q_s[r * D + d] = qp[(int64_t)r * p.q_sh + d];
+    }
+  }
+}
+
 // ============================================================ CUDA-core kernel
 // Any float cache type, runtime head_dim (multiple of 16, <= 256). A warp scores one
 // head over the 32 tokens of a tile (lane = token), the softmax update runs per head
@@ -538,7 +641,7 @@ paged_decode_generic_kernel(const DecodeParams p) {
   const int row_pitch = row_bytes + 16;  // padding keeps lane-per-row reads conflict-free
   const int chunks = row_bytes / 16;
   const int ring = 4 * kGenTile * row_pitch;
-  const int epi = (kMaxHeadsPerCta * D + (kMaxSplits + 1) * kMaxHeadsPerCta) * 4;
+  const int epi = kMaxHeadsPerCta * D * 4;
 
   uint8_t* kbuf = smem;                                             // [2][kGenTile][row_pitch]
   uint8_t* vbuf = kbuf + 2 * kGenTile * row_pitch;                  // [2][kGenTile][row_pitch]
@@ -688,16 +791,14 @@ paged_decode_generic_kernel(const DecodeParams p) {
     }
   }
   __syncthreads();
-  float* wts = o_s + kMaxHeadsPerCta * D;
-  finish_cta<QT>(p, sched.cur, h0, nh, o_s, D, m_s, l_s, wts);
+  finish_cta<QT>(p, sched.cur, h0, nh, o_s, D, m_s, l_s);
   }
 }
 
 size_t generic_smem_bytes(int head_dim, int elem_bytes) {
   const int row_pitch = head_dim * elem_bytes + 16;
   const size_t ring = (size_t)4 * kGenTile * row_pitch;
-  const size_t epi = (size_t)kMaxHeadsPerCta * head_dim * 4 +
-                     (size_t)(kMaxSplits + 1) * kMaxHeadsPerCta * 4;
+  const size_t epi = (size_t)kMaxHeadsPerCta * head_dim * 4;
   return (ring > epi ? ring : epi) + (size_t)kMaxHeadsPerCta * head_dim * 4 +
          (size_t)kMaxHeadsPerCta * kGenTile * 4 + 3 * kMaxHeadsPerCta * 4 + 2 * kGenTile +
          kMaxBtSmem * 4;
@@ -720,7 +821,6 @@ template <> struct TcTraits<fp8> {
   static constexpr bool kFp8 = true;
 };
 
-constexpr int kTcD = 128;
 
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t r;
@@ -730,10 +830,10 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
 
 // Epilogue buffers (floats), for a CTA of up to 8*NT query heads: the 4 warps' partial
 // O^T [4][8NT][D+4] (warp 0's slot is overwritten in place by the merged O), their m
-// and l [4][8NT] each, the merged m and l [8NT] each, merge weights [kMaxSplits+1][8NT].
+// and l [4][8NT] each, the merged m and l [8NT] each.
 template <int NT>
 constexpr size_t tc_epilogue_bytes() {
-  return (size_t)(4 * 8 * NT * (kTcD + 4) + 8 * 8 * NT + 2 * 8 * NT + (kMaxSplits + 1) * 8 * NT) * 4;
+  return (size_t)(4 * 8 * NT * (kTcD + 4) + 8 * 8 * NT + 2 * 8 * NT) * 4;
 }
 
 template <typename CT, int NT, int STAGES>
@@ -742,8 +842,9 @@ constexpr size_t tc_front_bytes() {  // ring, reused by the epilogue
   return ring > tc_epilogue_bytes<NT>() ? ring : tc_epilogue_bytes<NT>();
 }
 template <typename CT, int NT, int STAGES>
-constexpr size_t tc_smem_bytes() {  // + valid flags + staged block table
-  return tc_front_bytes<CT, NT, STAGES>() + (size_t)STAGES * kTcTile + kMaxBtSmem * 4;
+constexpr size_t tc_smem_bytes() {  // + valid flags + staged block table + query rows
+  return tc_front_bytes<CT, NT, STAGES>() + (size_t)STAGES * kTcTile + kMaxBtSmem * 4 +
+         (size_t)8 * NT * kTcD * 2;
 }
 
 template <typename QT, typename CT, int NT, int STAGES, int MINB>
@@ -762,12 +863,28 @@ paged_decode_tc_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* valid = smem + FRONT;                                 // [STAGES][kTcTile]
   int* bt_s = reinterpret_cast<int*>(valid + STAGES * kTcTile);  // [kMaxBtSmem]
+  QT* q_s = reinterpret_cast<QT*>(bt_s + kMaxBtSmem);             // [8 * NT][D]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
+  // Segment hand-over: when the epilogue fits in one ring stage, the next segment's first
+  // tiles are issued into the free stages before this segment's epilogue runs in the
+  // stage of its last tile, so the page fetch overlaps the merge and the partial write.
+  // Ring stage of tile `it` of a segment: (gt + it) % STAGES, gt = tiles begun before it.
+  constexpr bool kPrefetch = tc_epilogue_bytes<NT>() <= (size_t)STAGE_BYTES;
+  const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
+  // A tile never straddles a page when block_size is a power of two >= the tile.
+  const bool one_page_per_tile = p.bs_shift >= 6;
   __shared__ SchedState sched;
+  MKV_DTRACE(0);
   sched_init<kTcTile>(p, sched);
-  while (sched_next<kTcTile>(p, sched)) {
+  MKV_DTRACE(1);
+  bool has = sched_next<kTcTile>(p, sched);
+  int nseg = 0;
+  bool prefetched = false;
+  int gt = 0;
+  BlockSlice slice{0, 0};
+  while (has) {
   const TokRange rng{sched.cur.begin, sched.cur.end};
   const int seq = sched.cur.seq;
   const int kvh = sched.cur.y / p.head_groups;
@@ -777,34 +894,39 @@ paged_decode_tc_kernel(const DecodeParams p) {
   const bool count_invalid = (kvh == 0 && hgrp == 0);
 
   const int ntiles = (rng.end - rng.begin + kTcTile - 1) / kTcTile;  // 0 when empty
-  const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
-  __syncthreads();
+  MKV_DTRACE(2 + 10 * nseg);
+  if (!prefetched) {
+    slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
+    __syncthreads();
+  }
+  MKV_DTRACE(3 + 10 * nseg);
 
   // ---- producer: all threads issue 16-byte cp.async for their rows/chunks
-  const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
   const int64_t head_off = (int64_t)kvh * ROWB;
-  // A tile never straddles a page when block_size is a power of two >= the tile.
-  const bool one_page_per_tile = p.bs_shift >= 6;
   auto load_tile = [&](int it) {
-    const int stage = it % STAGES;
+    const int stage = (gt + it) % STAGES;
     uint8_t* kd = smem + stage * STAGE_BYTES;
     load_kv_tile<kTcTile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kTcTile, kd,
                                 kd + TILE_BYTES, valid + stage * kTcTile, row_stride, head_off,
                                 one_page_per_tile);
   };
 
-  // prologue: STAGES-1 tiles in flight before building the query fragments
-#pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < ntiles) load_tile(s);
+  // prologue: the query rows, then STAGES-1 tiles, in flight before the query fragments
+  if (!prefetched) {
+    load_q_rows<QT>(p, seq, h0, nh, q_s);
     cp_async_commit();
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+      if (s < ntiles) load_tile(s);
+      cp_async_commit();
+    }
   }
 
+  MKV_DTRACE(4 + 10 * nseg);
   // ---- Q^T fragments (B operand: K = head_dim, N = query heads of this CTA)
-  const QT* qp = reinterpret_cast<const QT*>(p.q);
-  auto qval = [&](int row, int d) -> float {
-    return row < nh ? to_f32(qp[(int64_t)seq * p.q_sb + (int64_t)(h0 + row) * p.q_sh + d]) : 0.0f;
-  };
+  cp_async_wait<STAGES - 1>();  // the query rows' group (older than the tiles')
+  __syncthreads();
+  auto qval = [&](int row, int d) -> float { return row < nh ? to_f32(q_s[row * D + d]) : 0.0f; };
   // head_dim index of B-fragment element (k-step ks, register half, element e).
   // 16-bit pages: b0 = k 2tig,2tig+1; b1 = k 2tig+8,2tig+9 (PTX m16n8k16 layout).
   // e4m3 pages: k is permuted so that one ldmatrix word (the 4 bytes d = 4tig..4tig+3)
@@ -840,6 +962,7 @@ paged_decode_tc_kernel(const DecodeParams p) {
       qb[nt][ks][0] = pack2<MT>(qval(row, qcol(ks, 0, 0)) * qpow2, qval(row, qcol(ks, 0, 1)) * qpow2);
       qb[nt][ks][1] = pack2<MT>(qval(row, qcol(ks, 1, 0)) * qpow2, qval(row, qcol(ks, 1, 1)) * qpow2);
     }
+  MKV_DTRACE(5 + 10 * nseg);
   const float ksc = kFp8 ? __ldg(p.k_scale) : 1.0f;
   const float sc = p.qk_scale_log2 * ksc / qpow2;
 
@@ -861,8 +984,9 @@ paged_decode_tc_kernel(const DecodeParams p) {
     __syncthreads();
     if (it + STAGES - 1 < ntiles) load_tile(it + STAGES - 1);
     cp_async_commit();
+    if (it == 0) MKV_DTRACE(6 + 10 * nseg);
 
-    const int stage = it % STAGES;
+    const int stage = (gt + it) % STAGES;
     const uint32_t kbase = smem_u32(smem + stage * STAGE_BYTES);
     const uint32_t vbase = kbase + TILE_BYTES;
     const uint8_t* vld = valid + stage * kTcTile;
@@ -990,18 +1114,52 @@ paged_decode_tc_kernel(const DecodeParams p) {
       }
     }
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  gt += ntiles;
+  MKV_DTRACE(7 + 10 * nseg);
 
-  // ---- merge the 4 warps' states through shared memory (reusing the ring)
+  // ---- hand over to the next segment, then merge this one
+  const Seg done = sched.cur;
+  uint8_t* scratch = smem;
+  if (kPrefetch) {
+    has = sched_next<kTcTile>(p, sched);  // its barrier: every warp is done with the ring
+    prefetched = false;
+    if (has) {
+      const TokRange nr{sched.cur.begin, sched.cur.end};
+      const int nkvh = sched.cur.y / p.head_groups;
+      const int nhg = sched.cur.y - nkvh * p.head_groups;
+      const int nt2 = (nr.end - nr.begin + kTcTile - 1) / kTcTile;
+      slice = stage_block_table(p, sched.cur.seq, nr, bt_s, nkvh == 0 && nhg == 0);
+      __syncthreads();
+      load_q_rows<QT>(p, sched.cur.seq, nkvh * p.group + nhg * p.heads_per_cta,
+                      min(p.heads_per_cta, p.group - nhg * p.heads_per_cta), q_s);
+      cp_async_commit();
+#pragma unroll
+      for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < nt2) {
+          uint8_t* kd = smem + ((gt + s) % STAGES) * STAGE_BYTES;
+          load_kv_tile<kTcTile, ROWB>(p, sched.cur.seq, slice, bt_s, nr, nr.begin + s * kTcTile,
+                                      kd, kd + TILE_BYTES, valid + ((gt + s) % STAGES) * kTcTile,
+                                      row_stride, (int64_t)nkvh * ROWB, one_page_per_tile);
+        }
+        cp_async_commit();
+      }
+      prefetched = true;
+    }
+    scratch = smem + ((gt + STAGES - 1) % STAGES) * STAGE_BYTES;  // stage of the last tile
+  } else {
+    cp_async_wait<0>();
+    __syncthreads();
+  }
+
+  MKV_DTRACE(8 + 10 * nseg);
+  // ---- merge the 4 warps' states through shared memory (in a free ring stage)
   constexpr int RP = D + 4;     // padded row pitch (floats)
   constexpr int HC = 8 * NT;    // head slots of this CTA
-  float* red_acc = reinterpret_cast<float*>(smem);  // [4][HC][RP]; slot 0 becomes the merged O
+  float* red_acc = reinterpret_cast<float*>(scratch);  // [4][HC][RP]; slot 0 becomes the merged O
   float* red_m = red_acc + 4 * HC * RP;             // [4][HC]
   float* red_l = red_m + 4 * HC;                    // [4][HC]
   float* m_s = red_l + 4 * HC;                      // [HC]
   float* l_s = m_s + HC;                            // [HC]
-  float* wts = l_s + HC;                            // [(kMaxSplits + 1) * HC]
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1048,8 +1206,13 @@ paged_decode_tc_kernel(const DecodeParams p) {
     red_acc[h * RP + d] = O;  // in place: this thread alone reads and writes (h, d)
   }
   __syncthreads();
-  finish_cta<QT>(p, sched.cur, h0, nh, red_acc, RP, m_s, l_s, wts);
+  MKV_DTRACE(9 + 10 * nseg);
+  finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s);
+  MKV_DTRACE(10 + 10 * nseg);
+  ++nseg;
+  if (!kPrefetch) has = sched_next<kTcTile>(p, sched);
   }
+  MKV_DTRACE(kTraceEventsLast);
 }
 
 // ============================================================ FP8 tensor-core kernel
@@ -1111,8 +1274,9 @@ constexpr size_t f8_front_bytes() {
   return ring > f8_epilogue_bytes<NT>() ? ring : f8_epilogue_bytes<NT>();
 }
 template <int NT, int STAGES>
-constexpr size_t f8_smem_bytes() {
-  return f8_front_bytes<NT, STAGES>() + (size_t)STAGES * kF8Tile + kMaxBtSmem * 4;
+constexpr size_t f8_smem_bytes() {  // + valid flags + staged block table + query rows
+  return f8_front_bytes<NT, STAGES>() + (size_t)STAGES * kF8Tile + kMaxBtSmem * 4 +
+         (size_t)8 * NT * kTcD * 2;
 }
 
 template <typename QT, int NT, int STAGES, int MINB>
@@ -1127,12 +1291,22 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* valid = smem + FRONT;                                  // [STAGES][kF8Tile]
   int* bt_s = reinterpret_cast<int*>(valid + STAGES * kF8Tile);   // [kMaxBtSmem]
+  QT* q_s = reinterpret_cast<QT*>(bt_s + kMaxBtSmem);              // [8 * NT][D]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
+  // Segment hand-over as in paged_decode_tc_kernel: the next segment's first tiles are
+  // issued before this segment's epilogue, which runs in the stage of its last tile.
+  constexpr bool kPrefetch = f8_epilogue_bytes<NT>() <= (size_t)STAGE_BYTES;
+  const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
+  const bool one_page_per_tile = p.bs_shift >= 7;  // power-of-two block_size >= 128
   __shared__ SchedState sched;
   sched_init<kF8Tile>(p, sched);
-  while (sched_next<kF8Tile>(p, sched)) {
+  bool has = sched_next<kF8Tile>(p, sched);
+  bool prefetched = false;
+  int gt = 0;  // tiles begun by this CTA before the current segment
+  BlockSlice slice{0, 0};
+  while (has) {
   const TokRange rng{sched.cur.begin, sched.cur.end};
   const int seq = sched.cur.seq;
   const int kvh = sched.cur.y / p.head_groups;
@@ -1142,31 +1316,34 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
   const bool count_invalid = (kvh == 0 && hgrp == 0);
 
   const int ntiles = (rng.end - rng.begin + kF8Tile - 1) / kF8Tile;
-  const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
-  __syncthreads();
+  if (!prefetched) {
+    slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
+    __syncthreads();
+  }
 
-  const int64_t row_stride = (int64_t)p.num_kv_heads * ROWB;
   const int64_t head_off = (int64_t)kvh * ROWB;
-  const bool one_page_per_tile = p.bs_shift >= 7;  // power-of-two block_size >= 128
   auto load_tile = [&](int it) {
-    const int stage = it % STAGES;
+    const int stage = (gt + it) % STAGES;
     uint8_t* kd = smem + stage * STAGE_BYTES;
     load_kv_tile<kF8Tile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kF8Tile, kd,
                                 kd + TILE_BYTES, valid + stage * kF8Tile, row_stride, head_off,
                                 one_page_per_tile);
   };
 
-#pragma unroll
-  for (int s = 0; s < STAGES - 1; ++s) {
-    if (s < ntiles) load_tile(s);
+  if (!prefetched) {
+    load_q_rows<QT>(p, seq, h0, nh, q_s);
     cp_async_commit();
+#pragma unroll
+    for (int s = 0; s < STAGES - 1; ++s) {
+      if (s < ntiles) load_tile(s);
+      cp_async_commit();
+    }
   }
 
   // ---- query as e4m3 hi + lo B fragments: b0 = d 32kq + 4tig + i, b1 = d 32kq + 16 + 4tig + i
-  const QT* qp = reinterpret_cast<const QT*>(p.q);
-  auto qval = [&](int row, int d) -> float {
-    return row < nh ? to_f32(qp[(int64_t)seq * p.q_sb + (int64_t)(h0 + row) * p.q_sh + d]) : 0.0f;
-  };
+  cp_async_wait<STAGES - 1>();  // the query rows' group (older than the tiles')
+  __syncthreads();
+  auto qval = [&](int row, int d) -> float { return row < nh ? to_f32(q_s[row * D + d]) : 0.0f; };
   float qmax = 0.0f;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -1218,7 +1395,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
     if (it + STAGES - 1 < ntiles) load_tile(it + STAGES - 1);
     cp_async_commit();
 
-    const int stage = it % STAGES;
+    const int stage = (gt + it) % STAGES;
     const uint32_t kbase = smem_u32(smem + stage * STAGE_BYTES);
     const uint32_t vbase = kbase + TILE_BYTES;
     const uint8_t* vld = valid + stage * kF8Tile;
@@ -1337,18 +1514,50 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       }
     }
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  gt += ntiles;
+
+  // ---- hand over to the next segment, then merge this one
+  const Seg done = sched.cur;
+  uint8_t* scratch = smem;
+  if (kPrefetch) {
+    has = sched_next<kF8Tile>(p, sched);  // its barrier: every warp is done with the ring
+    prefetched = false;
+    if (has) {
+      const TokRange nr{sched.cur.begin, sched.cur.end};
+      const int nkvh = sched.cur.y / p.head_groups;
+      const int nhg = sched.cur.y - nkvh * p.head_groups;
+      const int nt2 = (nr.end - nr.begin + kF8Tile - 1) / kF8Tile;
+      slice = stage_block_table(p, sched.cur.seq, nr, bt_s, nkvh == 0 && nhg == 0);
+      __syncthreads();
+      load_q_rows<QT>(p, sched.cur.seq, nkvh * p.group + nhg * p.heads_per_cta,
+                      min(p.heads_per_cta, p.group - nhg * p.heads_per_cta), q_s);
+      cp_async_commit();
+#pragma unroll
+      for (int s = 0; s < STAGES - 1; ++s) {
+        if (s < nt2) {
+          uint8_t* kd = smem + ((gt + s) % STAGES) * STAGE_BYTES;
+          load_kv_tile<kF8Tile, ROWB>(p, sched.cur.seq, slice, bt_s, nr, nr.begin + s * kF8Tile,
+                                      kd, kd + TILE_BYTES, valid + ((gt + s) % STAGES) * kF8Tile,
+                                      row_stride, (int64_t)nkvh * ROWB, one_page_per_tile);
+        }
+        cp_async_commit();
+      }
+      prefetched = true;
+    }
+    scratch = smem + ((gt + STAGES - 1) % STAGES) * STAGE_BYTES;  // stage of the last tile
+  } else {
+    cp_async_wait<0>();
+    __syncthreads();
+  }
 
   // ---- merge the 4 warps (reference q_ref plays the role of m; the x256 cancels)
   constexpr int RP = D + 4;
   constexpr int HC = 8 * NT;
-  float* red_acc = reinterpret_cast<float*>(smem);
+  float* red_acc = reinterpret_cast<float*>(scratch);
   float* red_m = red_acc + 4 * HC * RP;
   float* red_l = red_m + 4 * HC;
   float* m_s = red_l + 4 * HC;
   float* l_s = m_s + HC;
-  float* wts = l_s + HC;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1392,7 +1601,8 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
     red_acc[h * RP + d] = O;
   }
   __syncthreads();
-  finish_cta<QT>(p, sched.cur, h0, nh, red_acc, RP, m_s, l_s, wts);
+  finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s);
+  if (!kPrefetch) has = sched_next<kF8Tile>(p, sched);
   }
 }
 
@@ -1439,10 +1649,8 @@ SplitPlan plan_splits(int num_seqs, int num_kv_heads, int head_groups, int block
 
 int head_groups_for(int group) { return (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta; }
 
-// Balanced schedule bounds: at most kMaxResident CTAs (B200: 148 SMs x 4), each with at
-// least kMinCtaTokens tokens of work.
+// Balanced schedule bound: at most kMaxResident CTAs (B200: 148 SMs x 4).
 constexpr int kMaxResident = kNumSMs * 4;
-constexpr int kMinCtaTokens = 256;
 
 // The balanced schedule serves num_splits = 0 unless its work-item arithmetic
 // (W * G < 2^62 with W <= units * (cap / 32 + 1)) could overflow.
@@ -1454,13 +1662,14 @@ bool use_balanced(int num_seqs, int num_kv_heads, int head_groups, int block_siz
   return items * kMaxResident < 4.0e18;
 }
 
-// Work items per CTA at least: enough tokens to amortise a pipeline fill, and few enough
-// CTAs per unit that a unit has at most kMaxSplits partials (the merge-weight buffer).
+// Work items per CTA at least: few enough CTAs per unit that a unit has at most
+// kMaxSplits partials (bounding the merge's work). No larger minimum: a persistent CTA
+// without work exits at once, while fewer CTAs would serialise small units (256
+// one-token sequences: 30.4 us with >= 256 tokens per CTA, 8 us with one tile).
 int min_tiles_for(int tile, int block_size, int max_blocks) {
   const int64_t cap_tiles = ((int64_t)max_blocks * block_size + tile - 1) / tile;
   const int64_t by_merge = (cap_tiles + kMaxSplits - 3) / (kMaxSplits - 2);
-  const int64_t by_fill = (kMinCtaTokens + tile - 1) / tile;
-  return (int)(by_merge > by_fill ? by_merge : by_fill);
+  return (int)(by_merge > 1 ? by_merge : 1);
 }
 
 // Workspace layout (each part 256-byte aligned): partial accumulators, partial (m, l),
@@ -1680,6 +1889,10 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.q = query;
   p.q_sb = q_sb;
   p.q_sh = q_sh;
+  {
+    const int64_t qeb = q_dtype == MKV_DTYPE_F32 ? 4 : 2;
+    p.q_vec16 = ((uintptr_t)query % 16 == 0) && (q_sb * qeb) % 16 == 0 && (q_sh * qeb) % 16 == 0;
+  }
   p.k_cache = (const uint8_t*)k_cache;
   p.v_cache = (const uint8_t*)v_cache;
   p.num_blocks = num_blocks;
@@ -1795,6 +2008,16 @@ int noalloc_scratch(int device, void** out) {
 }  // namespace mkv
 
 using namespace mkv;
+
+#ifdef MKV_DECODE_TRACE
+extern "C" MKV_API int mkv_debug_decode_trace(void* host, int clear) {
+  if (clear) {
+    static unsigned long long zeros[kNumSMs * 4][kTraceEvents];
+    return (int)cudaMemcpyToSymbol(g_dtrace, zeros, sizeof(zeros));
+  }
+  return (int)cudaMemcpyFromSymbol(host, g_dtrace, sizeof(g_dtrace));
+}
+#endif
 
 extern "C" int32_t mkv_paged_decode_num_splits(int32_t num_seqs, int32_t num_heads,
                                                int32_t num_kv_heads, int32_t head_dim,
