@@ -133,6 +133,30 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
 _calib_work: dict[int, torch.Tensor] = {}
 
 
+_calibration_suspended = 0
+
+
+class fp8_calibration_suspended:
+    """Context manager: FP8 appends inside it quantise with the scales as they are and do
+    not calibrate a scale that still holds the 1.0 sentinel.
+
+    For a model runner's eager warm-up before CUDA-graph capture. The reference runner
+    (model_runner.py:783-795) calls the model once on dummy decode inputs before
+    capturing, which would otherwise calibrate the per-tensor scale from dummy K/V and
+    freeze it. The capture itself records the calibration kernel as usual, so the first
+    replay on real data still calibrates. Nests; not tied to a thread or stream."""
+
+    def __enter__(self):
+        global _calibration_suspended
+        _calibration_suspended += 1
+        return self
+
+    def __exit__(self, *exc):
+        global _calibration_suspended
+        _calibration_suspended -= 1
+        return False
+
+
 def _calibration_work(device: torch.device) -> torch.Tensor:
     """Per-device 16-byte scratch of the FP8 calibration kernel (zero between calls)."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
@@ -176,11 +200,12 @@ def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
     with _on_device(dev):
         stream = _stream(dev)
         work = _calibration_work(dev)
-        st = lib.mkv_calibrate_fp8_scales(
-            key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
-            value.stride(1), num_tokens, num_kv_heads, head_dim, dt, k_scale.data_ptr(),
-            v_scale.data_ptr(), work.data_ptr(), stream)
-        _lib.check("mkv_calibrate_fp8_scales", st)
+        if not _calibration_suspended:
+            st = lib.mkv_calibrate_fp8_scales(
+                key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
+                value.stride(1), num_tokens, num_kv_heads, head_dim, dt, k_scale.data_ptr(),
+                v_scale.data_ptr(), work.data_ptr(), stream)
+            _lib.check("mkv_calibrate_fp8_scales", st)
         st = lib.mkv_store_kvcache_fp8(
             key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
             value.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_scale.data_ptr(),

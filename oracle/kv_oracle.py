@@ -70,6 +70,58 @@ def store_kvcache_fp8_ref(key, value, k_cache, v_cache, k_scale, v_scale, slot_m
     store_kvcache_ref(kq, vq, k_cache, v_cache, slot_mapping, block_size)
 
 
+INT8_MAX, INT8_MIN = 127.0, -128.0  # attention.py:114-115
+
+
+def per_token_head_scales_ref(x: torch.Tensor, mode: str) -> torch.Tensor:
+    """Per-(token, kv head) scales of the dynamic quantisers, float32, shape x.shape[:-1]:
+      fp8:  attention.py:170-175  amax = max|x| over head_dim; scale = amax / 448 when
+            amax > 0, else 1.0 (a NaN amax also gives 1.0: NaN > 0 is false);
+      int8: attention.py:231-234  scale = maximum(amax / 127, 1e-6) (tl.maximum keeps the
+            non-NaN operand, so a NaN amax gives 1e-6).
+    Divisions are the correctly rounded float32 quotient."""
+    a = x.float().abs().amax(dim=-1)
+    if mode == "fp8":
+        q = a / torch.tensor(FP8_E4M3_MAX, dtype=torch.float32)
+        return torch.where(a > 0, q, torch.ones_like(q))
+    q = a / torch.tensor(INT8_MAX, dtype=torch.float32)
+    lo = torch.tensor(1e-6, dtype=torch.float32)
+    return torch.where(torch.isnan(q), lo, torch.maximum(q, lo))
+
+
+def quantize_int8_ref(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """attention.py:240-247: q = x * (1 / scale) in float32 (reciprocal first, as written),
+    rounded half away from zero by adding +-0.5 and truncating toward zero on the int8
+    store, after clamping to [-128, 127]. `scale` broadcasts over head_dim."""
+    inv = torch.tensor(1.0, dtype=torch.float32) / scale.float()
+    q = x.float() * inv.unsqueeze(-1)
+    q = torch.where(q >= 0, q + 0.5, q - 0.5)
+    q = q.clamp(INT8_MIN, INT8_MAX)
+    return torch.trunc(q).to(torch.int8)
+
+
+def store_kvcache_quant_per_token_head_ref(key, value, k_cache, v_cache, k_scales, v_scales,
+                                           slot_mapping, block_size, mode):
+    """store_kvcache_fp8 with kv_cache_dtype 'fp8_per_token_head' (attention.py:118-191 with
+    PER_TOKEN_HEAD=1, wrapper 281-333) and store_kvcache_int8 (attention.py:195-278): each
+    (token, kv head) row gets its own scale, written to k_scales/v_scales (num_blocks,
+    block_size, num_kv_heads) at the token's slot, and is quantised with it (FP8:
+    clamp(x / scale) -> e4m3 as in quantize_fp8_ref; INT8: quantize_int8_ref)."""
+    num_tokens, num_kv_heads, head_dim = key.shape
+    slots = slot_mapping.reshape(-1).long()
+    keep = slots != -1
+    for x, cache, scales in ((key, k_cache, k_scales), (value, v_cache, v_scales)):
+        sc = per_token_head_scales_ref(x, mode)  # (T, KVH)
+        if mode == "fp8":
+            q = x.float() / sc.unsqueeze(-1)
+            q = torch.where(torch.isnan(q), torch.full_like(q, -FP8_E4M3_MAX), q)
+            q = q.clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
+        else:
+            q = quantize_int8_ref(x, sc)
+        cache.view(-1, num_kv_heads, head_dim)[slots[keep]] = q[keep].view(cache.dtype)
+        scales.view(-1, num_kv_heads)[slots[keep]] = sc[keep]
+
+
 def e4m3_encode_reference(x: np.ndarray) -> np.ndarray:
     """Independent float32 -> E4M3 (OCP 'fn' variant) byte encoder, written from the
     format definition, used to pin torch's conversion: 1 sign bit, 4 exponent bits
@@ -136,7 +188,7 @@ def decode_torch_optimized(q, k_cache, v_cache, block_tables, context_lens, scal
 
 def paged_decode_ref(query, k_cache, v_cache, block_tables, context_lens, scale, num_heads,
                      num_kv_heads, head_dim, block_size, k_scale=None, v_scale=None,
-                     compute_dtype=torch.float64):
+                     compute_dtype=torch.float64, k_scales=None, v_scales=None):
     """Token-level restatement of paged_attention_decode_kernel (attention.py:517-646)
     and, with k_scale/v_scale, paged_attention_decode_fp8_kernel with PER_TOKEN_HEAD=0
     (attention.py:953-1121), evaluated in `compute_dtype`:
@@ -144,7 +196,10 @@ def paged_decode_ref(query, k_cache, v_cache, block_tables, context_lens, scale,
       * token t < context_len is visible when its logical block t // block_size is
         < max_num_blocks (581, 1040) and its page block_tables[b, t // block_size]
         is not -1 (586, 1045); invisible tokens carry no weight;
-      * FP8 values are dequantised as float(x) * scale (1051-1062, 1098-1107);
+      * FP8 values are dequantised as float(x) * scale (1051-1062, 1098-1107); with
+        per-token scales k_scales/v_scales (num_blocks, block_size, num_kv_heads) an
+        FP8 or INT8 value at (page, row, kv head) is float(x) * scales[page, row, head]
+        (per_token_head modes: 1054-1062, 1098-1107 and the tile kernel 1124-1210);
       * out = sum_t softmax(scale * q.k_t) v_t; a sequence with no visible token gives
         0/0 = NaN, like the kernel's acc / l_i with l_i = 0 (642, 1119).
     Returns (B, H, D) in compute_dtype."""
@@ -157,6 +212,9 @@ def paged_decode_ref(query, k_cache, v_cache, block_tables, context_lens, scale,
     if k_scale is not None:
         kc = kc * float(k_scale.reshape(-1)[0])
         vc = vc * float(v_scale.reshape(-1)[0])
+    if k_scales is not None:
+        kc = kc * k_scales.to(compute_dtype).unsqueeze(-1)
+        vc = vc * v_scales.to(compute_dtype).unsqueeze(-1)
     out = torch.empty(batch, num_heads, head_dim, dtype=compute_dtype)
     for b in range(batch):
         n = max(0, min(int(context_lens[b]), max_blocks * block_size))

@@ -23,6 +23,12 @@ What runs, per fixture (all on the CPU):
   decode_config1   decode_torch_optimized (benchmark_decoding.py:145-198, loaded from
                    the file's source text because the module's imports are stale) on
                    B=4, H=16, KVH=8, D=128, BS=16, ctx ~ U[64, 512]
+  append_fp8_pth   store_kvcache_fp8(..., 'fp8_per_token_head') (attention.py:118-191,
+                   PER_TOKEN_HEAD=1) on float32 "caches": per-(slot, head) scales and
+                   pre-cast quotients
+  append_int8      store_kvcache_int8 (attention.py:195-278): int8 bytes and scales
+  decode_fp8_pth,  paged_attention_decode_quantized with 'fp8_per_token_head' /
+  decode_int8      'int8_per_token_head' (the tile kernel, attention.py:1124-1210)
 """
 from __future__ import annotations
 
@@ -113,6 +119,75 @@ def make_append_fp8(ref_attn, rng):
     return out
 
 
+def _pth_rows(rng, T, KVH, D):
+    """bf16 K/V rows with 1% outliers x20, plus an all-zero row and a row of ties."""
+    import torch
+    x = rng.standard_normal((2, T, KVH, D)).astype(np.float32)
+    x = np.where(rng.random((2, T, KVH, D)) < 0.01, x * 20.0, x)
+    x[:, 5, 1, :] = 0.0                      # amax 0: FP8 scale 1.0, INT8 scale 1e-6
+    x[:, 9, 0, :] = np.tile([2.5, -2.5, 0.5, -127.0], D // 4)  # exact halves after scaling
+    return torch.from_numpy(x[0]).to(torch.bfloat16), torch.from_numpy(x[1]).to(torch.bfloat16)
+
+
+def make_append_pth(ref_attn, rng, mode):
+    """store_kvcache_fp8(..., 'fp8_per_token_head') or store_kvcache_int8 on 24 tokens.
+    FP8 runs with float32 "caches" (see append_fp8) and keeps the pre-cast quotients;
+    INT8 writes int8 caches directly (the interpreter's float->int8 conversion truncates
+    toward zero, as the GPU's does)."""
+    import torch
+    T, KVH, D, NB, BS = 24, 2, 32, 8, 4
+    key, value = _pth_rows(rng, T, KVH, D)
+    slots = torch.from_numpy(rng.permutation(NB * BS)[:T].astype(np.int64))
+    slots[[1, 7]] = -1
+    ks = torch.full((NB, BS, KVH), -1.0, dtype=torch.float32)  # -1 marks slots not written
+    vs = torch.full((NB, BS, KVH), -1.0, dtype=torch.float32)
+    if mode == "fp8":
+        kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float32)
+        vc = torch.zeros(NB, BS, KVH, D, dtype=torch.float32)
+        ref_attn.store_kvcache_fp8(key, value, kc, vc, ks, vs, slots, BS, "fp8_per_token_head")
+        caches = dict(k_quot=kc.numpy(), v_quot=vc.numpy())
+    else:
+        kc = torch.zeros(NB, BS, KVH, D, dtype=torch.int8)
+        vc = torch.zeros(NB, BS, KVH, D, dtype=torch.int8)
+        ref_attn.store_kvcache_int8(key, value, kc, vc, ks, vs, slots, BS)
+        caches = dict(k_cache=kc.numpy(), v_cache=vc.numpy())
+    return dict(key=_bf16_bits(key), value=_bf16_bits(value), slot_mapping=slots.numpy(),
+                k_scales=ks.numpy(), v_scales=vs.numpy(), block_size=np.int64(BS), **caches)
+
+
+def make_decode_pth(ref_attn, rng, mode):
+    """paged_attention_decode_quantized(..., 'fp8_per_token_head' | 'int8_per_token_head')
+    with head_dim <= 128, i.e. the reference's tile kernel (attention.py:1124-1210): FP8
+    codes held in float32 caches (the kernel converts loads to float32 either way), INT8
+    caches as int8, per-(page, row, kv head) scales. No -1 page lies inside a context
+    (that kernel would give such tokens score 0 rather than skip them)."""
+    import torch
+    B, H, KVH, D, BS, MAXB = 4, 8, 2, 32, 8, 6
+    lens = [5, 48, 20, 33]
+    q, kc, vc, bt, cl = _paged_inputs(rng, B, H, KVH, D, BS, lens, MAXB)
+    NB = kc.shape[0]
+    ks = (rng.random((NB, BS, KVH)) * 0.04 + 0.005).astype(np.float32)
+    vs = (rng.random((NB, BS, KVH)) * 0.04 + 0.005).astype(np.float32)
+    if mode == "fp8":
+        k = torch.from_numpy(kc * 40).to(torch.float8_e4m3fn)
+        v = torch.from_numpy(vc * 40).to(torch.float8_e4m3fn)
+        kin, vin = k.float(), v.float()
+        codes = dict(k_cache_e4m3=k.view(torch.uint8).numpy(), v_cache_e4m3=v.view(torch.uint8).numpy())
+        kvd = "fp8_per_token_head"
+    else:
+        kin = torch.from_numpy(np.clip(np.rint(kc * 40), -128, 127).astype(np.int8))
+        vin = torch.from_numpy(np.clip(np.rint(vc * 40), -128, 127).astype(np.int8))
+        codes = dict(k_cache_i8=kin.numpy(), v_cache_i8=vin.numpy())
+        kvd = "int8_per_token_head"
+    scale = 1.0 / np.sqrt(D)
+    out = ref_attn.paged_attention_decode_quantized(
+        torch.from_numpy(q), kin, vin, torch.from_numpy(ks), torch.from_numpy(vs),
+        torch.from_numpy(bt), torch.from_numpy(cl), float(scale), H, KVH, D, BS, kvd)
+    return dict(query=q, k_scales=ks, v_scales=vs, block_tables=bt, context_lens=cl,
+                scale=np.float64(scale), num_heads=np.int64(H), num_kv_heads=np.int64(KVH),
+                block_size=np.int64(BS), out=out.numpy(), **codes)
+
+
 def _paged_inputs(rng, B, H, KVH, D, BS, lens, max_blocks, extra_blocks=3):
     import torch
     need = [(n + BS - 1) // BS for n in lens]
@@ -195,6 +270,7 @@ def make_decode_config1(decode_torch_optimized):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--only", default="", help="comma-separated fixture names")
     args = ap.parse_args()
     ref_attn, dto = _load_reference(args.reference_src)
     jobs = [
@@ -203,8 +279,15 @@ def main():
         ("decode_small", lambda: make_decode_small(ref_attn, np.random.default_rng(303))),
         ("decode_fp8", lambda: make_decode_fp8(ref_attn, np.random.default_rng(404))),
         ("decode_config1", lambda: make_decode_config1(dto)),
+        ("append_fp8_pth", lambda: make_append_pth(ref_attn, np.random.default_rng(505), "fp8")),
+        ("append_int8", lambda: make_append_pth(ref_attn, np.random.default_rng(606), "int8")),
+        ("decode_fp8_pth", lambda: make_decode_pth(ref_attn, np.random.default_rng(707), "fp8")),
+        ("decode_int8", lambda: make_decode_pth(ref_attn, np.random.default_rng(808), "int8")),
     ]
+    only = set(args.only.split(",")) if args.only else None
     for name, job in jobs:
+        if only and name not in only:
+            continue
         data = job()
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **data)

@@ -220,3 +220,50 @@ def test_config2_append_fp8_bit_exact():
     assert float(ks) == float(eks) and float(vs) == float(evs)
     assert torch.equal(kc.cpu().view(torch.uint8), ek.view(torch.uint8))
     assert torch.equal(vc.cpu().view(torch.uint8), ev.view(torch.uint8))
+
+
+def test_fp8_capture_warmup_does_not_calibrate():
+    """A runner's eager warm-up on dummy inputs inside fp8_calibration_suspended() leaves the
+    sentinel scale alone; the graph captured afterwards calibrates on its first replay with
+    real K/V, and later replays keep that scale."""
+    T, KVH, D, BS, NB = 8, 4, 128, 16, 8
+    g = torch.Generator().manual_seed(3)
+    kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float8_e4m3fn, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.ones(1, dtype=torch.float32, device="cuda")
+    vs = torch.ones(1, dtype=torch.float32, device="cuda")
+    key = torch.zeros(T, KVH, D, dtype=torch.bfloat16, device="cuda")
+    val = torch.zeros_like(key)
+    slots = torch.arange(T, dtype=torch.int64, device="cuda")
+
+    def step():
+        attn.store_kvcache_fp8(key, val, kc, vc, ks, vs, slots, BS, "fp8_per_tensor")
+
+    key.copy_(torch.randn(T, KVH, D, generator=g).to(torch.bfloat16))  # dummy warm-up data
+    with attn.fp8_calibration_suspended():
+        step()
+    torch.cuda.synchronize()
+    assert float(ks) == 1.0 and float(vs) == 1.0
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s), attn.fp8_calibration_suspended():
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize()
+    assert float(ks) == 1.0  # capture runs nothing
+    real_k = torch.randn(T, KVH, D, generator=g) * 3.0
+    real_v = torch.randn(T, KVH, D, generator=g) * 0.5
+    key.copy_(real_k.to(torch.bfloat16))
+    val.copy_(real_v.to(torch.bfloat16))
+    graph.replay()
+    torch.cuda.synchronize()
+    want_k = float((key.abs().amax().float() * (1.0 / 448.0)).to(torch.bfloat16))
+    want_v = float((val.abs().amax().float() * (1.0 / 448.0)).to(torch.bfloat16))
+    assert float(ks) == want_k and float(vs) == want_v
+    key.mul_(10)
+    graph.replay()
+    torch.cuda.synchronize()
+    assert float(ks) == want_k  # frozen after the first calibration

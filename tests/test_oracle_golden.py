@@ -6,7 +6,9 @@ import torch
 
 from conftest import golden
 from oracle import (decode_torch_optimized, e4m3_encode_reference, fp8_scale_ref,
-                    paged_decode_ref, quantize_fp8_ref, store_kvcache_fp8_ref, store_kvcache_ref)
+                    paged_decode_ref, per_token_head_scales_ref, quantize_fp8_ref,
+                    store_kvcache_fp8_ref, store_kvcache_quant_per_token_head_ref,
+                    store_kvcache_ref)
 
 
 def bf16(a):
@@ -122,3 +124,81 @@ def test_decode_config1_oracles_match_reference():
     ref = torch.from_numpy(g["out"])
     assert torch.allclose(decode_torch_optimized(*args), ref, atol=1e-6, rtol=1e-6)
     assert torch.allclose(paged_decode_ref(*args).float(), ref, atol=2e-6, rtol=1e-5)
+
+
+# ------------------------------------------------------------- per-(token, head) modes
+def _pth_written(g):
+    slots = torch.from_numpy(g["slot_mapping"])
+    return slots, slots != -1
+
+
+def test_fp8_per_token_head_scales_and_quotients_match_reference():
+    """Per-row scales (amax / 448, 1.0 for the all-zero row) and the kernel's pre-cast
+    clamp(x / scale) equal the oracle's at every written slot; unwritten slots stay."""
+    g = golden("append_fp8_pth")
+    slots, keep = _pth_written(g)
+    for name, sk, qk in (("key", "k_scales", "k_quot"), ("value", "v_scales", "v_quot")):
+        x = bf16(g[name])
+        T, KVH, D = x.shape
+        sc = per_token_head_scales_ref(x, "fp8")
+        ref_sc = torch.from_numpy(g[sk]).view(-1, KVH)
+        assert torch.equal(sc[keep], ref_sc[slots[keep]])
+        assert int((ref_sc == -1.0).all(dim=1).sum()) == ref_sc.shape[0] - int(keep.sum())
+        assert float(sc[5, 1]) == 1.0  # all-zero row
+        quot = (x.float() / sc.unsqueeze(-1)).clamp(-448.0, 448.0)
+        ref_q = torch.from_numpy(g[qk]).view(-1, KVH, D)[slots[keep]]
+        assert torch.equal(quot[keep], ref_q)
+
+
+def test_fp8_per_token_head_store_end_to_end():
+    g = golden("append_fp8_pth")
+    slots, keep = _pth_written(g)
+    shape = g["k_quot"].shape
+    kc = torch.zeros(shape, dtype=torch.float8_e4m3fn)
+    vc = torch.zeros(shape, dtype=torch.float8_e4m3fn)
+    ks = torch.full(shape[:3], -1.0)
+    vs = torch.full(shape[:3], -1.0)
+    store_kvcache_quant_per_token_head_ref(bf16(g["key"]), bf16(g["value"]), kc, vc, ks, vs, slots,
+                                           int(g["block_size"]), "fp8")
+    assert torch.equal(ks, torch.from_numpy(g["k_scales"]))
+    assert torch.equal(vs, torch.from_numpy(g["v_scales"]))
+    exp_k = torch.from_numpy(g["k_quot"]).to(torch.float8_e4m3fn)
+    assert torch.equal(kc.view(torch.uint8), exp_k.view(torch.uint8))
+
+
+def test_int8_store_matches_reference():
+    """INT8 bytes and scales bit-exact, including the all-zero row (scale 1e-6) and a row
+    of exact halves rounded away from zero."""
+    g = golden("append_int8")
+    slots, keep = _pth_written(g)
+    kc = torch.zeros(g["k_cache"].shape, dtype=torch.int8)
+    vc = torch.zeros_like(kc)
+    ks = torch.full(g["k_scales"].shape, -1.0)
+    vs = torch.full(g["v_scales"].shape, -1.0)
+    store_kvcache_quant_per_token_head_ref(bf16(g["key"]), bf16(g["value"]), kc, vc, ks, vs, slots,
+                                           int(g["block_size"]), "int8")
+    assert torch.equal(kc, torch.from_numpy(g["k_cache"]))
+    assert torch.equal(vc, torch.from_numpy(g["v_cache"]))
+    assert torch.equal(ks, torch.from_numpy(g["k_scales"]))
+    assert torch.equal(vs, torch.from_numpy(g["v_scales"]))
+    x = bf16(g["key"])
+    assert float(per_token_head_scales_ref(x, "int8")[5, 1]) == float(np.float32(1e-6))
+    row = torch.from_numpy(g["k_cache"]).view(-1, x.shape[1], x.shape[2])[int(slots[9])][0]
+    assert row[:4].tolist() == [3, -3, 1, -127]  # 2.5 -> 3, -2.5 -> -3, 0.5 -> 1
+
+
+@pytest.mark.parametrize("mode", ["fp8", "int8"])
+def test_per_token_head_decode_oracle_matches_reference_kernel(mode):
+    g = golden(f"decode_{mode}_pth" if mode == "fp8" else "decode_int8")
+    H, KVH = int(g["num_heads"]), int(g["num_kv_heads"])
+    q = torch.from_numpy(g["query"])
+    if mode == "fp8":
+        kc = torch.from_numpy(g["k_cache_e4m3"]).view(torch.float8_e4m3fn)
+        vc = torch.from_numpy(g["v_cache_e4m3"]).view(torch.float8_e4m3fn)
+    else:
+        kc, vc = torch.from_numpy(g["k_cache_i8"]), torch.from_numpy(g["v_cache_i8"])
+    out = paged_decode_ref(q, kc, vc, torch.from_numpy(g["block_tables"]),
+                           torch.from_numpy(g["context_lens"]), float(g["scale"]), H, KVH,
+                           q.shape[2], int(g["block_size"]), k_scales=torch.from_numpy(g["k_scales"]),
+                           v_scales=torch.from_numpy(g["v_scales"]))
+    assert torch.allclose(out, torch.from_numpy(g["out"]).double(), atol=2e-6, rtol=1e-5)
