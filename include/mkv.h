@@ -55,6 +55,7 @@ extern "C" {
 #define MKV_DTYPE_F16 1
 #define MKV_DTYPE_BF16 2
 #define MKV_DTYPE_FP8_E4M3 3
+#define MKV_DTYPE_INT8 4
 
 /* Integer index types for slot_mapping / block_tables / context_lens. */
 #define MKV_INDEX_I32 0
@@ -136,6 +137,27 @@ MKV_API int mkv_store_kvcache_fp8(const void* key, const void* value,
                           int32_t dtype, int32_t* invalid_count, void* stream);
 
 /*
+ * KV append with a dynamic scale per (token, kv head) row, into an FP8 E4M3 or INT8
+ * cache (cache_dtype MKV_DTYPE_FP8_E4M3 or MKV_DTYPE_INT8). Replaces store_kvcache_fp8
+ * with kv_cache_dtype "fp8_per_token_head" (attention.py:281-333 with the kernel
+ * store_kvcache_fp8_kernel, PER_TOKEN_HEAD=1, attention.py:118-191) and store_kvcache_int8
+ * (attention.py:195-278). For each stored row, with amax = max |x| over head_dim:
+ *   FP8:  scale = amax > 0 ? amax / 448 : 1;  byte = e4m3(clamp(x / scale, -448, 448))
+ *   INT8: scale = max(amax / 127, 1e-6);      q = x * (1 / scale), rounded half away
+ *         from zero, clamped to [-128, 127]
+ * (IEEE float32 division; a row holding NaN gets scale 1 (FP8) or 1e-6 (INT8)).
+ * k_scales/v_scales are float32 (num_blocks, block_size, num_kv_heads); the row's scale
+ * is written at its slot. Slot rules as in mkv_store_kvcache. head_dim must be a
+ * multiple of 16 and at most 512; caches 16-byte aligned.
+ */
+MKV_API int mkv_store_kvcache_quant_per_token_head(
+    const void* key, const void* value, int64_t key_stride_token, int64_t key_stride_head,
+    int64_t value_stride_token, int64_t value_stride_head, void* k_cache, void* v_cache,
+    int32_t cache_dtype, float* k_scales, float* v_scales, int64_t num_blocks,
+    int32_t block_size, const void* slot_mapping, int32_t slot_index_type, int64_t num_tokens,
+    int32_t num_kv_heads, int32_t head_dim, int32_t dtype, int32_t* invalid_count, void* stream);
+
+/*
  * Split count the decode uses for this shape when num_splits = 0 (auto). Returns 0
  * when auto means the balanced schedule: the grid is the kernel's resident CTAs and
  * each takes an equal share of all (sequence, kv head) token tiles, computed on the
@@ -200,6 +222,29 @@ MKV_API int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq, int64_
                          float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
                          void* workspace, size_t workspace_bytes, int32_t num_splits,
                          int32_t* invalid_count, void* stream);
+
+/*
+ * Paged-attention decode over an FP8 E4M3 or INT8 cache (cache_dtype) with one scale
+ * per (page, row, kv head): K = float(k) * k_scales[page, row, kvh], V likewise, with
+ * k_scales/v_scales float32 (num_blocks, block_size, num_kv_heads) as written by
+ * mkv_store_kvcache_quant_per_token_head. Replaces paged_attention_decode_quantized for
+ * kv_cache_dtype "fp8_per_token_head" and "int8_per_token_head" (attention.py:1213-1268;
+ * kernels paged_attention_decode_quantized_tile_kernel, attention.py:1124-1210, and
+ * paged_attention_decode_fp8_kernel with PER_TOKEN_HEAD=1, attention.py:953-1121).
+ * A -1 (or out-of-range) page inside a context is skipped, as the reference's FP8
+ * kernel does (its tile kernel, used for head_dim <= 128, instead scores such tokens
+ * 0 against a zero V). Other arguments as in mkv_paged_decode; the workspace size is
+ * mkv_paged_decode_workspace_bytes(...).
+ */
+MKV_API int mkv_paged_decode_quant_per_token_head(
+    const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t cache_dtype, const float* k_scales,
+    const float* v_scales, int64_t num_blocks, int32_t block_size, const void* block_tables,
+    int32_t block_table_index_type, int64_t block_table_stride_seq, int32_t max_num_blocks,
+    const void* context_lens, int32_t context_lens_index_type, int32_t num_seqs,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
+    int64_t out_stride_seq, int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+    int32_t num_splits, int32_t* invalid_count, void* stream);
 
 /*
  * Paged-attention decode that allocates nothing and needs no workspace argument.

@@ -14,7 +14,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libmkv.so")
 
 # Constants mirrored from include/mkv.h.
-DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_FP8_E4M3 = 0, 1, 2, 3
+DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_FP8_E4M3, DTYPE_INT8 = 0, 1, 2, 3, 4
 INDEX_I32, INDEX_I64 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 FP8_CALIB_WORK_BYTES = 16
@@ -33,6 +33,9 @@ SIGNATURES: dict[str, tuple] = {
         _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p, _p, _p]),
     "mkv_store_kvcache_fp8": (ctypes.c_int, [
         _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _i32, _i32, _p, _p]),
+    "mkv_store_kvcache_quant_per_token_head": (ctypes.c_int, [
+        _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _i32,
+        _i32, _p, _p]),
     "mkv_paged_decode_num_splits": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "mkv_paged_decode_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "mkv_paged_decode": (ctypes.c_int, [
@@ -41,6 +44,9 @@ SIGNATURES: dict[str, tuple] = {
     "mkv_paged_decode_noalloc": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
+    "mkv_paged_decode_quant_per_token_head": (ctypes.c_int, [
+        _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
+        _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),
     "mkv_paged_decode_fp8": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),

@@ -60,6 +60,17 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
   return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
 }
 
+__device__ __forceinline__ float to_f32(int8_t x) { return (float)x; }
+
+// Two int8 bytes (low byte = element 0) -> half2 (x = element 0), exact: each byte,
+// sign-flipped to 0..255, becomes the low mantissa bits of f16 1024 (0x6400), and
+// 1152 = 1024 + 128 is subtracted (f16 is exact on 1024..2047).
+__device__ __forceinline__ uint32_t s8x2_to_f16x2(uint16_t v) {
+  const uint32_t w = __byte_perm((uint32_t)v, 0x64006400u, 0x7150) ^ 0x00800080u;
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&w), __half2(__half(1152.0f), __half(1152.0f)));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
 // Two e4m3 bytes (low byte = element 0) -> half2 (x = element 0), exact.
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
   __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
@@ -94,6 +105,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // without reading global memory.
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+// 4-byte cp.async (L1-allocating form, the only one for sizes below 16); src_bytes 0
+// zero-fills the destination.
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
                "r"(src_bytes)
                : "memory");
 }

@@ -75,6 +75,9 @@ struct DecodeParams {
   float qk_scale_log2;   // attention scale * log2(e)
   const float* k_scale;  // FP8 per-tensor scales (nullptr for float caches)
   const float* v_scale;
+  // per-(page, row, kv head) scales of 8-bit caches, (num_blocks, block_size, kv heads)
+  const float* k_scales;
+  const float* v_scales;
   void* out;
   int64_t o_sb, o_sh;  // elements
   float* part_acc;     // [num_seqs][num_heads][num_splits][head_dim]
@@ -547,7 +550,8 @@ __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
                                              const BlockSlice& slice, const int* bt_s,
                                              const TokRange& rng, int t0, uint8_t* kd,
                                              uint8_t* vd, uint8_t* valid, int64_t row_stride,
-                                             int64_t head_off, bool one_page_per_tile) {
+                                             int64_t head_off, bool one_page_per_tile,
+                                             float* rs = nullptr, int kvh = 0) {
   constexpr int CPR = ROWB / 16;         // 16-byte chunks per row
   constexpr int RPP = kThreads / CPR;    // rows per pass (a multiple of 8)
   constexpr int PASSES = TILE / RPP;
@@ -556,6 +560,21 @@ __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
   // (r & 7) is the same for all of this thread's rows r = ld_r0 + i * RPP
   const uint32_t soff0 = ld_r0 * ROWB + ((ld_c ^ (ld_r0 & 7)) << 4);
   const uint32_t kd0 = smem_u32(kd) + soff0, vd0 = smem_u32(vd) + soff0;
+  // per-token scales of 8-bit pages: thread r < TILE copies row r's K scale, thread
+  // TILE + r its V scale (zero for rows that are not loaded)
+  if (rs != nullptr && tid < 2 * TILE) {
+    const int r = tid < TILE ? tid : tid - TILE;
+    const float* src = tid < TILE ? p.k_scales : p.v_scales;
+    const int t = t0 + r;
+    int page = -1, boff = 0;
+    if (t < rng.end) {
+      int blk;
+      split_token(p, t, blk, boff);
+      page = slice_page(p, seq, slice, bt_s, blk);
+    }
+    const int64_t idx = page >= 0 ? ((int64_t)page * p.block_size + boff) * p.num_kv_heads + kvh : 0;
+    cp_async_4(smem_u32(rs + tid), src + idx, page >= 0 ? 4 : 0);
+  }
   if (one_page_per_tile) {
     const int page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
     const int nrows = page >= 0 ? min(TILE, rng.end - t0) : 0;
@@ -634,7 +653,7 @@ __global__ void __launch_bounds__(kThreads)
 paged_decode_generic_kernel(const DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int EB = sizeof(CT);
-  constexpr bool kFp8 = std::is_same<CT, fp8>::value;
+  constexpr bool kByte = sizeof(CT) == 1;  // e4m3 or int8 pages
   constexpr int kPer = 16 / EB;  // elements per 16-byte chunk
   const int D = p.head_dim;
   const int row_bytes = D * EB;
@@ -652,6 +671,8 @@ paged_decode_generic_kernel(const DecodeParams p) {
   float* a_s = l_s + kMaxHeadsPerCta;                              // [16]
   uint8_t* valid = reinterpret_cast<uint8_t*>(a_s + kMaxHeadsPerCta);  // [2][kGenTile]
   int* bt_s = reinterpret_cast<int*>(valid + 2 * kGenTile);        // [kMaxBtSmem]
+  float* rs_s = reinterpret_cast<float*>(bt_s + kMaxBtSmem);       // [2][2][kGenTile] row scales
+  const bool per_token = p.k_scales != nullptr;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ SchedState sched;
@@ -667,7 +688,7 @@ paged_decode_generic_kernel(const DecodeParams p) {
 
   const BlockSlice slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
 
-  const float ks = kFp8 ? __ldg(p.k_scale) : 1.0f;
+  const float ks = (kByte && !per_token) ? __ldg(p.k_scale) : 1.0f;
   const float qscale = p.qk_scale_log2 * ks;
   const QT* qp = reinterpret_cast<const QT*>(p.q);
   for (int i = tid; i < kMaxHeadsPerCta * D; i += kThreads) {
@@ -700,7 +721,15 @@ paged_decode_generic_kernel(const DecodeParams p) {
           ok ? ((int64_t)page * p.block_size + boff) * row_stride + head_off + c * 16 : 0;
       cp_async_16(smem_u32(kd + r * row_pitch + c * 16), p.k_cache + off, ok ? 16 : 0);
       cp_async_16(smem_u32(vd + r * row_pitch + c * 16), p.v_cache + off, ok ? 16 : 0);
-      if (c == 0) valid[stage * kGenTile + r] = ok ? 1 : 0;
+      if (c == 0) {
+        valid[stage * kGenTile + r] = ok ? 1 : 0;
+        if (per_token) {
+          const int64_t si = ok ? ((int64_t)page * p.block_size + boff) * p.num_kv_heads + kvh : 0;
+          float* rs = rs_s + stage * 2 * kGenTile;
+          cp_async_4(smem_u32(rs + r), p.k_scales + si, ok ? 4 : 0);
+          cp_async_4(smem_u32(rs + kGenTile + r), p.v_scales + si, ok ? 4 : 0);
+        }
+      }
     }
   };
 
@@ -724,6 +753,7 @@ paged_decode_generic_kernel(const DecodeParams p) {
     const uint8_t* kt = kbuf + stage * kGenTile * row_pitch;
     const uint8_t* vt = vbuf + stage * kGenTile * row_pitch;
     const uint8_t* vld = valid + stage * kGenTile;
+    const float* rs = rs_s + stage * 2 * kGenTile;  // row scales (per_token only)
 
     // scores: warp -> head, lane -> token
     for (int h = warp; h < nh; h += kThreads / 32) {
@@ -736,6 +766,7 @@ paged_decode_generic_kernel(const DecodeParams p) {
 #pragma unroll
         for (int j = 0; j < kPer; ++j) s = fmaf(qh[c * kPer + j], to_f32(e[j]), s);
       }
+      if (per_token) s *= rs[lane];
       s_s[h * kGenTile + lane] = vld[lane] ? s : -INFINITY;
     }
     __syncthreads();
@@ -767,7 +798,8 @@ paged_decode_generic_kernel(const DecodeParams p) {
         for (int h = 0; h < kMaxHeadsPerCta; ++h)
           if (h < nh) acc[h][j] *= a_s[h];
         for (int r = 0; r < kGenTile; ++r) {
-          const float v = to_f32(reinterpret_cast<const CT*>(vt + r * row_pitch)[d]);
+          float v = to_f32(reinterpret_cast<const CT*>(vt + r * row_pitch)[d]);
+          if (per_token) v *= rs[kGenTile + r];
 #pragma unroll
           for (int h = 0; h < kMaxHeadsPerCta; ++h)
             if (h < nh) acc[h][j] = fmaf(s_s[h * kGenTile + r], v, acc[h][j]);
@@ -801,24 +833,36 @@ size_t generic_smem_bytes(int head_dim, int elem_bytes) {
   const size_t epi = (size_t)kMaxHeadsPerCta * head_dim * 4;
   return (ring > epi ? ring : epi) + (size_t)kMaxHeadsPerCta * head_dim * 4 +
          (size_t)kMaxHeadsPerCta * kGenTile * 4 + 3 * kMaxHeadsPerCta * 4 + 2 * kGenTile +
-         kMaxBtSmem * 4;
+         kMaxBtSmem * 4 + 2 * 2 * kGenTile * 4;
 }
 
 // ============================================================ tensor-core kernel
 // head_dim = 128; query bf16 with bf16 pages, f16 with f16 pages, or bf16/f16 with
 // e4m3 pages (f16 MMAs). NT = query heads of the CTA in units of 8 (MMA N tiles).
+// MMA operand type of a page type; 8-bit pages (e4m3, int8) are converted to f16 in
+// registers, two elements per conversion.
 template <typename CT> struct TcTraits;
 template <> struct TcTraits<bf16> {
   using MT = bf16;
-  static constexpr bool kFp8 = false;
+  static constexpr bool kByte = false;
+  // 16-bit pages feed the MMA as they are; the 8-bit branch that calls this is dead
+  static __device__ __forceinline__ uint32_t to_f16x2(uint16_t) { return 0u; }
 };
 template <> struct TcTraits<f16> {
   using MT = f16;
-  static constexpr bool kFp8 = false;
+  static constexpr bool kByte = false;
+  // 16-bit pages feed the MMA as they are; the 8-bit branch that calls this is dead
+  static __device__ __forceinline__ uint32_t to_f16x2(uint16_t) { return 0u; }
 };
 template <> struct TcTraits<fp8> {
   using MT = f16;
-  static constexpr bool kFp8 = true;
+  static constexpr bool kByte = true;
+  static __device__ __forceinline__ uint32_t to_f16x2(uint16_t v) { return e4m3x2_to_f16x2(v); }
+};
+template <> struct TcTraits<int8_t> {
+  using MT = f16;
+  static constexpr bool kByte = true;
+  static __device__ __forceinline__ uint32_t to_f16x2(uint16_t v) { return s8x2_to_f16x2(v); }
 };
 
 
@@ -842,17 +886,20 @@ constexpr size_t tc_front_bytes() {  // ring, reused by the epilogue
   return ring > tc_epilogue_bytes<NT>() ? ring : tc_epilogue_bytes<NT>();
 }
 template <typename CT, int NT, int STAGES>
-constexpr size_t tc_smem_bytes() {  // + valid flags + staged block table + query rows
+constexpr size_t tc_smem_bytes() {  // + valid flags + block table + query rows + row scales
   return tc_front_bytes<CT, NT, STAGES>() + (size_t)STAGES * kTcTile + kMaxBtSmem * 4 +
-         (size_t)8 * NT * kTcD * 2;
+         (size_t)8 * NT * kTcD * 2 + (size_t)STAGES * 2 * kTcTile * 4;
 }
 
-template <typename QT, typename CT, int NT, int STAGES, int MINB>
+// kPT: 8-bit pages with a scale per (page, row, kv head): S^T rows are multiplied by
+// the K scale of their token and P by the V scale before the PV product (the softmax
+// denominator uses the unscaled P).
+template <typename QT, typename CT, int NT, int STAGES, int MINB, bool kPT>
 __global__ void __launch_bounds__(kThreads, MINB)
 paged_decode_tc_kernel(const DecodeParams p) {
   using Tr = TcTraits<CT>;
   using MT = typename Tr::MT;
-  constexpr bool kFp8 = Tr::kFp8;
+  constexpr bool kFp8 = Tr::kByte;  // 8-bit pages (e4m3 or int8), converted to f16
   constexpr int D = kTcD;
   constexpr int EB = sizeof(CT);
   constexpr int ROWB = D * EB;    // 256 (16-bit) or 128 (e4m3) bytes per token row
@@ -864,6 +911,7 @@ paged_decode_tc_kernel(const DecodeParams p) {
   uint8_t* valid = smem + FRONT;                                 // [STAGES][kTcTile]
   int* bt_s = reinterpret_cast<int*>(valid + STAGES * kTcTile);  // [kMaxBtSmem]
   QT* q_s = reinterpret_cast<QT*>(bt_s + kMaxBtSmem);             // [8 * NT][D]
+  float* rs_s = reinterpret_cast<float*>(q_s + 8 * NT * D);       // [STAGES][2][kTcTile]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
@@ -908,7 +956,7 @@ paged_decode_tc_kernel(const DecodeParams p) {
     uint8_t* kd = smem + stage * STAGE_BYTES;
     load_kv_tile<kTcTile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kTcTile, kd,
                                 kd + TILE_BYTES, valid + stage * kTcTile, row_stride, head_off,
-                                one_page_per_tile);
+                                one_page_per_tile, kPT ? rs_s + stage * 2 * kTcTile : nullptr, kvh);
   };
 
   // prologue: the query rows, then STAGES-1 tiles, in flight before the query fragments
@@ -963,7 +1011,7 @@ paged_decode_tc_kernel(const DecodeParams p) {
       qb[nt][ks][1] = pack2<MT>(qval(row, qcol(ks, 1, 0)) * qpow2, qval(row, qcol(ks, 1, 1)) * qpow2);
     }
   MKV_DTRACE(5 + 10 * nseg);
-  const float ksc = kFp8 ? __ldg(p.k_scale) : 1.0f;
+  const float ksc = (kFp8 && !kPT) ? __ldg(p.k_scale) : 1.0f;
   const float sc = p.qk_scale_log2 * ksc / qpow2;
 
   // ---- per-warp softmax state for heads nt*8 + 2tig + e, and O^T accumulators
@@ -1027,15 +1075,31 @@ paged_decode_tc_kernel(const DecodeParams p) {
 #pragma unroll
           for (int hc = 0; hc < 2; ++hc) {
             uint32_t a[4];
-            a[0] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc] & 0xffffu));
-            a[1] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc + 1] & 0xffffu));
-            a[2] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc] >> 16));
-            a[3] = e4m3x2_to_f16x2((uint16_t)(x[2 * hc + 1] >> 16));
+            a[0] = Tr::to_f16x2((uint16_t)(x[2 * hc] & 0xffffu));
+            a[1] = Tr::to_f16x2((uint16_t)(x[2 * hc + 1] & 0xffffu));
+            a[2] = Tr::to_f16x2((uint16_t)(x[2 * hc] >> 16));
+            a[3] = Tr::to_f16x2((uint16_t)(x[2 * hc + 1] >> 16));
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
               Mma<MT>::run(s[nt], a, qb[nt][2 * kq + hc][0], qb[nt][2 * kq + hc][1]);
           }
         }
+      }
+    }
+
+    // ---- per-token scales (kPT): K scale on S^T rows, V scale kept for P
+    float vsc0 = 1.0f, vsc1 = 1.0f;
+    if (kPT) {
+      const float* rs = rs_s + stage * 2 * kTcTile;
+      const float k0 = rs[warp * 16 + g], k1 = rs[warp * 16 + g + 8];
+      vsc0 = rs[kTcTile + warp * 16 + g];
+      vsc1 = rs[kTcTile + warp * 16 + g + 8];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        s[nt][0] *= k0;
+        s[nt][1] *= k0;
+        s[nt][2] *= k1;
+        s[nt][3] *= k1;
       }
     }
 
@@ -1072,8 +1136,8 @@ paged_decode_tc_kernel(const DecodeParams p) {
         }
       }
       // P^T as the B operand (K = tokens, N = heads): transpose the 8x8 blocks
-      pb[nt][0] = movmatrix_trans(pack2<MT>(s[nt][0], s[nt][1]));  // tokens 0-7
-      pb[nt][1] = movmatrix_trans(pack2<MT>(s[nt][2], s[nt][3]));  // tokens 8-15
+      pb[nt][0] = movmatrix_trans(pack2<MT>(s[nt][0] * vsc0, s[nt][1] * vsc0));  // tokens 0-7
+      pb[nt][1] = movmatrix_trans(pack2<MT>(s[nt][2] * vsc1, s[nt][3] * vsc1));  // tokens 8-15
     }
 
     // ---- O^T += V^T P^T, one 16-row (head_dim) M tile per MMA
@@ -1104,10 +1168,10 @@ paged_decode_tc_kernel(const DecodeParams p) {
           const uint32_t ya = __byte_perm(x[2 * hc], 0u, 0x3120);      // tokens 0-7
           const uint32_t yb = __byte_perm(x[2 * hc + 1], 0u, 0x3120);  // tokens 8-15
           uint32_t a[4];
-          a[0] = e4m3x2_to_f16x2((uint16_t)(ya & 0xffffu));
-          a[1] = e4m3x2_to_f16x2((uint16_t)(ya >> 16));
-          a[2] = e4m3x2_to_f16x2((uint16_t)(yb & 0xffffu));
-          a[3] = e4m3x2_to_f16x2((uint16_t)(yb >> 16));
+          a[0] = Tr::to_f16x2((uint16_t)(ya & 0xffffu));
+          a[1] = Tr::to_f16x2((uint16_t)(ya >> 16));
+          a[2] = Tr::to_f16x2((uint16_t)(yb & 0xffffu));
+          a[3] = Tr::to_f16x2((uint16_t)(yb >> 16));
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[nt][2 * cq + hc], a, pb[nt][0], pb[nt][1]);
         }
@@ -1139,7 +1203,9 @@ paged_decode_tc_kernel(const DecodeParams p) {
           uint8_t* kd = smem + ((gt + s) % STAGES) * STAGE_BYTES;
           load_kv_tile<kTcTile, ROWB>(p, sched.cur.seq, slice, bt_s, nr, nr.begin + s * kTcTile,
                                       kd, kd + TILE_BYTES, valid + ((gt + s) % STAGES) * kTcTile,
-                                      row_stride, (int64_t)nkvh * ROWB, one_page_per_tile);
+                                      row_stride, (int64_t)nkvh * ROWB, one_page_per_tile,
+                                      kPT ? rs_s + ((gt + s) % STAGES) * 2 * kTcTile : nullptr,
+                                      nkvh);
         }
         cp_async_commit();
       }
@@ -1785,15 +1851,16 @@ template <typename CT> struct TcConfig;
 template <> struct TcConfig<bf16> { static constexpr int kStages = MKV_TC16_STAGES, kMinBlocks = MKV_TC16_MINB; };
 template <> struct TcConfig<f16> { static constexpr int kStages = MKV_TC16_STAGES, kMinBlocks = MKV_TC16_MINB; };
 template <> struct TcConfig<fp8> { static constexpr int kStages = MKV_TC8_STAGES, kMinBlocks = MKV_TC8_MINB; };
+template <> struct TcConfig<int8_t> { static constexpr int kStages = MKV_TC8_STAGES, kMinBlocks = MKV_TC8_MINB; };
 
-template <typename QT, typename CT, int NT>
+template <typename QT, typename CT, int NT, bool kPT>
 int launch_tc_nt(const DecodeParams& p, cudaStream_t stream, int device) {
   constexpr int S = TcConfig<CT>::kStages, MB = TcConfig<CT>::kMinBlocks;
   constexpr size_t smem = tc_smem_bytes<CT, NT, S>();
-  int st = ensure_smem<paged_decode_tc_kernel<QT, CT, NT, S, MB>>(smem, device);
+  int st = ensure_smem<paged_decode_tc_kernel<QT, CT, NT, S, MB, kPT>>(smem, device);
   if (st != MKV_OK) return st;
-  return launch_decode<paged_decode_tc_kernel<QT, CT, NT, S, MB>>(p, kTcTile, smem, stream, device,
-                                                                  "paged_decode_tc launch");
+  return launch_decode<paged_decode_tc_kernel<QT, CT, NT, S, MB, kPT>>(
+      p, kTcTile, smem, stream, device, "paged_decode_tc launch");
 }
 
 // e4m3 pages with FP8 MMAs: 2 stages x 32 KB (128-token tiles), 3 CTAs/SM.
@@ -1816,15 +1883,16 @@ int launch_fp8mma(const DecodeParams& p, cudaStream_t stream, int device) {
                              : launch_fp8mma_nt<QT, 1>(p, stream, device);
 }
 
-template <typename QT, typename CT>
+template <typename QT, typename CT, bool kPT = false>
 int launch_tc(const DecodeParams& p, cudaStream_t stream, int device) {
-  return p.heads_per_cta > 8 ? launch_tc_nt<QT, CT, 2>(p, stream, device)
-                             : launch_tc_nt<QT, CT, 1>(p, stream, device);
+  return p.heads_per_cta > 8 ? launch_tc_nt<QT, CT, 2, kPT>(p, stream, device)
+                             : launch_tc_nt<QT, CT, 1, kPT>(p, stream, device);
 }
 
 int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, int q_dtype,
                 const void* k_cache, const void* v_cache, int cache_dtype, const float* k_scale,
-                const float* v_scale, int64_t num_blocks, int block_size, const void* bt,
+                const float* v_scale, const float* k_scales, const float* v_scales,
+                int64_t num_blocks, int block_size, const void* bt,
                 int bt_type, int64_t bt_sb, int max_blocks, const void* ctx, int ctx_type,
                 int num_seqs, int num_heads, int num_kv_heads, int head_dim, float scale,
                 void* out, int64_t o_sb, int64_t o_sh, void* workspace, size_t ws_bytes,
@@ -1858,9 +1926,20 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
                      "%s: head_dim must be a multiple of 16 and at most 256 (got %d)", fn,
                      head_dim);
   const bool fp8_cache = cache_dtype == MKV_DTYPE_FP8_E4M3;
-  if (fp8_cache && (!k_scale || !v_scale))
+  const bool per_token = k_scales != nullptr || v_scales != nullptr;
+  if (per_token && (!k_scales || !v_scales))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: both k_scales and v_scales are needed", fn);
+  if (per_token && (((uintptr_t)k_scales & 3u) || ((uintptr_t)v_scales & 3u)))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: scales must be 4-byte aligned", fn);
+  if (per_token && !fp8_cache && cache_dtype != MKV_DTYPE_INT8)
+    return set_error(MKV_ERR_UNSUPPORTED,
+                     "%s: per-token scales need an FP8_E4M3 or INT8 cache (got %d)", fn,
+                     cache_dtype);
+  if (fp8_cache && !per_token && (!k_scale || !v_scale))
     return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: FP8 cache needs k_scale and v_scale", fn);
-  if (!fp8_cache && cache_dtype != q_dtype)
+  if (cache_dtype == MKV_DTYPE_INT8 && !per_token)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: an INT8 cache needs per-token scales", fn);
+  if (!fp8_cache && !per_token && cache_dtype != q_dtype)
     return set_error(MKV_ERR_UNSUPPORTED,
                      "%s: cache dtype (%d) must equal the query dtype (%d) for float caches", fn,
                      cache_dtype, q_dtype);
@@ -1912,8 +1991,10 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.heads_per_cta = hpc;
   p.head_groups = hgs;
   p.qk_scale_log2 = scale * kLog2e;
-  p.k_scale = fp8_cache ? k_scale : nullptr;
-  p.v_scale = fp8_cache ? v_scale : nullptr;
+  p.k_scale = fp8_cache && !per_token ? k_scale : nullptr;
+  p.v_scale = fp8_cache && !per_token ? v_scale : nullptr;
+  p.k_scales = per_token ? k_scales : nullptr;
+  p.v_scales = per_token ? v_scales : nullptr;
   p.out = out;
   p.o_sb = o_sb;
   p.o_sh = o_sh;
@@ -1938,7 +2019,7 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   }
 
   // The tcgen05 kernel (compiled in with MKV_ENABLE_TC05) runs fixed split plans only.
-  if (!balanced && tc05::supported(q_dtype, cache_dtype, head_dim, block_size, hpc)) {
+  if (!balanced && !per_token && tc05::supported(q_dtype, cache_dtype, head_dim, block_size, hpc)) {
     tc05::Params t;
     t.q = query; t.q_sb = q_sb; t.q_sh = q_sh;
     t.num_blocks = num_blocks; t.block_size = block_size; t.bs_shift = p.bs_shift;
@@ -1956,12 +2037,23 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   }
 
   const bool tc_ok = head_dim == kTcD && q_dtype != MKV_DTYPE_F32;
+  if (per_token) {  // 8-bit pages with per-(page, row, kv head) scales
+    const bool i8 = cache_dtype == MKV_DTYPE_INT8;
+    if (tc_ok && q_dtype == MKV_DTYPE_BF16)
+      return i8 ? launch_tc<bf16, int8_t, true>(p, s, device) : launch_tc<bf16, fp8, true>(p, s, device);
+    if (tc_ok && q_dtype == MKV_DTYPE_F16)
+      return i8 ? launch_tc<f16, int8_t, true>(p, s, device) : launch_tc<f16, fp8, true>(p, s, device);
+    switch (q_dtype) {
+      case MKV_DTYPE_F32:
+        return i8 ? launch_generic<float, int8_t>(p, s, device) : launch_generic<float, fp8>(p, s, device);
+      case MKV_DTYPE_F16:
+        return i8 ? launch_generic<f16, int8_t>(p, s, device) : launch_generic<f16, fp8>(p, s, device);
+      default:
+        return i8 ? launch_generic<bf16, int8_t>(p, s, device) : launch_generic<bf16, fp8>(p, s, device);
+    }
+  }
   if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, bf16>(p, s, device);
   if (tc_ok && !fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, f16>(p, s, device);
-#ifdef MKV_FP8_CONVERT_PATH
-  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_tc<bf16, fp8>(p, s, device);
-  if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_tc<f16, fp8>(p, s, device);
-#endif
   if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_BF16) return launch_fp8mma<bf16>(p, s, device);
   if (tc_ok && fp8_cache && q_dtype == MKV_DTYPE_F16) return launch_fp8mma<f16>(p, s, device);
   if (fp8_cache) {
@@ -2059,8 +2151,8 @@ extern "C" int mkv_paged_decode(const void* query, int64_t q_stride_seq, int64_t
     return set_error(MKV_ERR_INVALID_ARGUMENT,
                      "mkv_paged_decode: FP8 caches go through mkv_paged_decode_fp8");
   return decode_impl("mkv_paged_decode", query, q_stride_seq, q_stride_head, q_dtype, k_cache,
-                     v_cache, cache_dtype, nullptr, nullptr, num_blocks, block_size, block_tables,
-                     block_table_index_type, block_table_stride_seq, max_num_blocks, context_lens,
+                     v_cache, cache_dtype, nullptr, nullptr, nullptr, nullptr, num_blocks,
+                     block_size, block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks, context_lens,
                      context_lens_index_type, num_seqs, num_heads, num_kv_heads, head_dim, scale,
                      out, out_stride_seq, out_stride_head, workspace, workspace_bytes, num_splits,
                      invalid_count, stream);
@@ -2079,7 +2171,7 @@ extern "C" int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq,
                                     void* workspace, size_t workspace_bytes, int32_t num_splits,
                                     int32_t* invalid_count, void* stream) {
   return decode_impl("mkv_paged_decode_fp8", query, q_stride_seq, q_stride_head, q_dtype, k_cache,
-                     v_cache, MKV_DTYPE_FP8_E4M3, k_scale, v_scale, num_blocks, block_size,
+                     v_cache, MKV_DTYPE_FP8_E4M3, k_scale, v_scale, nullptr, nullptr, num_blocks, block_size,
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
@@ -2120,10 +2212,35 @@ extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
     if (st != MKV_OK) return st;
   }
   return decode_impl("mkv_paged_decode_noalloc", query, q_stride_seq, q_stride_head, q_dtype,
-                     k_cache, v_cache, cache_dtype, nullptr, nullptr, num_blocks, block_size,
+                     k_cache, v_cache, cache_dtype, nullptr, nullptr, nullptr, nullptr, num_blocks,
+                     block_size,
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, scratch,
                      scratch ? (size_t)MKV_NOALLOC_SCRATCH_BYTES : 0, num_splits, invalid_count,
                      stream);
+}
+
+extern "C" int mkv_paged_decode_quant_per_token_head(
+    const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t cache_dtype, const float* k_scales,
+    const float* v_scales, int64_t num_blocks, int32_t block_size, const void* block_tables,
+    int32_t block_table_index_type, int64_t block_table_stride_seq, int32_t max_num_blocks,
+    const void* context_lens, int32_t context_lens_index_type, int32_t num_seqs,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
+    int64_t out_stride_seq, int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+    int32_t num_splits, int32_t* invalid_count, void* stream) {
+  clear_error();
+  const char* fn = "mkv_paged_decode_quant_per_token_head";
+  if (cache_dtype != MKV_DTYPE_FP8_E4M3 && cache_dtype != MKV_DTYPE_INT8)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: cache_dtype must be FP8_E4M3 or INT8 (got %d)", fn,
+                     cache_dtype);
+  if (num_seqs > 0 && (!k_scales || !v_scales))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: null scale pointer", fn);
+  return decode_impl(fn, query, q_stride_seq, q_stride_head, q_dtype, k_cache, v_cache,
+                     cache_dtype, nullptr, nullptr, k_scales, v_scales, num_blocks, block_size,
+                     block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
+                     context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
+                     head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
+                     workspace_bytes, num_splits, invalid_count, stream);
 }

@@ -1,10 +1,13 @@
 // KV append into block-table pages: same-dtype copy, FP8 E4M3 quantisation with a
-// per-tensor scale, and the device-side sentinel-aware FP8 scale calibration.
+// per-tensor scale, the device-side sentinel-aware FP8 scale calibration, and FP8 /
+// INT8 quantisation with a dynamic scale per (token, kv head) row.
 //
 // Reference behaviour (heart1128/mini-kvllm, src/myvllm/layers/attention.py):
 //   store_kvcache_kernel       attention.py:7-64    cache.view(-1,KVH,D)[slot] = x, slot -1 skipped
-//   store_kvcache_fp8_kernel   attention.py:118-191 e4m3(clamp(x / scale, -448, 448)), per-tensor branch 182-191
+//   store_kvcache_fp8_kernel   attention.py:118-191 e4m3(clamp(x / scale, -448, 448)), per-tensor branch 182-191,
+//                                                   per-(token, head) branch 168-181 (scale = amax / 448)
 //   store_kvcache_fp8 (host)   attention.py:315-323 scale calibrated once from amax while it is 1.0
+//   store_kvcache_int8_kernel  attention.py:195-252 scale = max(amax / 127, 1e-6), round half away
 //
 // B200 design: the append is pure HBM traffic (one read of the new rows, one write
 // into the pages). Each thread moves one 16-byte chunk of a (token, head) row for
@@ -167,6 +170,101 @@ store_kv_fp8_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
                   ((uint32_t)quantize_e4m3(x[4 * w + 3], vs) << 24);
     }
     st_v4(v_cache + dst, make_uint4(packed[0], packed[1], packed[2], packed[3]));
+  }
+}
+
+// -------------------------------------------------------------------- per-(token, head) scales
+// clamp(round-half-away(x * (1 / scale)), -128, 127) as int8: the product and the +-0.5
+// are separately rounded (no fused multiply-add), as the reference computes them.
+__device__ __forceinline__ int8_t quantize_int8(float x, float inv) {
+  float q = __fmul_rn(x, inv);
+  q = q >= 0.0f ? __fadd_rn(q, 0.5f) : __fadd_rn(q, -0.5f);
+  q = fminf(fmaxf(q, -128.0f), 127.0f);
+  return (int8_t)__float2int_rz(q);
+}
+
+// One group of LPR lanes (a power of two >= head_dim / 16) per (token, kv head) row:
+// each lane loads 16 elements of K and of V, the group reduces the row's amax with
+// shuffles, and each lane writes its 16 quantised bytes; lane 0 of the group writes
+// the row's two scales. The loop is warp-uniform so that every lane takes part in the
+// shuffles.
+template <typename T, bool kInt8, typename SlotT>
+__global__ void __launch_bounds__(kStoreThreads)
+store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
+                    int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
+                    uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
+                    float* __restrict__ k_scales, float* __restrict__ v_scales,
+                    const SlotT* __restrict__ slots, int64_t num_slots, int64_t num_tokens,
+                    int num_heads, int groups_per_row, int lpr_shift, bool vec,
+                    int32_t* invalid) {
+  const int lpr = 1 << lpr_shift;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & (lpr - 1);
+  const int64_t rows = num_tokens * num_heads;
+  const int64_t step = ((int64_t)gridDim.x * blockDim.x) >> lpr_shift;
+  for (int64_t r0 = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >> lpr_shift;
+       r0 < rows; r0 += step) {
+    const int64_t row = r0 + (lane >> lpr_shift);
+    int64_t t = 0, slot = -1;
+    int h = 0;
+    if (row < rows) {
+      t = row / num_heads;
+      h = (int)(row - t * num_heads);
+      slot = load_index(slots, t);
+      if (slot >= num_slots && h == 0 && sub == 0 && invalid != nullptr) atomicAdd(invalid, 1);
+    }
+    const bool ok = row < rows && slot >= 0 && slot < num_slots;
+    const bool has = ok && sub < groups_per_row;
+    const int64_t src_off = (int64_t)sub * 16 * (int64_t)sizeof(T);
+    const int64_t dst = ((slot * num_heads + h) * groups_per_row + sub) * 16;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const uint8_t* src = which == 0 ? key + t * k_st + h * k_sh : value + t * v_st + h * v_sh;
+      float x[16];
+      float amax = 0.0f;
+      int nan = 0;
+      if (has) {
+        load16<T>(src + src_off, vec, x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float a = fabsf(x[j]);
+          nan |= isnan(a) ? 1 : 0;
+          amax = fmaxf(amax, a);
+        }
+      }
+      for (int o = 1; o < lpr; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+      }
+      float scale;
+      if (kInt8) {
+        scale = nan ? 1e-6f : fmaxf(amax / 127.0f, 1e-6f);
+      } else {
+        scale = (!nan && amax > 0.0f) ? amax / 448.0f : 1.0f;
+      }
+      if (has) {
+        uint32_t packed[4];
+        if (kInt8) {
+          const float inv = 1.0f / scale;
+#pragma unroll
+          for (int w = 0; w < 4; ++w)
+            packed[w] = (uint32_t)(uint8_t)quantize_int8(x[4 * w + 0], inv) |
+                        ((uint32_t)(uint8_t)quantize_int8(x[4 * w + 1], inv) << 8) |
+                        ((uint32_t)(uint8_t)quantize_int8(x[4 * w + 2], inv) << 16) |
+                        ((uint32_t)(uint8_t)quantize_int8(x[4 * w + 3], inv) << 24);
+        } else {
+#pragma unroll
+          for (int w = 0; w < 4; ++w)
+            packed[w] = (uint32_t)quantize_e4m3(x[4 * w + 0], scale) |
+                        ((uint32_t)quantize_e4m3(x[4 * w + 1], scale) << 8) |
+                        ((uint32_t)quantize_e4m3(x[4 * w + 2], scale) << 16) |
+                        ((uint32_t)quantize_e4m3(x[4 * w + 3], scale) << 24);
+        }
+        st_v4((which == 0 ? k_cache : v_cache) + dst,
+              make_uint4(packed[0], packed[1], packed[2], packed[3]));
+      }
+      if (ok && sub == 0) (which == 0 ? k_scales : v_scales)[slot * num_heads + h] = scale;
+    }
   }
 }
 
@@ -333,6 +431,26 @@ int launch_store_fp8(const void* key, const void* value, int64_t k_st, int64_t k
   return cuda_status(cudaGetLastError(), "store_kvcache_fp8 launch");
 }
 
+template <typename T, bool kInt8, typename SlotT>
+int launch_store_pth(const void* key, const void* value, int64_t k_st, int64_t k_sh,
+                     int64_t v_st, int64_t v_sh, void* k_cache, void* v_cache, float* k_scales,
+                     float* v_scales, int64_t num_slots, const SlotT* slots, int64_t num_tokens,
+                     int num_heads, int head_dim, int32_t* invalid, cudaStream_t stream) {
+  const int64_t eb = sizeof(T);
+  const bool vec = aligned16(key) && aligned16(value) && ((k_st * eb) % 16 == 0) &&
+                   ((k_sh * eb) % 16 == 0) && ((v_st * eb) % 16 == 0) &&
+                   ((v_sh * eb) % 16 == 0);
+  const int groups = head_dim / 16;
+  int lpr_shift = 0;
+  while ((1 << lpr_shift) < groups) ++lpr_shift;
+  const int grid = grid_for(num_tokens * num_heads << lpr_shift, kStoreThreads);
+  store_kv_pth_kernel<T, kInt8, SlotT><<<grid, kStoreThreads, 0, stream>>>(
+      (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,
+      (uint8_t*)k_cache, (uint8_t*)v_cache, k_scales, v_scales, slots, num_slots, num_tokens,
+      num_heads, groups, lpr_shift, vec, invalid);
+  return cuda_status(cudaGetLastError(), "store_kvcache_quant_per_token_head launch");
+}
+
 template <typename T>
 int launch_calibrate(const void* key, const void* value, int64_t k_st, int64_t k_sh,
                      int64_t v_st, int64_t v_sh, int64_t num_tokens, int num_heads, int head_dim,
@@ -474,4 +592,61 @@ extern "C" int mkv_store_kvcache_fp8(const void* key, const void* value,
                        "mkv_store_kvcache_fp8: key dtype must be f32, f16 or bf16 (got %d)", dtype);
   }
 #undef MKV_STORE8
+}
+
+extern "C" int mkv_store_kvcache_quant_per_token_head(
+    const void* key, const void* value, int64_t key_stride_token, int64_t key_stride_head,
+    int64_t value_stride_token, int64_t value_stride_head, void* k_cache, void* v_cache,
+    int32_t cache_dtype, float* k_scales, float* v_scales, int64_t num_blocks,
+    int32_t block_size, const void* slot_mapping, int32_t slot_index_type, int64_t num_tokens,
+    int32_t num_kv_heads, int32_t head_dim, int32_t dtype, int32_t* invalid_count, void* stream) {
+  clear_error();
+  const char* fn = "mkv_store_kvcache_quant_per_token_head";
+  int st = check_common(key, value, k_cache, v_cache, slot_mapping, slot_index_type, num_blocks,
+                        block_size, num_tokens, num_kv_heads, head_dim, fn);
+  if (st != MKV_OK) return st;
+  if (cache_dtype != MKV_DTYPE_FP8_E4M3 && cache_dtype != MKV_DTYPE_INT8)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: cache_dtype must be FP8_E4M3 or INT8 (got %d)", fn,
+                     cache_dtype);
+  if (head_dim % 16 != 0 || head_dim > 512)
+    return set_error(MKV_ERR_UNSUPPORTED,
+                     "%s: head_dim must be a multiple of 16 and at most 512 (got %d)", fn,
+                     head_dim);
+  if (!k_scales || !v_scales)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: null scale pointer", fn);
+  if ((((uintptr_t)k_scales) & 3u) || (((uintptr_t)v_scales) & 3u))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: scales must be 4-byte aligned", fn);
+  if ((((uintptr_t)k_cache) & 15u) || (((uintptr_t)v_cache) & 15u))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: caches must be 16-byte aligned", fn);
+  if (num_tokens == 0) return MKV_OK;
+  const int64_t num_slots = num_blocks * block_size;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool i64 = slot_index_type == MKV_INDEX_I64;
+  const bool i8 = cache_dtype == MKV_DTYPE_INT8;
+#define MKV_PTH(T, I8)                                                                          \
+  return i64 ? launch_store_pth<T, I8, int64_t>(key, value, key_stride_token, key_stride_head,  \
+                                                value_stride_token, value_stride_head, k_cache, \
+                                                v_cache, k_scales, v_scales, num_slots,         \
+                                                (const int64_t*)slot_mapping, num_tokens,       \
+                                                num_kv_heads, head_dim, invalid_count, s)       \
+             : launch_store_pth<T, I8, int32_t>(key, value, key_stride_token, key_stride_head,  \
+                                                value_stride_token, value_stride_head, k_cache, \
+                                                v_cache, k_scales, v_scales, num_slots,         \
+                                                (const int32_t*)slot_mapping, num_tokens,       \
+                                                num_kv_heads, head_dim, invalid_count, s)
+  switch (dtype) {
+    case MKV_DTYPE_F32:
+      if (i8) MKV_PTH(float, true);
+      MKV_PTH(float, false);
+    case MKV_DTYPE_F16:
+      if (i8) MKV_PTH(f16, true);
+      MKV_PTH(f16, false);
+    case MKV_DTYPE_BF16:
+      if (i8) MKV_PTH(bf16, true);
+      MKV_PTH(bf16, false);
+    default:
+      return set_error(MKV_ERR_UNSUPPORTED, "%s: key dtype must be f32, f16 or bf16 (got %d)", fn,
+                       dtype);
+  }
+#undef MKV_PTH
 }

@@ -1,9 +1,11 @@
 """Drop-in replacements for mini-kvllm's paged KV-cache hot path.
 
-The four functions keep the reference's names, argument order and meaning
+The functions keep the reference's names, argument order and meaning
 (heart1128/mini-kvllm, src/myvllm/layers/attention.py):
 
   store_kvcache(key, value, k_cache, v_cache, slot_mapping, block_size)           # :67
+  store_kvcache_int8(key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping,
+                     block_size)                                                   # :255
   store_kvcache_fp8(key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping,
                     block_size, kv_cache_dtype)                                    # :281
   paged_attention_decode(query, k_cache, v_cache, block_tables, context_lens, scale,
@@ -11,6 +13,9 @@ The four functions keep the reference's names, argument order and meaning
   paged_attention_decode_quantized(query, k_cache, v_cache, k_scale, v_scale,
                          block_tables, context_lens, scale, num_heads, num_kv_heads,
                          head_dim, block_size, kv_cache_dtype)                     # :1213
+
+with kv_cache_dtype "fp8_per_tensor" (scales of shape (1,)), "fp8_per_token_head" and
+"int8_per_token_head" (scales of shape (num_blocks, block_size, num_kv_heads)).
 
 and `Attention` keeps the module contract of attention.py:1617-1807 (cache tensors and
 scales injected as attributes by the model runner, metadata read from the global
@@ -37,7 +42,9 @@ _DTYPES = {
     torch.float16: _lib.DTYPE_F16,
     torch.bfloat16: _lib.DTYPE_BF16,
     torch.float8_e4m3fn: _lib.DTYPE_FP8_E4M3,
+    torch.int8: _lib.DTYPE_INT8,
 }
+_PER_TOKEN_HEAD = ("fp8_per_token_head", "int8_per_token_head")
 _INDEX = {torch.int32: _lib.INDEX_I32, torch.int64: _lib.INDEX_I64}
 _FLOAT_IO = (torch.float32, torch.float16, torch.bfloat16)
 
@@ -179,9 +186,13 @@ def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
     this batch (bf16/fp16/fp32 amax / 448, computed on the device); afterwards it stays
     frozen. Reference: attention.py:281-333 (calibration 315-323, kernel 118-191)."""
     fn = "store_kvcache_fp8"
+    if kv_cache_dtype == "fp8_per_token_head":
+        return _store_per_token_head(fn, key, value, k_cache, v_cache, k_scale, v_scale,
+                                     slot_mapping, block_size, _lib.DTYPE_FP8_E4M3)
     if kv_cache_dtype != "fp8_per_tensor":
         raise NotImplementedError(
-            f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented (only 'fp8_per_tensor')")
+            f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented "
+            "('fp8_per_tensor' or 'fp8_per_token_head')")
     num_tokens, num_kv_heads, head_dim = key.shape
     dev = _require_cuda(fn, key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping)
     if key.dtype not in _FLOAT_IO or value.dtype != key.dtype:
@@ -214,9 +225,56 @@ def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
     _lib.check(fn, st)
 
 
+def _check_row_scales(fn: str, k_scale: torch.Tensor, v_scale: torch.Tensor, num_blocks: int,
+                      block_size: int, num_kv_heads: int) -> None:
+    n = num_blocks * block_size * num_kv_heads
+    for name, t in (("k_scale", k_scale), ("v_scale", v_scale)):
+        if t.dtype != torch.float32 or t.numel() != n or not t.is_contiguous():
+            raise ValueError(f"{fn}: {name} must be a contiguous float32 tensor of "
+                             f"(num_blocks, block_size, num_kv_heads) = {n} elements")
+
+
+def _store_per_token_head(fn, key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping,
+                          block_size, cache_code):
+    num_tokens, num_kv_heads, head_dim = key.shape
+    dev = _require_cuda(fn, key, value, k_cache, v_cache, k_scale, v_scale, slot_mapping)
+    if key.dtype not in _FLOAT_IO or value.dtype != key.dtype:
+        raise ValueError(f"{fn}: key/value must share a float32/float16/bfloat16 dtype")
+    want = torch.int8 if cache_code == _lib.DTYPE_INT8 else (torch.float8_e4m3fn, torch.uint8)
+    if (k_cache.dtype != want) if isinstance(want, torch.dtype) else (k_cache.dtype not in want):
+        raise ValueError(f"{fn}: caches have dtype {k_cache.dtype}, expected {want}")
+    assert slot_mapping.numel() == num_tokens, "Slot mapping size must match number of tokens"
+    key, value = _row_major_tokens(key), _row_major_tokens(value)
+    num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
+    _check_row_scales(fn, k_scale, v_scale, num_blocks, block_size, num_kv_heads)
+    slots = _index_tensor(slot_mapping.reshape(-1), fn, "slot_mapping")
+    lib = _lib.load()
+    with _on_device(dev):
+        st = lib.mkv_store_kvcache_quant_per_token_head(
+            key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
+            value.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), cache_code,
+            k_scale.data_ptr(), v_scale.data_ptr(), num_blocks, block_size, slots.data_ptr(),
+            _INDEX[slots.dtype], num_tokens, num_kv_heads, head_dim, _DTYPES[key.dtype], None,
+            _stream(dev))
+    _lib.check(fn, st)
+
+
+def store_kvcache_int8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
+                       v_cache: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
+                       slot_mapping: torch.Tensor, block_size: int) -> None:
+    """Quantises each (token, kv head) row of key/value to INT8 with its own scale
+    max(amax / 127, 1e-6) (x * (1 / scale), rounded half away from zero, clamped to
+    [-128, 127]) and stores it into the int8 paged caches, writing the scale into
+    k_scale/v_scale (num_blocks, block_size, num_kv_heads) at the token's slot.
+    Reference: attention.py:255-278 (kernel 195-252)."""
+    _store_per_token_head("store_kvcache_int8", key, value, k_cache, v_cache, k_scale, v_scale,
+                          slot_mapping, block_size, _lib.DTYPE_INT8)
+
+
 # ---------------------------------------------------------------------------------- decode
 def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, context_lens,
-            scale, num_heads, num_kv_heads, head_dim, block_size, num_splits: int = 0):
+            scale, num_heads, num_kv_heads, head_dim, block_size, num_splits: int = 0,
+            per_token_head: bool = False):
     if query.dim() != 3 or query.shape[1] != num_heads or query.shape[2] != head_dim:
         raise ValueError(f"{fn}: query must be (batch, {num_heads}, {head_dim}), got {tuple(query.shape)}")
     if query.dtype not in _FLOAT_IO:
@@ -239,6 +297,8 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
     if lens.numel() != batch_size or block_tables.shape[0] < batch_size:
         raise ValueError(f"{fn}: context_lens/block_tables do not cover {batch_size} sequences")
     num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
+    if per_token_head:
+        _check_row_scales(fn, k_scale, v_scale, num_blocks, block_size, num_kv_heads)
     lib = _lib.load()
     ws_bytes = lib.mkv_paged_decode_workspace_bytes(batch_size, num_heads, num_kv_heads, head_dim,
                                                     block_size, max_num_blocks, num_splits)
@@ -246,7 +306,16 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
     ws_ptr = ws.data_ptr() if ws is not None else None
     with _on_device(dev):
         stream = _stream(dev)
-        if k_scale is None:
+        if per_token_head:
+            st = lib.mkv_paged_decode_quant_per_token_head(
+                query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
+                k_cache.data_ptr(), v_cache.data_ptr(), _DTYPES[k_cache.dtype], k_scale.data_ptr(),
+                v_scale.data_ptr(), num_blocks, block_size, block_tables.data_ptr(),
+                _INDEX[block_tables.dtype], block_tables.stride(0), max_num_blocks, lens.data_ptr(),
+                _INDEX[lens.dtype], batch_size, num_heads, num_kv_heads, head_dim, float(scale),
+                output.data_ptr(), output.stride(0), output.stride(1), ws_ptr, ws_bytes, num_splits,
+                None, stream)
+        elif k_scale is None:
             st = lib.mkv_paged_decode(
                 query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
                 k_cache.data_ptr(), v_cache.data_ptr(), _DTYPES[k_cache.dtype], num_blocks,
@@ -287,13 +356,24 @@ def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
                                      context_lens: torch.Tensor, scale: float, num_heads: int,
                                      num_kv_heads: int, head_dim: int, block_size: int,
                                      kv_cache_dtype: str, num_splits: int = 0) -> torch.Tensor:
-    """Decode attention over an FP8 E4M3 paged cache with per-tensor scales: pages are
-    dequantised as float(e4m3) * scale while they are loaded. Reference:
-    attention.py:1213-1268 with paged_attention_decode_fp8_kernel (953-1121)."""
+    """Decode attention over a quantised paged cache, dequantised while the pages are
+    loaded: 'fp8_per_tensor' (e4m3 pages, scales of shape (1,)), 'fp8_per_token_head'
+    (e4m3) and 'int8_per_token_head' (int8), the last two with a scale per (page, row,
+    kv head) in k_scale/v_scale (num_blocks, block_size, num_kv_heads). Reference:
+    attention.py:1213-1268 with paged_attention_decode_fp8_kernel (953-1121) and
+    paged_attention_decode_quantized_tile_kernel (1124-1210)."""
     fn = "paged_attention_decode_quantized"
+    if kv_cache_dtype in _PER_TOKEN_HEAD:
+        want = torch.int8 if kv_cache_dtype.startswith("int8") else torch.float8_e4m3fn
+        if k_cache.dtype != want:
+            raise ValueError(f"{fn}: {kv_cache_dtype} needs {want} caches (got {k_cache.dtype})")
+        return _decode(fn, query, k_cache, v_cache, k_scale, v_scale, block_tables,
+                       context_lens, scale, num_heads, num_kv_heads, head_dim, block_size,
+                       num_splits, per_token_head=True)
     if kv_cache_dtype != "fp8_per_tensor":
         raise NotImplementedError(
-            f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented (only 'fp8_per_tensor')")
+            f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented "
+            "('fp8_per_tensor', 'fp8_per_token_head' or 'int8_per_token_head')")
     if k_cache.dtype not in (torch.float8_e4m3fn, torch.uint8):
         raise ValueError(f"{fn}: caches must be float8_e4m3fn (got {k_cache.dtype})")
     if k_scale.dtype != torch.float32 or v_scale.dtype != torch.float32:
@@ -307,8 +387,10 @@ class Attention(nn.Module):
     """Attention layer with a paged KV cache (reference attention.py:1617-1807).
 
     The model runner injects `k_cache`/`v_cache` (per-layer views of one
-    (2, L, num_blocks, block_size, KVH, D) allocation), `kv_cache_dtype`, and for FP8 the
-    per-layer `k_scale`/`v_scale` (float32, shape (1,), initialised to the sentinel 1.0).
+    (2, L, num_blocks, block_size, KVH, D) allocation), `kv_cache_dtype`, and for the
+    quantised modes the per-layer `k_scale`/`v_scale` (float32; shape (1,) initialised to
+    the sentinel 1.0 for 'fp8_per_tensor', (num_blocks, block_size, KVH) for the
+    per-(token, head) modes).
     `forward` appends the step's K/V at context.slot_mapping and, for a decode batch,
     returns (batch, num_heads * head_dim). Prefill attention is outside this library."""
 
@@ -328,23 +410,27 @@ class Attention(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
-        fp8 = self.kv_cache_dtype == "fp8_per_tensor"
-        if self.kv_cache_dtype not in ("auto", "fp8_per_tensor"):
-            raise NotImplementedError(f"kv_cache_dtype {self.kv_cache_dtype!r} is not implemented")
+        mode = self.kv_cache_dtype
+        quant = mode != "auto"
+        if mode not in ("auto", "fp8_per_tensor") + _PER_TOKEN_HEAD:
+            raise NotImplementedError(f"kv_cache_dtype {mode!r} is not implemented")
         if k_cache.numel() > 0 and v_cache.numel() > 0 and context.slot_mapping is not None:
             if k.dim() == 4:
                 b, n, kvh, d = k.shape
                 k, v = k.reshape(b * n, kvh, d), v.reshape(b * n, kvh, d)
-            if fp8:
+            if mode == "int8_per_token_head":
+                store_kvcache_int8(k, v, k_cache, v_cache, self.k_scale, self.v_scale,
+                                   context.slot_mapping, self.block_size)
+            elif quant:
                 store_kvcache_fp8(k, v, k_cache, v_cache, self.k_scale, self.v_scale,
-                                  context.slot_mapping, self.block_size, self.kv_cache_dtype)
+                                  context.slot_mapping, self.block_size, mode)
             else:
                 store_kvcache(k, v, k_cache, v_cache, context.slot_mapping, self.block_size)
         scale = self.scale / (self.head_dim ** 0.5)
         if context.is_prefill:
             raise NotImplementedError(
                 "prefill / mixed-batch attention is not part of this library (decode hot path only)")
-        if fp8:
+        if quant:
             o = paged_attention_decode_quantized(
                 q, k_cache, v_cache, self.k_scale, self.v_scale, context.block_tables,
                 context.context_lens, scale, self.num_heads, self.num_kv_heads, self.head_dim,

@@ -166,4 +166,7 @@ def test_python_wrappers_reject_cpu_tensors(attn):
                                     torch.ones(2, dtype=torch.long), 0.1, 8, 2, 128, 16)
     with pytest.raises(NotImplementedError):
         attn.paged_attention_decode_quantized(q, cache, cache, None, None, None, None, 0.1, 8, 2,
-                                              128, 16, "fp8_per_token_head")
+                                              128, 16, "kivi_2bit")
+    with pytest.raises(ValueError, match="int8"):  # per-(token, head) INT8 needs int8 pages
+        attn.paged_attention_decode_quantized(q, cache, cache, None, None, None, None, 0.1, 8, 2,
+                                              128, 16, "int8_per_token_head")
