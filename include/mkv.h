@@ -247,6 +247,32 @@ MKV_API int mkv_paged_decode_quant_per_token_head(
     int32_t num_splits, int32_t* invalid_count, void* stream);
 
 /*
+ * Chunked-prefill / extend attention over the paged cache. Replaces
+ * paged_attention_prefill_triton (attention.py:852-892; kernel 704-849) and
+ * paged_attention_prefill_torch (649-701). query (total_q, num_heads, head_dim) holds the
+ * new tokens of every sequence, sequence b owning rows [cu_seqlens_q[b], cu_seqlens_q[b+1]);
+ * row q at absolute position positions[q] attends to the cached tokens
+ * t < min(context_lens[b], positions[q] + 1) on pages block_tables[b, t / block_size]
+ * (its own K/V must already be appended). -1 and out-of-range pages are skipped (not
+ * counted); a row that sees no token gives NaN. out has query's layout and dtype.
+ * Caches: the query dtype (bf16, f16, f32), or 8-bit with scales dequantised on load
+ * (not in the reference, whose TODO asks for it): FP8_E4M3 with per-tensor k_scale /
+ * v_scale, or FP8_E4M3 / INT8 with per-(page, row, kv head) k_scales / v_scales (pass
+ * the other pair as NULL). Tensor cores for bf16/f16 queries with head_dim 64 or 128;
+ * CUDA cores otherwise (head_dim a multiple of 16, at most 256).
+ */
+MKV_API int mkv_paged_prefill(
+    const void* query, int64_t q_stride_token, int64_t q_stride_head, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t cache_dtype, const float* k_scale,
+    const float* v_scale, const float* k_scales, const float* v_scales, int64_t num_blocks,
+    int32_t block_size, const void* block_tables, int32_t block_table_index_type,
+    int64_t block_table_stride_seq, int32_t max_num_blocks, const void* context_lens,
+    int32_t context_lens_index_type, const void* cu_seqlens_q, int32_t cu_seqlens_index_type,
+    const void* positions, int32_t positions_index_type, int32_t num_seqs, int64_t total_q,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
+    int64_t out_stride_token, int64_t out_stride_head, void* stream);
+
+/*
  * Paged-attention decode that allocates nothing and needs no workspace argument.
  * This entry point has no counterpart in the reference; it exists for callers that
  * cannot allocate device memory on their own: a host runtime that reserves all device

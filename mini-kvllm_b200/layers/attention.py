@@ -13,6 +13,9 @@ The functions keep the reference's names, argument order and meaning
   paged_attention_decode_quantized(query, k_cache, v_cache, k_scale, v_scale,
                          block_tables, context_lens, scale, num_heads, num_kv_heads,
                          head_dim, block_size, kv_cache_dtype)                     # :1213
+  paged_attention_prefill(query, k_cache, v_cache, block_tables, context_lens,
+                          cu_seqlens_q, positions, scale, num_heads, num_kv_heads,
+                          head_dim, block_size)        # paged_attention_prefill_triton :852
 
 with kv_cache_dtype "fp8_per_tensor" (scales of shape (1,)), "fp8_per_token_head" and
 "int8_per_token_head" (scales of shape (num_blocks, block_size, num_kv_heads)).
@@ -382,6 +385,85 @@ def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
                    scale, num_heads, num_kv_heads, head_dim, block_size, num_splits)
 
 
+# ---------------------------------------------------------------------------------- prefill
+def paged_attention_prefill(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            block_tables: torch.Tensor, context_lens: torch.Tensor,
+                            cu_seqlens_q: torch.Tensor, positions: torch.Tensor, scale: float,
+                            num_heads: int, num_kv_heads: int, head_dim: int, block_size: int,
+                            k_scale: torch.Tensor | None = None,
+                            v_scale: torch.Tensor | None = None,
+                            kv_cache_dtype: str = "auto") -> torch.Tensor:
+    """Chunked-prefill / extend attention over the paged cache: query (total_q, num_heads,
+    head_dim) holds every sequence's new tokens (sequence b owns rows
+    [cu_seqlens_q[b], cu_seqlens_q[b+1])); row q at absolute position positions[q] sees the
+    cached tokens t < min(context_lens[b], positions[q] + 1), so its own K/V must have
+    been appended. Returns (total_q, num_heads, head_dim) in the query dtype. Reference:
+    paged_attention_prefill_triton, attention.py:852-892 (kernel 704-849). The
+    quantised caches ('fp8_per_tensor', 'fp8_per_token_head', 'int8_per_token_head'
+    with their k_scale / v_scale) are extensions the reference lists as a TODO."""
+    fn = "paged_attention_prefill"
+    if query.dim() != 3 or query.shape[1] != num_heads or query.shape[2] != head_dim:
+        raise ValueError(f"{fn}: query must be (total_q, {num_heads}, {head_dim}), got {tuple(query.shape)}")
+    if query.dtype not in _FLOAT_IO:
+        raise ValueError(f"{fn}: unsupported query dtype {query.dtype}")
+    tensors = [query, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q, positions]
+    quant = kv_cache_dtype != "auto"
+    if quant:
+        if kv_cache_dtype not in ("fp8_per_tensor",) + _PER_TOKEN_HEAD:
+            raise NotImplementedError(f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented")
+        if k_scale is None or v_scale is None:
+            raise ValueError(f"{fn}: {kv_cache_dtype} needs k_scale and v_scale")
+        tensors += [k_scale, v_scale]
+    dev = _require_cuda(fn, *tensors)
+    total_q = query.shape[0]
+    query = query if query.stride(-1) == 1 and query.stride(1) % 8 == 0 and query.stride(0) % 8 == 0 \
+        else query.contiguous()
+    output = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    num_seqs = context_lens.numel()
+    if total_q == 0 or num_seqs == 0:
+        return output
+    if block_tables.stride(-1) != 1:
+        block_tables = block_tables.contiguous()
+    if block_tables.dtype not in _INDEX:
+        raise ValueError(f"{fn}: block_tables must be int32 or int64 (got {block_tables.dtype})")
+    lens = _index_tensor(context_lens.reshape(-1), fn, "context_lens")
+    cu = _index_tensor(cu_seqlens_q.reshape(-1), fn, "cu_seqlens_q")
+    pos = _index_tensor(positions.reshape(-1), fn, "positions")
+    if cu.numel() != num_seqs + 1 or pos.numel() != total_q or block_tables.shape[0] < num_seqs:
+        raise ValueError(f"{fn}: cu_seqlens_q/positions/block_tables do not match "
+                         f"{num_seqs} sequences and {total_q} query tokens")
+    num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
+    kp = vp = kps = vps = None
+    if kv_cache_dtype == "fp8_per_tensor":
+        if k_cache.dtype not in (torch.float8_e4m3fn, torch.uint8):
+            raise ValueError(f"{fn}: fp8_per_tensor needs float8_e4m3fn caches (got {k_cache.dtype})")
+        kp, vp = k_scale.data_ptr(), v_scale.data_ptr()
+        cache_code = _lib.DTYPE_FP8_E4M3
+    elif quant:
+        want = torch.int8 if kv_cache_dtype.startswith("int8") else torch.float8_e4m3fn
+        if k_cache.dtype != want:
+            raise ValueError(f"{fn}: {kv_cache_dtype} needs {want} caches (got {k_cache.dtype})")
+        _check_row_scales(fn, k_scale, v_scale, num_blocks, block_size, num_kv_heads)
+        kps, vps = k_scale.data_ptr(), v_scale.data_ptr()
+        cache_code = _DTYPES[want]
+    else:
+        if k_cache.dtype != query.dtype:
+            raise ValueError(f"{fn}: cache dtype {k_cache.dtype} must equal the query dtype {query.dtype}")
+        cache_code = _DTYPES[k_cache.dtype]
+    lib = _lib.load()
+    with _on_device(dev):
+        st = lib.mkv_paged_prefill(
+            query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
+            k_cache.data_ptr(), v_cache.data_ptr(), cache_code, kp, vp, kps, vps, num_blocks,
+            block_size, block_tables.data_ptr(), _INDEX[block_tables.dtype], block_tables.stride(0),
+            block_tables.shape[1], lens.data_ptr(), _INDEX[lens.dtype], cu.data_ptr(),
+            _INDEX[cu.dtype], pos.data_ptr(), _INDEX[pos.dtype], num_seqs, total_q, num_heads,
+            num_kv_heads, head_dim, float(scale), output.data_ptr(), output.stride(0),
+            output.stride(1), _stream(dev))
+    _lib.check(fn, st)
+    return output
+
+
 # ---------------------------------------------------------------------------------- module
 class Attention(nn.Module):
     """Attention layer with a paged KV cache (reference attention.py:1617-1807).
@@ -392,7 +474,8 @@ class Attention(nn.Module):
     the sentinel 1.0 for 'fp8_per_tensor', (num_blocks, block_size, KVH) for the
     per-(token, head) modes).
     `forward` appends the step's K/V at context.slot_mapping and, for a decode batch,
-    returns (batch, num_heads * head_dim). Prefill attention is outside this library."""
+    returns (batch, num_heads * head_dim); a prefill, chunked-prefill or mixed batch
+    attends through the paged cache (paged_attention_prefill for its prefill rows)."""
 
     def __init__(self, num_heads: int, head_dim: int, scale: float = 1.0,
                  num_kv_heads: int | None = None, block_size: int = 16):
@@ -428,8 +511,7 @@ class Attention(nn.Module):
                 store_kvcache(k, v, k_cache, v_cache, context.slot_mapping, self.block_size)
         scale = self.scale / (self.head_dim ** 0.5)
         if context.is_prefill:
-            raise NotImplementedError(
-                "prefill / mixed-batch attention is not part of this library (decode hot path only)")
+            return self._prefill(q, k_cache, v_cache, context, scale, mode, quant)
         if quant:
             o = paged_attention_decode_quantized(
                 q, k_cache, v_cache, self.k_scale, self.v_scale, context.block_tables,
@@ -439,4 +521,43 @@ class Attention(nn.Module):
             o = paged_attention_decode(
                 q, k_cache, v_cache, context.block_tables, context.context_lens, scale,
                 self.num_heads, self.num_kv_heads, self.head_dim, self.block_size)
+        return o.reshape(o.shape[0], self.num_heads * self.head_dim)
+
+    def _decode_rows(self, q, k_cache, v_cache, block_tables, context_lens, scale, mode, quant):
+        if quant:
+            return paged_attention_decode_quantized(
+                q, k_cache, v_cache, self.k_scale, self.v_scale, block_tables, context_lens,
+                scale, self.num_heads, self.num_kv_heads, self.head_dim, self.block_size, mode)
+        return paged_attention_decode(q, k_cache, v_cache, block_tables, context_lens, scale,
+                                      self.num_heads, self.num_kv_heads, self.head_dim,
+                                      self.block_size)
+
+    def _prefill(self, q, k_cache, v_cache, context, scale, mode, quant):
+        """Prefill, chunked prefill and extend read the whole visible context from the paged
+        cache (the step's K/V were appended just before), as attention.py:1695-1776 does
+        for its non-full-prefill path; a mixed batch's decode rows go through the decode
+        kernels (1711-1760). Quantised caches are dequantised in the kernel (the reference
+        raises NotImplementedError there, 1702-1708)."""
+        if context.cu_seqlens_q is None:
+            raise ValueError("cu_seqlens_q must be provided for varlen attention")
+        if context.positions is None or context.context_lens is None or context.block_tables is None:
+            raise ValueError("paged prefill requires positions, context_lens, and block_tables")
+        ks, vs = (self.k_scale, self.v_scale) if quant else (None, None)
+        split = getattr(context, "mixed_attention_split", None)
+        if split is not None and split.decode_token_indices and split.prefill_token_indices:
+            o = torch.empty_like(q)
+            di, ds = split.decode_token_indices_tensor, split.decode_seq_indices_tensor
+            o.index_copy_(0, di, self._decode_rows(
+                q.index_select(0, di), k_cache, v_cache, context.block_tables.index_select(0, ds),
+                context.context_lens.index_select(0, ds), scale, mode, quant))
+            pi, ps = split.prefill_token_indices_tensor, split.prefill_seq_indices_tensor
+            o.index_copy_(0, pi, paged_attention_prefill(
+                q.index_select(0, pi), k_cache, v_cache, context.block_tables.index_select(0, ps),
+                context.context_lens.index_select(0, ps), split.prefill_cu_seqlens_q_tensor,
+                context.positions.index_select(0, pi), scale, self.num_heads, self.num_kv_heads,
+                self.head_dim, self.block_size, ks, vs, mode))
+            return o.reshape(o.shape[0], self.num_heads * self.head_dim)
+        o = paged_attention_prefill(q, k_cache, v_cache, context.block_tables, context.context_lens,
+                                    context.cu_seqlens_q, context.positions, scale, self.num_heads,
+                                    self.num_kv_heads, self.head_dim, self.block_size, ks, vs, mode)
         return o.reshape(o.shape[0], self.num_heads * self.head_dim)

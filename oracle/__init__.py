@@ -2,7 +2,8 @@
 
 This package restates, on the CPU with torch, the reference algorithm of
 heart1128/mini-kvllm for the KV append (bf16/fp16/fp32, FP8 E4M3 per-tensor, FP8 and
-INT8 per-(token, head)) and the paged-attention decode. It is the checker, never the product: only
+INT8 per-(token, head)), the paged-attention decode and the chunked-prefill / extend
+attention over the paged cache. It is the checker, never the product: only
 tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may import it.
 The CUDA library (libmkv.so) never calls into it and has no CPU fallback.
 
@@ -20,6 +21,7 @@ from .kv_oracle import (  # noqa: F401
     e4m3_encode_reference,
     fp8_scale_ref,
     paged_decode_ref,
+    paged_prefill_ref,
     per_token_head_scales_ref,
     quantize_fp8_ref,
     quantize_int8_ref,

@@ -92,10 +92,13 @@ def per_token_head_scales_ref(x: torch.Tensor, mode: str) -> torch.Tensor:
 def quantize_int8_ref(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     """attention.py:240-247: q = x * (1 / scale) in float32 (reciprocal first, as written),
     rounded half away from zero by adding +-0.5 and truncating toward zero on the int8
-    store, after clamping to [-128, 127]. `scale` broadcasts over head_dim."""
+    store, after clamping to [-128, 127]. `scale` broadcasts over head_dim. tl.clamp
+    keeps the non-NaN bound (min(max(x, lo), hi) without NaN propagation), so a NaN
+    element stores -128."""
     inv = torch.tensor(1.0, dtype=torch.float32) / scale.float()
     q = x.float() * inv.unsqueeze(-1)
     q = torch.where(q >= 0, q + 0.5, q - 0.5)
+    q = torch.where(torch.isnan(q), torch.full_like(q, INT8_MIN), q)
     q = q.clamp(INT8_MIN, INT8_MAX)
     return torch.trunc(q).to(torch.int8)
 
@@ -231,4 +234,53 @@ def paged_decode_ref(query, k_cache, v_cache, block_tables, context_lens, scale,
         s = torch.einsum("hgd,thd->hgt", q, K) * scale
         p = torch.softmax(s, dim=-1)
         out[b] = torch.einsum("hgt,thd->hgd", p, V).reshape(num_heads, head_dim)
+    return out
+
+
+# ------------------------------------------------------------------- prefill / extend
+def paged_prefill_ref(query, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q,
+                      positions, scale, num_heads, num_kv_heads, block_size, k_scale=None,
+                      v_scale=None, k_scales=None, v_scales=None, compute_dtype=torch.float64):
+    """Chunked-prefill / extend attention over the paged cache, restating
+    paged_attention_prefill_torch (attention.py:649-701) and the kernel
+    paged_attention_prefill_kernel (attention.py:704-849): query token q of sequence b
+    (q in [cu_seqlens_q[b], cu_seqlens_q[b+1])) at absolute position positions[q] sees
+    the cached tokens t < min(context_lens[b], positions[q] + 1) (749), gathered through
+    block_tables[b, t // block_size]; a -1 page is skipped (792-796). GQA kv head
+    h // (H / KVH). With per-tensor k_scale/v_scale or per-(page, row, kv head)
+    k_scales/v_scales the 8-bit pages are dequantised as float(x) * scale, as the decode
+    kernels do (the reference has no quantised prefill; its TODO,
+    docs/chunked_prefill_todo.md:23-30, asks for exactly this). A query that sees no
+    token gives 0/0 = NaN. Returns (total_q, H, D) in compute_dtype."""
+    total_q, _, head_dim = query.shape
+    group = num_heads // num_kv_heads
+    num_blocks = k_cache.shape[0]
+    max_blocks = block_tables.shape[1]
+    kc = k_cache.to(compute_dtype)
+    vc = v_cache.to(compute_dtype)
+    if k_scale is not None:
+        kc = kc * float(k_scale.reshape(-1)[0])
+        vc = vc * float(v_scale.reshape(-1)[0])
+    if k_scales is not None:
+        kc = kc * k_scales.to(compute_dtype).unsqueeze(-1)
+        vc = vc * v_scales.to(compute_dtype).unsqueeze(-1)
+    out = torch.empty(total_q, num_heads, head_dim, dtype=compute_dtype)
+    cu = cu_seqlens_q.reshape(-1).tolist()
+    for b in range(len(cu) - 1):
+        ctx = int(context_lens[b])
+        for q in range(cu[b], cu[b + 1]):
+            n = max(0, min(ctx, int(positions[q]) + 1, max_blocks * block_size))
+            t = torch.arange(n)
+            blk = block_tables[b, t // block_size].long() if n > 0 else torch.zeros(0, dtype=torch.long)
+            ok = (blk >= 0) & (blk < num_blocks)
+            t, blk = t[ok], blk[ok]
+            if t.numel() == 0:
+                out[q] = float("nan")
+                continue
+            K = kc[blk, t % block_size]  # (n, KVH, D)
+            V = vc[blk, t % block_size]
+            qv = query[q].to(compute_dtype).view(num_kv_heads, group, head_dim)
+            s = torch.einsum("hgd,thd->hgt", qv, K) * scale
+            p = torch.softmax(s, dim=-1)
+            out[q] = torch.einsum("hgt,thd->hgd", p, V).reshape(num_heads, head_dim)
     return out

@@ -29,6 +29,8 @@ What runs, per fixture (all on the CPU):
   append_int8      store_kvcache_int8 (attention.py:195-278): int8 bytes and scales
   decode_fp8_pth,  paged_attention_decode_quantized with 'fp8_per_token_head' /
   decode_int8      'int8_per_token_head' (the tile kernel, attention.py:1124-1210)
+  prefill          paged_attention_prefill_triton (attention.py:852-892; kernel 704-849),
+                   chunked prefill over cached prefixes with a -1 page inside one context
 """
 from __future__ import annotations
 
@@ -188,6 +190,38 @@ def make_decode_pth(ref_attn, rng, mode):
                 block_size=np.int64(BS), out=out.numpy(), **codes)
 
 
+def make_prefill(ref_attn, rng):
+    """paged_attention_prefill_triton (attention.py:852-892) and paged_attention_prefill_torch
+    (649-701), interpreted: 3 sequences extending a cached prefix (chunked prefill), one
+    starting at position 0, one chunk of a single token, and a -1 page inside a context;
+    fp32 pages."""
+    import torch
+    B, H, KVH, D, BS, MAXB = 3, 4, 2, 32, 4, 9
+    ctx = [13, 30, 7]                  # tokens in the cache after this chunk was appended
+    chunk = [5, 1, 7]                  # new query tokens per sequence (the last ctx tokens)
+    q_, kc, vc, bt, cl = _paged_inputs(rng, B, H, KVH, D, BS, ctx, MAXB)
+    bt[1, 2] = -1                      # a -1 page inside sequence 1's context
+    cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    pos = np.concatenate([np.arange(c - n, c) for c, n in zip(ctx, chunk)]).astype(np.int64)
+    q = rng.standard_normal((int(cu[-1]), H, D)).astype(np.float32)
+    scale = 1.0 / np.sqrt(D)
+    args = (torch.from_numpy(q), torch.from_numpy(kc), torch.from_numpy(vc), torch.from_numpy(bt),
+            torch.from_numpy(cl), torch.from_numpy(cu), torch.from_numpy(pos), float(scale))
+    out_triton = ref_attn.paged_attention_prefill_triton(*args, H, KVH, D, BS)
+    # paged_attention_prefill_torch indexes every page it reads (a -1 entry would read the
+    # last block through Python's negative indexing), so it runs on the same inputs with
+    # the -1 entry replaced by the page the triton case skipped
+    bt_t = bt.copy()
+    bt_t[1, 2] = int(bt[1, 3]) if bt[1, 3] >= 0 else 0
+    out_torch = ref_attn.paged_attention_prefill_torch(
+        torch.from_numpy(q), torch.from_numpy(kc), torch.from_numpy(vc), torch.from_numpy(bt_t),
+        torch.from_numpy(cl), torch.from_numpy(cu), torch.from_numpy(pos), float(scale), H, KVH, BS)
+    return dict(query=q, k_cache=kc, v_cache=vc, block_tables=bt, context_lens=cl, cu_seqlens_q=cu,
+                positions=pos, scale=np.float64(scale), num_heads=np.int64(H),
+                num_kv_heads=np.int64(KVH), block_size=np.int64(BS), out=out_triton.numpy(),
+                block_tables_torch=bt_t, out_torch=out_torch.numpy())
+
+
 def _paged_inputs(rng, B, H, KVH, D, BS, lens, max_blocks, extra_blocks=3):
     import torch
     need = [(n + BS - 1) // BS for n in lens]
@@ -283,6 +317,7 @@ def main():
         ("append_int8", lambda: make_append_pth(ref_attn, np.random.default_rng(606), "int8")),
         ("decode_fp8_pth", lambda: make_decode_pth(ref_attn, np.random.default_rng(707), "fp8")),
         ("decode_int8", lambda: make_decode_pth(ref_attn, np.random.default_rng(808), "int8")),
+        ("prefill", lambda: make_prefill(ref_attn, np.random.default_rng(909))),
     ]
     only = set(args.only.split(",")) if args.only else None
     for name, job in jobs:

@@ -6,7 +6,8 @@ import torch
 
 from conftest import golden
 from oracle import (decode_torch_optimized, e4m3_encode_reference, fp8_scale_ref,
-                    paged_decode_ref, per_token_head_scales_ref, quantize_fp8_ref,
+                    paged_decode_ref, paged_prefill_ref, per_token_head_scales_ref,
+                    quantize_fp8_ref,
                     store_kvcache_fp8_ref, store_kvcache_quant_per_token_head_ref,
                     store_kvcache_ref)
 
@@ -202,3 +203,19 @@ def test_per_token_head_decode_oracle_matches_reference_kernel(mode):
                            q.shape[2], int(g["block_size"]), k_scales=torch.from_numpy(g["k_scales"]),
                            v_scales=torch.from_numpy(g["v_scales"]))
     assert torch.allclose(out, torch.from_numpy(g["out"]).double(), atol=2e-6, rtol=1e-5)
+
+
+# ---------------------------------------------------------------------- prefill / extend
+@pytest.mark.parametrize("which", ["triton", "torch"])
+def test_prefill_oracle_matches_reference(which):
+    """Chunked prefill over cached prefixes: the oracle against the reference's Triton kernel
+    (with a -1 page inside a context, skipped) and its torch version (all pages valid)."""
+    g = golden("prefill")
+    bt = torch.from_numpy(g["block_tables"] if which == "triton" else g["block_tables_torch"])
+    out = paged_prefill_ref(torch.from_numpy(g["query"]), torch.from_numpy(g["k_cache"]),
+                            torch.from_numpy(g["v_cache"]), bt, torch.from_numpy(g["context_lens"]),
+                            torch.from_numpy(g["cu_seqlens_q"]), torch.from_numpy(g["positions"]),
+                            float(g["scale"]), int(g["num_heads"]), int(g["num_kv_heads"]),
+                            int(g["block_size"]))
+    ref = torch.from_numpy(g["out"] if which == "triton" else g["out_torch"]).double()
+    assert torch.allclose(out, ref, atol=2e-6, rtol=1e-5)

@@ -1,0 +1,154 @@
+"""Chunked-prefill / extend attention over the paged cache (paged_attention_prefill) on the
+GPU against the CPU oracle paged_prefill_ref, which is pinned to the reference's
+paged_attention_prefill_triton / _torch by tests/golden/prefill.npz.
+
+Tolerances: bf16/fp16 queries atol 2e-2 / rtol 1e-2 (fp32 accumulation; P rounded to the
+query dtype for the PV product), fp32 queries atol 2e-5 / rtol 1e-4."""
+import math
+
+import pytest
+import torch
+
+from conftest import golden, mkv_module
+from oracle import paged_prefill_ref
+
+pytestmark = pytest.mark.gpu
+attn = mkv_module("layers.attention")
+TOL = {torch.float32: (2e-5, 1e-4), torch.float16: (2e-2, 1e-2), torch.bfloat16: (2e-2, 1e-2)}
+
+
+def make_case(ctx, chunk, H, KVH, D, BS, dtype, seed, cache="same", start=None):
+    """Sequences whose last chunk[b] tokens of ctx[b] are the new queries (positions
+    ctx - chunk .. ctx - 1), pages a random permutation."""
+    g = torch.Generator().manual_seed(seed)
+    B = len(ctx)
+    need = [(n + BS - 1) // BS for n in ctx]
+    NB = sum(need) + 3
+    perm = torch.randperm(NB, generator=g)
+    bt = torch.full((B, max(max(need), 1)), -1, dtype=torch.int32)
+    pos = 0
+    for b, k in enumerate(need):
+        bt[b, :k] = perm[pos:pos + k].int()
+        pos += k
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(chunk), 0).tolist()), dtype=torch.int32)
+    positions = torch.cat([torch.arange(c - n, c) for c, n in zip(ctx, chunk)]).long()
+    q = torch.randn(int(cu[-1]), H, D, generator=g).to(dtype)
+    raw = torch.randn(2, NB, BS, KVH, D, generator=g)
+    ks = vs = None
+    if cache == "same":
+        kc, vc = raw[0].to(dtype), raw[1].to(dtype)
+    elif cache == "fp8_per_tensor":
+        kc, vc = (raw[0] * 40).to(torch.float8_e4m3fn), (raw[1] * 40).to(torch.float8_e4m3fn)
+        ks, vs = torch.tensor([0.021]), torch.tensor([0.032])
+    else:
+        if cache == "fp8_per_token_head":
+            kc, vc = (raw[0] * 40).to(torch.float8_e4m3fn), (raw[1] * 40).to(torch.float8_e4m3fn)
+        else:
+            kc = (raw[0] * 40).round().clamp(-128, 127).to(torch.int8)
+            vc = (raw[1] * 40).round().clamp(-128, 127).to(torch.int8)
+        ks = torch.rand(NB, BS, KVH, generator=g) * 0.04 + 0.002
+        vs = torch.rand(NB, BS, KVH, generator=g) * 0.04 + 0.002
+    return q, kc, vc, bt, torch.tensor(ctx, dtype=torch.int64), cu, positions, ks, vs
+
+
+def run(case, H, KVH, D, BS, scale, cache="same"):
+    q, kc, vc, bt, cl, cu, pos, ks, vs = case
+    mode = "auto" if cache == "same" else cache
+    kw = {} if ks is None else dict(k_scale=ks.cuda(), v_scale=vs.cuda(), kv_cache_dtype=mode)
+    out = attn.paged_attention_prefill(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), cl.cuda(), cu.cuda(),
+                                       pos.cuda(), scale, H, KVH, D, BS, **kw)
+    torch.cuda.synchronize()
+    if ks is None:
+        ref = paged_prefill_ref(q, kc, vc, bt, cl, cu, pos, scale, H, KVH, BS)
+    elif cache == "fp8_per_tensor":
+        ref = paged_prefill_ref(q, kc, vc, bt, cl, cu, pos, scale, H, KVH, BS, k_scale=ks, v_scale=vs)
+    else:
+        ref = paged_prefill_ref(q, kc, vc, bt, cl, cu, pos, scale, H, KVH, BS, k_scales=ks, v_scales=vs)
+    return out.cpu(), ref
+
+
+def close(out, ref, dtype):
+    atol, rtol = TOL[dtype]
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(out), nan), "NaN pattern differs"
+    diff = (out.double() - ref)[~nan].abs()
+    assert bool((diff <= atol + rtol * ref[~nan].abs()).all()), f"max abs err {float(diff.max()):.3e}"
+
+
+CTX = [300, 64, 1, 130, 17, 700]
+CHUNK = [300, 5, 1, 65, 17, 256]  # full prefill, short extend, single token, chunked
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("H,KVH", [(8, 8), (16, 4), (32, 2), (6, 2)])
+@pytest.mark.parametrize("BS", [16, 256])
+def test_prefill_matches_oracle(dtype, H, KVH, BS):
+    D = 128
+    case = make_case(CTX, CHUNK, H, KVH, D, BS, dtype, seed=H * 3 + KVH + BS)
+    out, ref = run(case, H, KVH, D, BS, 1.0 / math.sqrt(D))
+    close(out, ref, dtype)
+
+
+@pytest.mark.parametrize("D", [64, 96, 256])
+def test_prefill_other_head_dims(D):
+    case = make_case(CTX, CHUNK, 8, 2, D, 16, torch.bfloat16, seed=D)
+    out, ref = run(case, 8, 2, D, 16, 1.0 / math.sqrt(D))
+    close(out, ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("cache", ["fp8_per_tensor", "fp8_per_token_head", "int8_per_token_head"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_prefill_quantised_caches(cache, dtype):
+    """Quantised caches dequantised in the kernel (the reference's TODO)."""
+    case = make_case(CTX, CHUNK, 16, 4, 128, 16, dtype, seed=7, cache=cache)
+    out, ref = run(case, 16, 4, 128, 16, 0.0883, cache=cache)
+    close(out, ref, dtype)
+
+
+def test_prefill_invalid_pages_and_empty_rows():
+    """-1 pages inside a context are skipped; a query whose visible range holds only
+    missing pages gives NaN."""
+    case = list(make_case([40, 20], [40, 10], 8, 2, 128, 16, torch.bfloat16, seed=3))
+    bt = case[3].clone()
+    bt[0, 1] = -1            # tokens 16..31 of sequence 0 missing
+    bt[1, 0] = 10 ** 6       # tokens 0..15 of sequence 1 out of range: its rows at
+                             # positions 10..15 see nothing
+    case[3] = bt
+    out, ref = run(tuple(case), 8, 2, 128, 16, 0.09)
+    assert torch.isnan(ref).any()  # sequence 1's early rows see only missing pages
+    close(out, ref, torch.bfloat16)
+
+
+def test_prefill_long_chunk():
+    """A 2048-token chunk extending a 4096-token prefix (many KV tiles, causal edge in
+    the middle of a tile), GQA 4."""
+    case = make_case([6144, 900], [2048, 900], 32, 8, 128, 256, torch.bfloat16, seed=11)
+    out, ref = run(case, 32, 8, 128, 256, 1.0 / math.sqrt(128))
+    close(out, ref, torch.bfloat16)
+
+
+def test_golden_prefill_through_cuda():
+    g = golden("prefill")
+    t = lambda k: torch.from_numpy(g[k])
+    H, KVH, BS = int(g["num_heads"]), int(g["num_kv_heads"]), int(g["block_size"])
+    q = t("query")
+    out = attn.paged_attention_prefill(q.cuda(), t("k_cache").cuda(), t("v_cache").cuda(),
+                                       t("block_tables").cuda(), t("context_lens").cuda(),
+                                       t("cu_seqlens_q").cuda(), t("positions").cuda(), float(g["scale"]),
+                                       H, KVH, q.shape[2], BS).cpu()
+    close(out, t("out").double(), torch.float32)
+
+
+def test_prefill_matches_decode_for_last_token():
+    """For each sequence, the prefill row of its last context token equals the decode of
+    that sequence over the same cache."""
+    H, KVH, D, BS = 32, 8, 128, 16
+    case = make_case(CTX, CHUNK, H, KVH, D, BS, torch.bfloat16, seed=5)
+    q, kc, vc, bt, cl, cu, pos, _, _ = case
+    out = attn.paged_attention_prefill(q.cuda(), kc.cuda(), vc.cuda(), bt.cuda(), cl.cuda(), cu.cuda(),
+                                       pos.cuda(), 0.09, H, KVH, D, BS)
+    last = (cu[1:] - 1).long()
+    dec = attn.paged_attention_decode(q[last].cuda(), kc.cuda(), vc.cuda(), bt.cuda(), cl.cuda(), 0.09,
+                                      H, KVH, D, BS)
+    torch.cuda.synchronize()
+    close(out[last.cuda()].cpu(), dec.cpu().double(), torch.bfloat16)
