@@ -27,10 +27,14 @@
 //     so the host never reads device data (graph-safe).
 // A CUDA-core kernel (one warp per query token and head) covers fp32 queries and head
 // dims other than 64 / 128.
+#include <cuda.h>
+#include <cstdlib>
+
 #include <cstdio>
 #include <type_traits>
 
 #include "mkv_common.cuh"
+#include "sm100.cuh"
 
 namespace mkv {
 namespace {
@@ -97,13 +101,14 @@ __device__ __forceinline__ int pf_visible(const PrefillParams& p, int64_t ctx, i
 struct PfUnit {
   int seq, q0, nq;
 };
+template <int NTHREADS = kPThreads>
 __device__ bool pf_find_unit(const PrefillParams& p, int64_t unit, PfUnit& u) {
-  __shared__ long long red[kPThreads / 32];
+  __shared__ long long red[NTHREADS / 32];
   __shared__ int found[3];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) found[0] = -1;
   long long carry = 0;
-  for (int base = 0; base < p.num_seqs; base += kPThreads) {
+  for (int base = 0; base < p.num_seqs; base += NTHREADS) {
     const int s = base + tid;
     int len = 0;
     int64_t q0 = 0;
@@ -124,7 +129,7 @@ __device__ bool pf_find_unit(const PrefillParams& p, int64_t unit, PfUnit& u) {
     __syncthreads();
     long long off = carry, chunk = 0;
 #pragma unroll
-    for (int i = 0; i < kPThreads / 32; ++i) {
+    for (int i = 0; i < NTHREADS / 32; ++i) {
       if (i < warp) off += red[i];
       chunk += red[i];
     }
@@ -410,6 +415,636 @@ paged_prefill_tc_kernel(const PrefillParams p) {
   }
 }
 
+// ============================================================ tcgen05 kernel
+// 16-bit caches, head_dim 128, power-of-two block_size >= 8: a CTA owns NQ = 1 or 2 tiles
+// of 128 rows (query token, GQA head) of one kv head and runs FlashAttention-2 with the
+// accumulators and P in tensor memory:
+//   warp 0     producer: 128-token K and V tiles by TMA (one 2D box per page segment and
+//              64-column half, 128-byte swizzle) into separate K and V rings, K one tile
+//              ahead of V (the order the MMAs consume them); a missing page's V rows are
+//              zero-filled instead (its K columns are masked);
+//   warp 1     MMA issuer: S = Q K(i)^T (M = N = 128, K = 128, operands K-major) into TMEM,
+//              O += P V(i) with P read from TMEM (the first 64 columns of its S buffer, two
+//              16-bit values per column) and V MN-major straight from the TMA tile. A K
+//              stage is released when its last QK product completes, a V stage when its
+//              last PV product does.
+//              NQ = 1: two S buffers; QK(i) is issued one tile ahead of PV(i-1).
+//              NQ = 2: one S buffer per query tile; PV_q(i) then QK_q(i+1), alternating
+//              between the tiles, so that one tile's softmax runs while the other's
+//              products do;
+//   softmax    one warpgroup per query tile (warps 2-5, 6-9), thread = row = TMEM lane: S
+//              row read once into registers, mask (causal per row, missing pages), online
+//              softmax in the exp2 domain with a lazy reference (O in TMEM is rescaled
+//              only when a row's maximum grows by more than 2^8), P stored into TMEM over
+//              S; finally O / l to global memory.
+// tcgen05.mma operations of a CTA run in issue order, so a QK product issued after PV(i)
+// overwrites P(i) only after PV(i) has read it.
+// Every mbarrier wait is bounded (sm100::kWaitCycles); a role that gives up raises the
+// CTA abort flag, the others stop, in-flight TMA loads and MMAs are waited for (bounded)
+// and TMEM is freed.
+#ifdef MKV_PREFILL_TRACE
+// Debug-only event timeline (globaltimer, ns) of one CTA: [event][tile].
+__device__ unsigned long long g_pftrace[16][64];
+#define PF_TRACE(ev, tile)                                                   \
+  do {                                                                       \
+    if (blockIdx.x == 8 && blockIdx.y == 0 && (tile) < 64) {                 \
+      unsigned long long t_;                                                 \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                 \
+      g_pftrace[(ev)][(tile)] = t_;                                          \
+    }                                                                        \
+  } while (0)
+#else
+#define PF_TRACE(ev, tile) \
+  do {                     \
+  } while (0)
+#endif
+namespace pf05 {
+using namespace sm100;
+constexpr int kRows = 128;     // MMA M: (query token, head) rows of one query tile
+constexpr int kTile = 128;     // MMA N of S: kv tokens per tile
+constexpr int kD = 128;
+constexpr uint32_t kTmemCols = 512;  // S buffers (P over their first 64 columns) at 0 / 128, O at 256 (+128)
+constexpr int BLK = 128 * 128;       // 128 rows x 128 bytes: one 64-column half
+constexpr int TILE = 2 * BLK;        // 128 rows x 256 bytes
+template <int NQ>
+struct Layout {
+  static constexpr int kThreads = 64 + 128 * NQ;
+  static constexpr int kKStages = 3;
+  static constexpr int kVStages = NQ == 1 ? 3 : 2;
+  static constexpr int Q0 = 0;                           // [NQ] query tiles
+  static constexpr int K0 = Q0 + NQ * TILE;              // [stage] K tile
+  static constexpr int V0 = K0 + kKStages * TILE;        // [stage] V tile
+  static constexpr int BAR0 = V0 + kVStages * TILE;
+  // K full/empty, V full/empty, q, s[2], p[2], o[NQ], drain
+  static constexpr int NBAR = 2 * kKStages + 2 * kVStages + 1 + 2 + 2 + NQ + 1;
+  static constexpr int MISC0 = BAR0 + NBAR * 8;          // tmem base, abort flag, nkv
+  static constexpr int BYTES = MISC0 + 16 + 1024;        // + alignment slack
+  static_assert(BYTES <= 232448, "shared memory per CTA");
+};
+}  // namespace pf05
+
+template <typename QT, int NQ>
+__global__ void __launch_bounds__(pf05::Layout<NQ>::kThreads, 1)
+paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap vmap, int units) {
+  using namespace pf05;
+  using L = Layout<NQ>;
+  constexpr int kKS = L::kKStages, kVS = L::kVStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR0);
+  uint64_t* kfull = bars;
+  uint64_t* kempty = kfull + kKS;
+  uint64_t* vfull = kempty + kKS;
+  uint64_t* vempty = vfull + kVS;
+  uint64_t* qfull = vempty + kVS;
+  uint64_t* sfull = qfull + 1;
+  uint64_t* pfull = sfull + 2;
+  uint64_t* ofull = pfull + 2;
+  uint64_t* drain = ofull + NQ;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + L::MISC0);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC0 + 4);
+  int* nkv_s = reinterpret_cast<int*>(smem + L::MISC0 + 8);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kvh = blockIdx.y;
+  PfUnit u;
+  // heaviest query blocks (latest in each sequence) first
+  if (!pf_find_unit<L::kThreads>(p, (int64_t)units - 1 - blockIdx.x, u)) return;
+  const int seq = u.seq;
+  const int64_t ctx = pf_ctx(p, seq);
+
+  if (tid == 0) {
+    for (int s = 0; s < kKS; ++s) {
+      mbar_init(&kfull[s], 1);
+      mbar_init(&kempty[s], 1);
+    }
+    for (int s = 0; s < kVS; ++s) {
+      mbar_init(&vfull[s], 1);
+      mbar_init(&vempty[s], 1);
+    }
+    mbar_init(qfull, 4 * NQ);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sfull[b], 1);
+      mbar_init(&pfull[b], 4);
+    }
+    for (int q = 0; q < NQ; ++q) mbar_init(&ofull[q], 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *nkv_s = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_base_s, kTmemCols);
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tmem_base_s;
+
+  // softmax warp w >= 2 serves query tile qt = (w - 2) / 4; its thread owns the tile's row
+  // rt = 32 * (w % 4) + lane, which is also its TMEM lane (warp w reaches lanes 32 (w % 4) ..)
+  const int qt = warp >= 2 ? (warp - 2) >> 2 : 0;
+  const int rt = 32 * (warp & 3) + lane;
+  int vis = 0, qrow = -1, hrow = 0;
+  if (warp >= 2) {
+    const int row = kRows * qt + rt;
+    const int tok = row / p.group, gh = row - tok * p.group;
+    if (tok < u.nq) {
+      qrow = u.q0 + tok;
+      hrow = kvh * p.group + gh;
+      vis = pf_visible(p, ctx, pf_pos(p, qrow));
+    }
+    atomicMax(nkv_s, vis);
+  }
+  __syncthreads();
+  const int nkv = *nkv_s;
+  const int ntiles = (nkv + kTile - 1) / kTile;
+  // a tile is loaded in segments of one page (or of kTile tokens of a larger page)
+  const int seg_rows = p.block_size < kTile ? p.block_size : kTile;
+  const int nseg = kTile / seg_rows;
+
+  if (warp == 0) {
+    // ================================================================ producer
+    if (lane == 0) {
+      tma_prefetch_map(&kmap);
+      tma_prefetch_map(&vmap);
+    }
+    // page of segment `lane` of tile t (-1: missing, or past the CTA's last kv token)
+    auto seg_page_of = [&](int t) -> int {
+      int pg = -1;
+      if (lane < nseg) {
+        const int ts = t * kTile + lane * seg_rows;
+        if (ts < nkv) pg = pf_page(p, seq, ts / p.block_size);
+      }
+      return pg;
+    };
+    // K(t) and V(t) are issued in the order K(0), K(1), V(0), K(2), V(1), ...
+    auto issue = [&](int t, bool is_v, int seg_page) -> bool {
+      const int ns = is_v ? kVS : kKS;
+      const int st = t % ns;
+      uint64_t* empty = is_v ? vempty : kempty;
+      uint64_t* full = is_v ? vfull : kfull;
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[st], ((t / ns) & 1) ^ 1, abort_flag))) return false;
+      if (lane == 0) PF_TRACE(is_v ? 9 : 0, t);
+      uint8_t* dst = smem + (is_v ? L::V0 : L::K0) + st * TILE;
+      uint32_t bytes = 0;
+      for (int sgi = 0; sgi < nseg; ++sgi) {
+        const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
+        if (pg >= 0) {
+          bytes += 2u * seg_rows * 128u;
+        } else if (is_v) {  // a missing segment's V rows: zeros (P is 0 there; 0 * garbage may not be)
+          for (int k = lane; k < 2 * seg_rows * 8; k += 32) {
+            const int b = k / (seg_rows * 8), kk = k - b * seg_rows * 8;
+            *reinterpret_cast<uint4*>(dst + b * BLK + sgi * seg_rows * 128 + kk * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+      }
+      if (is_v) fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes);
+      if (lane == 0 && !is_v) PF_TRACE(1, t);
+      for (int sgi = 0; sgi < nseg; ++sgi) {
+        const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
+        if (lane == 0 && pg >= 0) {
+          const int ts = t * kTile + sgi * seg_rows;
+          const int y = pg * p.block_size + (ts & (p.block_size - 1));
+          for (int b = 0; b < 2; ++b)
+            tma_load_2d(smem_u32(dst + b * BLK + sgi * seg_rows * 128), is_v ? &vmap : &kmap,
+                        kvh * kD + b * 64, y, &full[st]);
+        }
+      }
+      __syncwarp();
+      return true;
+    };
+    int nk = 0, nv = 0;  // K and V tiles issued
+    int page_v = -1;     // segment pages of the V tile next in line
+    bool ok = true;
+    for (int t = 0; t <= ntiles && ok; ++t) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;  // warp-uniform exit
+      const int page_k = t < ntiles ? seg_page_of(t) : -1;
+      if (t < ntiles) {
+        ok = issue(t, false, page_k);
+        if (ok) ++nk;
+      }
+      if (ok && t > 0) {
+        ok = issue(t - 1, true, page_v);
+        if (ok) ++nv;
+      }
+      page_v = page_k;
+    }
+    if (!ok) *abort_flag = 1;
+    if (lane == 0 && *abort_flag) {  // let issued loads land before the CTA exits
+      for (int k = nk - kKS; k < nk; ++k)
+        if (k >= 0) mbar_wait(&kfull[k % kKS], (k / kKS) & 1, nullptr);
+      for (int k = nv - kVS; k < nv; ++k)
+        if (k >= 0) mbar_wait(&vfull[k % kVS], (k / kVS) & 1, nullptr);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    constexpr uint32_t fmt = std::is_same<QT, bf16>::value ? 1u : 0u;
+    constexpr uint32_t kIdQK = instr_desc(fmt, fmt, 0, 0, kRows, kTile);
+    constexpr uint32_t kIdPV = instr_desc(fmt, fmt, 0, 1, kRows, kD);
+    bool ok = ntiles == 0 || __all_sync(0xffffffffu, mbar_wait(qfull, 0, abort_flag));
+    bool issued = false;  // any MMA issued (they must finish before TMEM is freed)
+    // S_q(i) = Q_q K(i)^T into S buffer sb; release: the last QK product of K tile i
+    auto qk = [&](int q, int i, int sb, bool release) -> bool {
+      const int st = i % kKS;
+      if (!__all_sync(0xffffffffu, mbar_wait(&kfull[st], (i / kKS) & 1, abort_flag))) return false;
+      if (lane == 0 && q == 0) PF_TRACE(14, i);
+      tc_fence_after_sync();
+      if (lane == 0) {
+        const uint32_t qaddr = smem_u32(smem + L::Q0 + q * TILE);
+        const uint32_t kaddr = smem_u32(smem + L::K0 + st * TILE);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {  // 16 head_dim columns per MMA
+          const uint64_t a = smem_desc(qaddr + (k >> 2) * BLK + (k & 3) * 32, 16, 1024, kLayoutSw128);
+          const uint64_t b = smem_desc(kaddr + (k >> 2) * BLK + (k & 3) * 32, 16, 1024, kLayoutSw128);
+          mma_f16(tmem + sb * kTile, a, b, kIdQK, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&sfull[sb]);
+        if (release) mma_commit(&kempty[st]);
+        if (q == 0) PF_TRACE(2, i);
+      }
+      __syncwarp();
+      issued = true;
+      return true;
+    };
+    // O_q += P_q(j) V(j), P in S buffer sb (its pfull phase = ph); release: the last PV
+    // product of V tile j
+    auto pv = [&](int q, int j, int sb, int ph, bool release) -> bool {
+      const int st = j % kVS;
+      bool got = mbar_wait(&pfull[sb], ph, abort_flag) && mbar_wait(&vfull[st], (j / kVS) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) return false;
+      if (lane == 0 && q == 0) PF_TRACE(12, j);
+      tc_fence_after_sync();
+      if (lane == 0) {
+        const uint32_t vaddr = smem_u32(smem + L::V0 + st * TILE);
+#pragma unroll
+        for (int k = 0; k < kTile / 16; ++k) {  // 16 kv tokens per MMA = 8 TMEM columns of P
+          const uint64_t b = smem_desc(vaddr + k * 2048, BLK, 1024, kLayoutSw128);
+          mma_f16_ts(tmem + 256 + q * kD, tmem + sb * kTile + 8 * k, b, kIdPV, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        if (q == 0) PF_TRACE(13, j);
+        mma_commit(&ofull[q]);
+        if (release) mma_commit(&vempty[st]);
+        if (q == 0) PF_TRACE(3, j);
+      }
+      __syncwarp();
+      issued = true;
+      return true;
+    };
+    if constexpr (NQ == 1) {
+      for (int i = 0; i < ntiles && ok; ++i) {
+        // S buffer i & 1 last held P(i-2), read by PV(i-2), which was issued before
+        ok = qk(0, i, i & 1, true);
+        if (ok && i > 0) ok = pv(0, i - 1, (i - 1) & 1, ((i - 1) >> 1) & 1, true);
+      }
+      if (ok && ntiles > 0) ok = pv(0, ntiles - 1, (ntiles - 1) & 1, ((ntiles - 1) >> 1) & 1, true);
+    } else {
+      // PV_q(i) then QK_q(i+1) (after PV_q(i), which reads P_q(i) from the S buffer
+      // QK_q(i+1) overwrites), tile 0 then tile 1. (Polling both tiles' P barriers to take
+      // whichever is ready first measured slower: the polling warp takes issue slots from
+      // the softmax warps that share its SM sub-partition.)
+      for (int q = 0; q < 2 && ok && ntiles > 0; ++q) ok = qk(q, 0, q, q == 1);
+      for (int i = 0; i < ntiles && ok; ++i) {
+        for (int q = 0; q < 2 && ok; ++q) {
+          ok = pv(q, i, q, i & 1, q == 1);
+          if (ok && i + 1 < ntiles) ok = qk(q, i + 1, q, q == 1);
+        }
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    if (lane == 0 && issued) {  // every MMA of this CTA done before TMEM is freed
+      mma_commit(drain);
+      mbar_wait(drain, 0, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // ================================================================ softmax (warpgroup qt)
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const uint32_t o_col = 256 + qt * kD;
+    // stage this row of Q (128-byte swizzle, two 64-column halves)
+    {
+      const QT* src = reinterpret_cast<const QT*>(p.q) + (int64_t)(qrow >= 0 ? qrow : 0) * p.q_st +
+                      (int64_t)hrow * p.q_sh;
+      uint8_t* qdst = smem + L::Q0 + qt * TILE + rt * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (qrow >= 0) v = *reinterpret_cast<const uint4*>(src + c * 8);
+        const int b = c >> 3, cc = c & 7;
+        *reinterpret_cast<uint4*>(qdst + b * BLK + ((cc ^ (rt & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(qfull);
+    }
+    const float sc = p.qk_scale_log2;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    // page of segment `lane` of tile t (0 past the CTA's last kv token), looked up one
+    // tile ahead
+    auto seg_page_of = [&](int t) -> int {
+      const int ts = t * kTile + lane * seg_rows;
+      return (lane < nseg && ts < nkv) ? pf_page(p, seq, ts / p.block_size) : 0;
+    };
+    int pg_next = ntiles > 0 ? seg_page_of(0) : 0;
+    for (int i = 0; i < ntiles && ok; ++i) {
+      const int sb = NQ == 1 ? (i & 1) : qt;
+      const int ph = NQ == 1 ? ((i >> 1) & 1) : (i & 1);
+      const int t0 = i * kTile;
+      const int pg = pg_next;
+      if (i + 1 < ntiles) pg_next = seg_page_of(i + 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], ph, abort_flag));
+      if (!ok) break;
+      const uint32_t bad = __ballot_sync(0xffffffffu, pg < 0);  // bit s: segment s missing
+      if (warp == 2 && lane == 0) PF_TRACE(4, i);
+      tc_fence_after_sync();
+      const uint32_t sa = tmem + lane_base + sb * kTile;
+      // mask: the causal edge of this row (tokens >= vis, which also covers tokens past
+      // the context) and missing pages
+      uint32_t mw[4];
+      bool all = true;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = vis - t0 - 32 * k;
+        mw[k] = r >= 32 ? 0xffffffffu : (r <= 0 ? 0u : (1u << r) - 1u);
+      }
+      if (bad != 0u) {
+#pragma unroll 1
+        for (int sgi = 0; sgi < nseg; ++sgi) {
+          if (!((bad >> sgi) & 1u)) continue;
+          const int t = sgi * seg_rows;  // segment's first token in the tile
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (seg_rows >= 32) {
+              if (32 * k >= t && 32 * k < t + seg_rows) mw[k] = 0u;
+            } else if (k == (t >> 5)) {
+              mw[k] &= ~(((1u << seg_rows) - 1u) << (t & 31));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) all = all && mw[k] == 0xffffffffu;
+      all = all || qrow < 0;  // padding rows are never written
+      const bool masked = !__all_sync(0xffffffffu, all);
+      auto apply_mask = [&](float* v, int c0, int n) {
+        if (masked) {
+#pragma unroll
+          for (int e = 0; e < n; ++e)
+            if (!((mw[(c0 + e) >> 5] >> ((c0 + e) & 31)) & 1u)) v[e] = -INFINITY;
+        }
+      };
+      // P = 2^(s sc - ref) of columns 64h .. 64h + 63 as 16-bit pairs into w, their sum into
+      // acc and their raw maximum into mx8
+      auto p_half = [&](int h, float ref, uint32_t (&w)[32], uint64_t (&acc)[4], float (&mx8)[8]) {
+        float v[64];
+        tmem_ld64(sa + 64 * h, v);
+        apply_mask(v, 64 * h, 64);
+#pragma unroll
+        for (int e = 0; e < 64; e += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], v[e + k], v[e + 8 + k]);
+        const uint64_t sc2 = f2_pack(sc, sc), nref2 = f2_pack(-ref, -ref);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(v[2 * e], v[2 * e + 1]), sc2, nref2), x0, x1);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);  // 0 for masked (-inf)
+          acc[e & 3] = f2_add(acc[e & 3], f2_pack(p0, p1));
+          w[e] = pack2<QT>(p0, p1);
+        }
+      };
+      // both halves: P into w0 / w1; returns the row sum, the raw row maximum into mxr
+      auto p_tile = [&](float ref, uint32_t (&w0)[32], uint32_t (&w1)[32], float& mxr) -> float {
+        uint64_t acc[4];
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k] = f2_pack(0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+        p_half(0, ref, w0, acc, mx8);
+        reg_fence32(w0);
+        p_half(1, ref, w1, acc, mx8);
+        mxr = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float a0, a1;
+          f2_unpack(acc[k], a0, a1);
+          sum += a0 + a1;
+        }
+        return sum;
+      };
+      // One pass in the common case: P against the current reference m, computed together
+      // with the tile's maximum, is kept unless a row's maximum grew by more than 2^8 (the
+      // lazy rescale threshold); then, and on a row's first visible tile, P is computed again
+      // against the new maximum. S stays in TMEM until P is stored.
+      uint32_t w0[32], w1[32];
+      float lsum, mxr;
+      bool need;
+      float m_new, alpha;
+      // lazy reference: move it (and rescale O) only when the maximum grows by > 2^8
+      auto new_ref = [&]() {
+        const float mx = mxr * sc;  // the scale is > 0
+        need = mx > m + 8.0f;
+        m_new = need ? mx : m;
+        alpha = need ? exp2f(m - m_new) : 1.0f;  // 0 when m was -inf
+      };
+      if (__any_sync(0xffffffffu, m == -INFINITY)) {
+        // a row's first visible tile: the maximum first (64 columns at a time)
+        float mx8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          float v[64];
+          tmem_ld64(sa + 64 * h, v);
+          apply_mask(v, 64 * h, 64);
+#pragma unroll
+          for (int e = 0; e < 64; e += 16)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], v[e + k], v[e + 8 + k]);
+        }
+        mxr = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        new_ref();
+        float unused;
+        lsum = p_tile(m_new == -INFINITY ? 0.0f : m_new, w0, w1, unused);
+      } else {
+        lsum = p_tile(m, w0, w1, mxr);
+        new_ref();
+        if (__any_sync(0xffffffffu, need)) {
+          float unused;
+          lsum = p_tile(m_new, w0, w1, unused);
+        }
+      }
+      if (warp == 2 && lane == 0) PF_TRACE(5, i);
+      m = m_new;
+      l = l * alpha + lsum;
+      // P over the first 64 columns of this S buffer
+      tmem_st32(sa, w0);
+      tmem_st32(sa + 32, w1);
+      if (warp == 2 && lane == 0) PF_TRACE(10, i);
+      // PV(i-1) done: O may be rescaled, and the next wait on this O barrier is for PV(i)
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&ofull[qt], (i - 1) & 1, abort_flag));
+        if (!ok) break;
+        if (warp == 2 && lane == 0) PF_TRACE(11, i);
+        tc_fence_after_sync();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < kD / 16; ++c) {
+            float v[16];
+            tmem_ld16(tmem + lane_base + o_col + 16 * c, v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] *= alpha;
+            tmem_st16(tmem + lane_base + o_col + 16 * c, v);
+          }
+        }
+      }
+      tmem_wait_st();
+      if (warp == 2 && lane == 0) PF_TRACE(6, i);
+      // V rows past the last visible token of every row may hold anything (the page's
+      // other tokens or never-written memory): zero them so that 0 * V stays 0. Query
+      // tile 0 does it, before its PV product, which is issued before tile 1's.
+      if (qt == 0 && t0 + kTile > nkv) {
+        const int st = i % kVS;
+        ok = __all_sync(0xffffffffu, mbar_wait(&vfull[st], (i / kVS) & 1, abort_flag));
+        if (!ok) break;
+        if (t0 + rt >= nkv) {
+          uint8_t* vrow = smem + L::V0 + st * TILE + rt * 128;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            *reinterpret_cast<uint4*>(vrow + k * 16) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(vrow + BLK + k * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfull[sb]);
+      if (warp == 2 && lane == 0) PF_TRACE(7, i);
+      if (warp == 5 && lane == 0) PF_TRACE(15, i);
+    }
+    if (!ok) *abort_flag = 1;
+    // ---- epilogue: out = O / l (0/0 = NaN for a row that sees nothing)
+    if (ok && ntiles > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&ofull[qt], (ntiles - 1) & 1, abort_flag));
+      if (!ok) *abort_flag = 1;
+      tc_fence_after_sync();
+    }
+    const float inv = 1.0f / l;
+    QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)(qrow >= 0 ? qrow : 0) * p.o_st + (int64_t)hrow * p.o_sh;
+#pragma unroll 1
+    for (int c = 0; c < kD / 16; ++c) {
+      float v[16];
+      if (ntiles > 0 && ok) {
+        tmem_ld16(tmem + lane_base + o_col + 16 * c, v);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+      }
+      if (qrow >= 0) {
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) w[e >> 1] = pack2<QT>(v[e] * inv, v[e + 1] * inv);
+        *reinterpret_cast<uint4*>(dst + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst + 16 * c + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+typedef CUresult (*PfEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PfEncodeTiledFn pf_encode_fn() {
+  static PfEncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfEncodeTiledFn>(f);
+    tried = true;
+  }
+  return fn;
+}
+
+// tcgen05 path: 16-bit caches, head_dim 128, GQA group <= 128, power-of-two block size
+// >= 8, 16-byte aligned query and output rows.
+bool pf05_supported(const PrefillParams& p, int q_dtype, int cache_dtype) {
+  if (p.head_dim != pf05::kD || p.group > pf05::kRows || !(p.qk_scale_log2 > 0.0f)) return false;
+  if (q_dtype != MKV_DTYPE_BF16 && q_dtype != MKV_DTYPE_F16) return false;
+  if (cache_dtype != q_dtype) return false;
+  if (p.block_size < 8 || (p.block_size & (p.block_size - 1)) != 0) return false;
+  if (((uintptr_t)p.out & 15u) || (p.o_st * 2) % 16 != 0 || (p.o_sh * 2) % 16 != 0) return false;
+  return pf_encode_fn() != nullptr;
+}
+
+template <typename QT, int NQ>
+int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t stream) {
+  using L = pf05::Layout<NQ>;
+  PfEncodeTiledFn enc = pf_encode_fn();
+  const cuuint64_t dims[2] = {(cuuint64_t)p.num_kv_heads * pf05::kD,
+                              (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size};
+  const cuuint64_t strides[1] = {(cuuint64_t)p.num_kv_heads * pf05::kD * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)(p.block_size < pf05::kTile ? p.block_size : pf05::kTile)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = cache_dtype == MKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap km, vm;
+  CUresult r = enc(&km, dt, 2, const_cast<uint8_t*>(p.k_cache), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS)
+    r = enc(&vm, dt, 2, const_cast<uint8_t*>(p.v_cache), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc05_kernel<QT, NQ>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill tc05 smem)");
+    configured[dev] = true;
+  }
+  PrefillParams q = p;
+  q.qb = NQ * pf05::kRows / p.group;  // query tokens per CTA: 128 NQ rows
+  const int64_t units = (int64_t)q.total_q / q.qb + q.num_seqs;
+  dim3 grid((unsigned)units, q.num_kv_heads, 1);
+  paged_prefill_tc05_kernel<QT, NQ><<<grid, L::kThreads, L::BYTES, stream>>>(q, km, vm, (int)units);
+  return cuda_status(cudaGetLastError(), "paged_prefill_tc05 launch");
+}
+
+// Two query tiles per CTA keep the tensor core busy while a tile's softmax runs, but
+// leave more rows idle when sequences contribute few rows. They are used when the
+// average sequence holds at least two CTAs' worth of rows and the grid still fills the
+// GPU twice over.
+// MKV_PREFILL_QTILES=1 or 2 in the environment overrides the choice (tests, tuning).
+template <typename QT>
+int launch_prefill_tc05_auto(const PrefillParams& p, int cache_dtype, cudaStream_t stream) {
+  const char* force = getenv("MKV_PREFILL_QTILES");
+  if (force != nullptr && force[0] == '1') return launch_prefill_tc05<QT, 1>(p, cache_dtype, stream);
+  if (force != nullptr && force[0] == '2') return launch_prefill_tc05<QT, 2>(p, cache_dtype, stream);
+  const int64_t rows = (int64_t)p.total_q * p.group;
+  const int64_t ctas2 = (rows + 2 * pf05::kRows - 1) / (2 * pf05::kRows) * p.num_kv_heads;
+  if (rows >= (int64_t)p.num_seqs * 4 * pf05::kRows && ctas2 >= 2 * kNumSMs)
+    return launch_prefill_tc05<QT, 2>(p, cache_dtype, stream);
+  return launch_prefill_tc05<QT, 1>(p, cache_dtype, stream);
+}
+
 // ============================================================ CUDA-core kernel
 // One warp per (query token, query head): lanes take 32 cached tokens at a time, the
 // warp keeps the online softmax state, and each lane accumulates head_dim / 32 outputs.
@@ -538,8 +1173,10 @@ int launch_prefill_generic(const PrefillParams& p, cudaStream_t stream) {
 }
 
 template <typename QT>
-int dispatch_prefill(const PrefillParams& p, int cache_dtype, int64_t units, cudaStream_t s) {
+int dispatch_prefill(const PrefillParams& p, int cache_dtype, int64_t units, cudaStream_t s,
+                     int q_dtype) {
   if constexpr (!std::is_same<QT, float>::value) {
+    if (pf05_supported(p, q_dtype, cache_dtype)) return launch_prefill_tc05_auto<QT>(p, cache_dtype, s);
     if ((p.head_dim == 128 || p.head_dim == 64) && p.group <= kPRows) {
       if (cache_dtype == MKV_DTYPE_FP8_E4M3)
         return p.head_dim == 128 ? launch_prefill_tc<QT, fp8, 128>(p, units, s)
@@ -656,8 +1293,14 @@ extern "C" int mkv_paged_prefill(
   const int64_t units = total_q / p.qb + num_seqs;
   cudaStream_t s = (cudaStream_t)stream;
   switch (q_dtype) {
-    case MKV_DTYPE_F32: return dispatch_prefill<float>(p, cache_dtype, units, s);
-    case MKV_DTYPE_F16: return dispatch_prefill<f16>(p, cache_dtype, units, s);
-    default: return dispatch_prefill<bf16>(p, cache_dtype, units, s);
+    case MKV_DTYPE_F32: return dispatch_prefill<float>(p, cache_dtype, units, s, q_dtype);
+    case MKV_DTYPE_F16: return dispatch_prefill<f16>(p, cache_dtype, units, s, q_dtype);
+    default: return dispatch_prefill<bf16>(p, cache_dtype, units, s, q_dtype);
   }
 }
+
+#ifdef MKV_PREFILL_TRACE
+extern "C" __attribute__((visibility("default"))) int mkv_debug_prefill_trace(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, mkv::g_pftrace, sizeof(mkv::g_pftrace));
+}
+#endif

@@ -75,6 +75,17 @@ def close(out, ref, dtype):
     assert bool((diff <= atol + rtol * ref[~nan].abs()).all()), f"max abs err {float(diff.max()):.3e}"
 
 
+@pytest.fixture(params=["auto", "1", "2"])
+def qtiles(request, monkeypatch):
+    """The tensor-core prefill's query tiles per CTA: the library's choice, or forced to
+    one or two (MKV_PREFILL_QTILES, read per call)."""
+    if request.param == "auto":
+        monkeypatch.delenv("MKV_PREFILL_QTILES", raising=False)
+    else:
+        monkeypatch.setenv("MKV_PREFILL_QTILES", request.param)
+    return request.param
+
+
 CTX = [300, 64, 1, 130, 17, 700]
 CHUNK = [300, 5, 1, 65, 17, 256]  # full prefill, short extend, single token, chunked
 
@@ -82,7 +93,7 @@ CHUNK = [300, 5, 1, 65, 17, 256]  # full prefill, short extend, single token, ch
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("H,KVH", [(8, 8), (16, 4), (32, 2), (6, 2)])
 @pytest.mark.parametrize("BS", [16, 256])
-def test_prefill_matches_oracle(dtype, H, KVH, BS):
+def test_prefill_matches_oracle(dtype, H, KVH, BS, qtiles):
     D = 128
     case = make_case(CTX, CHUNK, H, KVH, D, BS, dtype, seed=H * 3 + KVH + BS)
     out, ref = run(case, H, KVH, D, BS, 1.0 / math.sqrt(D))
@@ -105,7 +116,7 @@ def test_prefill_quantised_caches(cache, dtype):
     close(out, ref, dtype)
 
 
-def test_prefill_invalid_pages_and_empty_rows():
+def test_prefill_invalid_pages_and_empty_rows(qtiles):
     """-1 pages inside a context are skipped; a query whose visible range holds only
     missing pages gives NaN."""
     case = list(make_case([40, 20], [40, 10], 8, 2, 128, 16, torch.bfloat16, seed=3))
@@ -119,7 +130,21 @@ def test_prefill_invalid_pages_and_empty_rows():
     close(out, ref, torch.bfloat16)
 
 
-def test_prefill_long_chunk():
+@pytest.mark.parametrize("BS", [16, 64, 256])
+def test_prefill_missing_pages_by_block_size(BS, qtiles):
+    """Missing pages that cover a part of a 128-token tile (BS 16, 64) or a whole tile and
+    more (BS 256), on top of the causal edge."""
+    case = list(make_case([700, 600], [300, 600], 16, 4, 128, BS, torch.bfloat16, seed=BS))
+    bt = case[3].clone()
+    bt[0, 1] = -1        # sequence 0: tokens BS .. 2 BS - 1 missing
+    bt[1, 0] = 10 ** 6   # sequence 1: its first page out of range
+    case[3] = bt
+    out, ref = run(tuple(case), 16, 4, 128, BS, 0.09)
+    assert torch.isnan(ref).any()
+    close(out, ref, torch.bfloat16)
+
+
+def test_prefill_long_chunk(qtiles):
     """A 2048-token chunk extending a 4096-token prefix (many KV tiles, causal edge in
     the middle of a tile), GQA 4."""
     case = make_case([6144, 900], [2048, 900], 32, 8, 128, 256, torch.bfloat16, seed=11)
@@ -139,7 +164,7 @@ def test_golden_prefill_through_cuda():
     close(out, t("out").double(), torch.float32)
 
 
-def test_prefill_matches_decode_for_last_token():
+def test_prefill_matches_decode_for_last_token(qtiles):
     """For each sequence, the prefill row of its last context token equals the decode of
     that sequence over the same cache."""
     H, KVH, D, BS = 32, 8, 128, 16
