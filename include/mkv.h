@@ -260,6 +260,13 @@ MKV_API int mkv_paged_decode_quant_per_token_head(
  * v_scale, or FP8_E4M3 / INT8 with per-(page, row, kv head) k_scales / v_scales (pass
  * the other pair as NULL). Tensor cores for bf16/f16 queries with head_dim 64 or 128;
  * CUDA cores otherwise (head_dim a multiple of 16, at most 256).
+ *
+ * workspace (16-byte aligned) may be NULL. With 8-bit caches and long chunks, a
+ * workspace of at least mkv_paged_prefill_workspace_bytes(...) lets the call convert
+ * each visible page to 16 bits once, into the workspace, and run the 16-bit tensor-core
+ * kernel over it; without one, the 8-bit tiles are converted inside the attention
+ * kernel, once per query block. Both compute the same attention. Its contents on entry
+ * do not matter.
  */
 MKV_API int mkv_paged_prefill(
     const void* query, int64_t q_stride_token, int64_t q_stride_head, int32_t q_dtype,
@@ -270,7 +277,23 @@ MKV_API int mkv_paged_prefill(
     int32_t context_lens_index_type, const void* cu_seqlens_q, int32_t cu_seqlens_index_type,
     const void* positions, int32_t positions_index_type, int32_t num_seqs, int64_t total_q,
     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
-    int64_t out_stride_token, int64_t out_stride_head, void* stream);
+    int64_t out_stride_token, int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+    void* stream);
+
+/*
+ * Workspace bytes mkv_paged_prefill uses for the given shape: 2 x num_seqs x
+ * max_num_blocks x block_size x num_kv_heads x head_dim 16-bit values (the visible pages
+ * converted to the query dtype) when the cache is 8-bit (FP8_E4M3 or INT8), the query
+ * bf16 or f16, head_dim 128, num_heads / num_kv_heads <= 128, block_size a power of two
+ * >= 8, the sequences hold at least 512 query rows (query tokens x GQA group) on average,
+ * and the total is at most 1 GiB; 0 otherwise (no workspace is used). Host-only: reads
+ * no device memory.
+ */
+MKV_API size_t mkv_paged_prefill_workspace_bytes(int32_t num_seqs, int64_t total_q,
+                                                 int32_t num_heads, int32_t num_kv_heads,
+                                                 int32_t head_dim, int32_t block_size,
+                                                 int32_t max_num_blocks, int32_t q_dtype,
+                                                 int32_t cache_dtype);
 
 /*
  * Paged-attention decode that allocates nothing and needs no workspace argument.

@@ -49,7 +49,8 @@ SIGNATURES: dict[str, tuple] = {
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),
     "mkv_paged_prefill": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
-        _p, _i32, _p, _i32, _i32, _i64, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p]),
+        _p, _i32, _p, _i32, _i32, _i64, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _p]),
+    "mkv_paged_prefill_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "mkv_paged_decode_fp8": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),

@@ -6,8 +6,9 @@
 Each case is (sequences, cached prefix tokens, chunk tokens): every sequence appends a
 chunk of query tokens after its prefix, so query position p sees min(p + 1, context)
 cached tokens. H=32 query heads, 8 KV heads, head_dim 128, 256-token pages in a random
-order per sequence, bf16 queries; the cache is bf16, e4m3 with a per-tensor scale, or
-int8 with per-(token, head) scales. Inputs are synthetic (seeded normal values).
+order per sequence, bf16 queries; the cache is bf16, e4m3 with a per-tensor scale or
+per-(token, head) scales, or int8 with per-(token, head) scales. Inputs are synthetic
+(seeded normal values).
 
 Throughput counts 4 · Σ visible tokens · H · D FLOPs per call, the work of QKᵀ and PV
 over the visible tokens only, and times CUDA-graph replays with CUDA events. One JSON
@@ -31,7 +32,8 @@ attn = importlib.import_module(os.path.basename(_HERE) + ".layers.attention")
 
 H, KVH, D, BS = 32, 8, 128, 256
 CASES = [(8, 0, 2048, "auto"), (8, 4096, 2048, "auto"), (4, 16384, 4096, "auto"),
-         (8, 4096, 2048, "fp8_per_tensor"), (8, 4096, 2048, "int8_per_token_head")]
+         (8, 4096, 2048, "fp8_per_tensor"), (8, 4096, 2048, "fp8_per_token_head"),
+         (8, 4096, 2048, "int8_per_token_head")]
 
 
 def make(nseq: int, prefix: int, chunk: int, mode: str, seed: int = 0):
@@ -56,8 +58,12 @@ def make(nseq: int, prefix: int, chunk: int, mode: str, seed: int = 0):
         kw = dict(k_scale=torch.full((1,), 0.025, device="cuda"), v_scale=torch.full((1,), 0.025, device="cuda"),
                   kv_cache_dtype=mode)
     else:
-        kc = torch.randint(-127, 128, shape, device="cuda", generator=g, dtype=torch.int8)
-        vc = torch.randint(-127, 128, shape, device="cuda", generator=g, dtype=torch.int8)
+        if mode == "fp8_per_token_head":
+            kc = (torch.randn(shape, device="cuda", generator=g) * 40).to(torch.float8_e4m3fn)
+            vc = (torch.randn(shape, device="cuda", generator=g) * 40).to(torch.float8_e4m3fn)
+        else:
+            kc = torch.randint(-127, 128, shape, device="cuda", generator=g, dtype=torch.int8)
+            vc = torch.randint(-127, 128, shape, device="cuda", generator=g, dtype=torch.int8)
         kw = dict(k_scale=torch.rand(nb, BS, KVH, device="cuda", generator=g) * 0.02,
                   v_scale=torch.rand(nb, BS, KVH, device="cuda", generator=g) * 0.02, kv_cache_dtype=mode)
     vis = nseq * sum(min(ctx, p + 1) for p in range(prefix, ctx))

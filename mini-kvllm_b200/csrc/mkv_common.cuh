@@ -77,6 +77,17 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
   return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
+// Four e4m3 bytes of w (byte i = element i) -> two half2 words (elements 0,1 and 2,3),
+// exact: one cvt.rn.f16x2.e4m3x2 per pair, on the halves of w.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& h01, uint32_t& h23) {
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "mov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(h01), "=r"(h23)
+      : "r"(w));
+}
+
 // ---------------------------------------------------------------- index loads
 template <typename I> __device__ __forceinline__ int64_t load_index(const I* p, int64_t i) {
   return (int64_t)__ldg(p + i);

@@ -69,6 +69,12 @@ struct PrefillParams {
   const float* v_scales;
   void* out;
   int64_t o_st, o_sh;  // elements
+  // tcgen05 kernel over dequantised pages: page blk of sequence seq is scratch page
+  // seq * max_blocks + blk of scratch_k / scratch_v (16-bit, the cache's row layout);
+  // page validity still comes from the block table
+  int scratch;
+  const uint8_t* scratch_k;
+  const uint8_t* scratch_v;
 };
 
 __device__ __forceinline__ int64_t ld_idx(const void* p, int i64, int64_t i) {
@@ -442,6 +448,41 @@ paged_prefill_tc_kernel(const PrefillParams p) {
 // Every mbarrier wait is bounded (sm100::kWaitCycles); a role that gives up raises the
 // CTA abort flag, the others stop, in-flight TMA loads and MMAs are waited for (bounded)
 // and TMEM is freed.
+// 16 bytes of an 8-bit page row (CT = e4m3 or int8; byte i = element i) -> 16 values of
+// QT in lo (elements 0-7) and hi (8-15). Conversions to half are exact; bf16 goes through
+// fp32 (exact for e4m3 and int8 values). kTok: times the token's scale, in fp32 for bf16
+// (one rounding) and in half for f16.
+template <typename QT, typename CT, bool kTok>
+__device__ __forceinline__ uint32_t pf_to_qt(uint32_t h, float scale) {
+  if constexpr (!kTok && std::is_same<QT, f16>::value) {
+    return h;
+  } else if constexpr (kTok && std::is_same<QT, f16>::value) {
+    const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&h), __float2half2_rn(scale));
+    return *reinterpret_cast<const uint32_t*>(&r);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    return kTok ? pack2<QT>(f.x * scale, f.y * scale) : pack2<QT>(f.x, f.y);
+  }
+}
+template <typename QT, typename CT, bool kTok>
+__device__ __forceinline__ void pf_cvt16(const uint4 raw, float scale, uint4& lo, uint4& hi) {
+  uint32_t h[8];
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if constexpr (std::is_same<CT, int8_t>::value) {
+      h[2 * j] = s8x2_to_f16x2((uint16_t)w[j]);
+      h[2 * j + 1] = s8x2_to_f16x2((uint16_t)(w[j] >> 16));
+    } else {
+      e4m3x4_to_f16x2x2(w[j], h[2 * j], h[2 * j + 1]);
+    }
+  }
+  lo = make_uint4(pf_to_qt<QT, CT, kTok>(h[0], scale), pf_to_qt<QT, CT, kTok>(h[1], scale),
+                  pf_to_qt<QT, CT, kTok>(h[2], scale), pf_to_qt<QT, CT, kTok>(h[3], scale));
+  hi = make_uint4(pf_to_qt<QT, CT, kTok>(h[4], scale), pf_to_qt<QT, CT, kTok>(h[5], scale),
+                  pf_to_qt<QT, CT, kTok>(h[6], scale), pf_to_qt<QT, CT, kTok>(h[7], scale));
+}
+
 #ifdef MKV_PREFILL_TRACE
 // Debug-only event timeline (globaltimer, ns) of one CTA: [event][tile].
 __device__ unsigned long long g_pftrace[16][64];
@@ -466,30 +507,36 @@ constexpr int kD = 128;
 constexpr uint32_t kTmemCols = 512;  // S buffers (P over their first 64 columns) at 0 / 128, O at 256 (+128)
 constexpr int BLK = 128 * 128;       // 128 rows x 128 bytes: one 64-column half
 constexpr int TILE = 2 * BLK;        // 128 rows x 256 bytes
-template <int NQ>
+template <int NQ, bool kByte = false>
 struct Layout {
-  static constexpr int kThreads = 64 + 128 * NQ;
-  static constexpr int kKStages = 3;
-  static constexpr int kVStages = NQ == 1 ? 3 : 2;
+  static constexpr int kConvWarps = kByte ? 4 : 0;  // 8-bit pages: converter warpgroup
+  static constexpr int kThreads = 64 + 128 * NQ + 32 * kConvWarps;
+  static constexpr int kKStages = kByte ? 2 : 3;
+  static constexpr int kVStages = kByte ? 2 : (NQ == 1 ? 3 : 2);
+  static constexpr int kRStages = kByte ? 2 : 0;
   static constexpr int Q0 = 0;                           // [NQ] query tiles
-  static constexpr int K0 = Q0 + NQ * TILE;              // [stage] K tile
-  static constexpr int V0 = K0 + kKStages * TILE;        // [stage] V tile
-  static constexpr int BAR0 = V0 + kVStages * TILE;
-  // K full/empty, V full/empty, q, s[2], p[2], o[NQ], drain
-  static constexpr int NBAR = 2 * kKStages + 2 * kVStages + 1 + 2 + 2 + NQ + 1;
+  static constexpr int K0 = Q0 + NQ * TILE;              // [stage] K tile (16-bit)
+  static constexpr int V0 = K0 + kKStages * TILE;        // [stage] V tile (16-bit)
+  static constexpr int R0 = V0 + kVStages * TILE;        // [stage][K, V] 8-bit tiles, 128 x 128 B
+  static constexpr int BAR0 = R0 + kRStages * 2 * BLK;
+  // K full/empty, V full/empty, raw full/empty, q, s[2], p[2], o[NQ], drain
+  static constexpr int NBAR = 2 * kKStages + 2 * kVStages + 2 * kRStages + 1 + 2 + 2 + NQ + 1;
   static constexpr int MISC0 = BAR0 + NBAR * 8;          // tmem base, abort flag, nkv
   static constexpr int BYTES = MISC0 + 16 + 1024;        // + alignment slack
   static_assert(BYTES <= 232448, "shared memory per CTA");
+  static_assert(!kByte || NQ == 1, "8-bit pages: one query tile (the converters take the other's warps)");
 };
 }  // namespace pf05
 
-template <typename QT, int NQ>
-__global__ void __launch_bounds__(pf05::Layout<NQ>::kThreads, 1)
+template <typename QT, int NQ, typename CT, bool kTok>
+__global__ void __launch_bounds__(pf05::Layout<NQ, sizeof(CT) == 1>::kThreads, 1)
 paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap vmap, int units) {
   using namespace pf05;
-  using L = Layout<NQ>;
-  constexpr int kKS = L::kKStages, kVS = L::kVStages;
+  constexpr bool kByte = sizeof(CT) == 1;  // e4m3 or int8 pages, converted by warps 6-9
+  using L = Layout<NQ, kByte>;
+  constexpr int kKS = L::kKStages, kVS = L::kVStages, kRS = L::kRStages;
+  constexpr int kSoftmaxEnd = 2 + 4 * NQ;  // softmax warps 2 .. kSoftmaxEnd - 1
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR0);
@@ -497,7 +544,9 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
   uint64_t* kempty = kfull + kKS;
   uint64_t* vfull = kempty + kKS;
   uint64_t* vempty = vfull + kVS;
-  uint64_t* qfull = vempty + kVS;
+  uint64_t* rfull = vempty + kVS;  // 8-bit tiles landed (TMA)
+  uint64_t* rempty = rfull + kRS;  // 8-bit tiles converted
+  uint64_t* qfull = rempty + kRS;
   uint64_t* sfull = qfull + 1;
   uint64_t* pfull = sfull + 2;
   uint64_t* ofull = pfull + 2;
@@ -515,13 +564,19 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
   const int64_t ctx = pf_ctx(p, seq);
 
   if (tid == 0) {
+    // 16-bit tiles are filled by TMA (one arrival + bytes); converted ones by the four
+    // converter warps
     for (int s = 0; s < kKS; ++s) {
-      mbar_init(&kfull[s], 1);
+      mbar_init(&kfull[s], kByte ? 4 : 1);
       mbar_init(&kempty[s], 1);
     }
     for (int s = 0; s < kVS; ++s) {
-      mbar_init(&vfull[s], 1);
+      mbar_init(&vfull[s], kByte ? 4 : 1);
       mbar_init(&vempty[s], 1);
+    }
+    for (int s = 0; s < kRS; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 4);
     }
     mbar_init(qfull, 4 * NQ);
     for (int b = 0; b < 2; ++b) {
@@ -540,12 +595,14 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_base_s;
 
-  // softmax warp w >= 2 serves query tile qt = (w - 2) / 4; its thread owns the tile's row
-  // rt = 32 * (w % 4) + lane, which is also its TMEM lane (warp w reaches lanes 32 (w % 4) ..)
-  const int qt = warp >= 2 ? (warp - 2) >> 2 : 0;
+  // softmax warp w in [2, kSoftmaxEnd) serves query tile qt = (w - 2) / 4; its thread owns
+  // the tile's row rt = 32 * (w % 4) + lane, which is also its TMEM lane (warp w reaches
+  // lanes 32 (w % 4) ..)
+  const bool softmax_warp = warp >= 2 && warp < kSoftmaxEnd;
+  const int qt = softmax_warp ? (warp - 2) >> 2 : 0;
   const int rt = 32 * (warp & 3) + lane;
   int vis = 0, qrow = -1, hrow = 0;
-  if (warp >= 2) {
+  if (softmax_warp) {
     const int row = kRows * qt + rt;
     const int tok = row / p.group, gh = row - tok * p.group;
     if (tok < u.nq) {
@@ -577,66 +634,102 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       }
       return pg;
     };
-    // K(t) and V(t) are issued in the order K(0), K(1), V(0), K(2), V(1), ...
-    auto issue = [&](int t, bool is_v, int seg_page) -> bool {
-      const int ns = is_v ? kVS : kKS;
-      const int st = t % ns;
-      uint64_t* empty = is_v ? vempty : kempty;
-      uint64_t* full = is_v ? vfull : kfull;
-      if (!__all_sync(0xffffffffu, mbar_wait(&empty[st], ((t / ns) & 1) ^ 1, abort_flag))) return false;
-      if (lane == 0) PF_TRACE(is_v ? 9 : 0, t);
-      uint8_t* dst = smem + (is_v ? L::V0 : L::K0) + st * TILE;
-      uint32_t bytes = 0;
-      for (int sgi = 0; sgi < nseg; ++sgi) {
-        const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
-        if (pg >= 0) {
-          bytes += 2u * seg_rows * 128u;
-        } else if (is_v) {  // a missing segment's V rows: zeros (P is 0 there; 0 * garbage may not be)
-          for (int k = lane; k < 2 * seg_rows * 8; k += 32) {
-            const int b = k / (seg_rows * 8), kk = k - b * seg_rows * 8;
-            *reinterpret_cast<uint4*>(dst + b * BLK + sgi * seg_rows * 128 + kk * 16) = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (kByte) {
+      // 8-bit pages: K(t) and V(t) together into one raw stage; missing segments are not
+      // loaded (the converters write zeros for their rows)
+      int nr = 0;  // raw stages issued
+      bool ok = true;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;  // warp-uniform exit
+        const int seg_page = seg_page_of(t);
+        const int rs = t % kRS;
+        ok = __all_sync(0xffffffffu, mbar_wait(&rempty[rs], ((t / kRS) & 1) ^ 1, abort_flag));
+        if (!ok) break;
+        uint32_t bytes = 0;
+        for (int sgi = 0; sgi < nseg; ++sgi)
+          if (__shfl_sync(0xffffffffu, seg_page, sgi) >= 0) bytes += 2u * seg_rows * 128u;
+        if (lane == 0) mbar_arrive_expect_tx(&rfull[rs], bytes);
+        uint8_t* dst = smem + L::R0 + rs * 2 * BLK;
+        for (int sgi = 0; sgi < nseg; ++sgi) {
+          const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
+          if (lane == 0 && pg >= 0) {
+            const int ts = t * kTile + sgi * seg_rows;
+            const int y = pg * p.block_size + (ts & (p.block_size - 1));
+            tma_load_2d(smem_u32(dst + sgi * seg_rows * 128), &kmap, kvh * kD, y, &rfull[rs]);
+            tma_load_2d(smem_u32(dst + BLK + sgi * seg_rows * 128), &vmap, kvh * kD, y, &rfull[rs]);
           }
         }
+        __syncwarp();
+        ++nr;
       }
-      if (is_v) fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes);
-      if (lane == 0 && !is_v) PF_TRACE(1, t);
-      for (int sgi = 0; sgi < nseg; ++sgi) {
-        const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
-        if (lane == 0 && pg >= 0) {
-          const int ts = t * kTile + sgi * seg_rows;
-          const int y = pg * p.block_size + (ts & (p.block_size - 1));
-          for (int b = 0; b < 2; ++b)
-            tma_load_2d(smem_u32(dst + b * BLK + sgi * seg_rows * 128), is_v ? &vmap : &kmap,
-                        kvh * kD + b * 64, y, &full[st]);
+      if (!ok) *abort_flag = 1;
+      if (lane == 0 && *abort_flag) {  // let issued loads land before the CTA exits
+        for (int k = nr - kRS; k < nr; ++k)
+          if (k >= 0) mbar_wait(&rfull[k % kRS], (k / kRS) & 1, nullptr);
+      }
+    } else {
+      // K(t) and V(t) are issued in the order K(0), K(1), V(0), K(2), V(1), ...
+      auto issue = [&](int t, bool is_v, int seg_page) -> bool {
+        const int ns = is_v ? kVS : kKS;
+        const int st = t % ns;
+        uint64_t* empty = is_v ? vempty : kempty;
+        uint64_t* full = is_v ? vfull : kfull;
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty[st], ((t / ns) & 1) ^ 1, abort_flag))) return false;
+        if (lane == 0) PF_TRACE(is_v ? 9 : 0, t);
+        uint8_t* dst = smem + (is_v ? L::V0 : L::K0) + st * TILE;
+        uint32_t bytes = 0;
+        for (int sgi = 0; sgi < nseg; ++sgi) {
+          const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
+          if (pg >= 0) {
+            bytes += 2u * seg_rows * 128u;
+          } else if (is_v) {  // a missing segment's V rows: zeros (P is 0 there; 0 * garbage may not be)
+            for (int k = lane; k < 2 * seg_rows * 8; k += 32) {
+              const int b = k / (seg_rows * 8), kk = k - b * seg_rows * 8;
+              *reinterpret_cast<uint4*>(dst + b * BLK + sgi * seg_rows * 128 + kk * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
         }
+        if (is_v) fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes);
+        if (lane == 0 && !is_v) PF_TRACE(1, t);
+        for (int sgi = 0; sgi < nseg; ++sgi) {
+          const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
+          if (lane == 0 && pg >= 0) {
+            const int ts = t * kTile + sgi * seg_rows;
+            const int pg_row = p.scratch ? seq * p.max_blocks + ts / p.block_size : pg;
+            const int y = pg_row * p.block_size + (ts & (p.block_size - 1));
+            for (int b = 0; b < 2; ++b)
+              tma_load_2d(smem_u32(dst + b * BLK + sgi * seg_rows * 128), is_v ? &vmap : &kmap,
+                          kvh * kD + b * 64, y, &full[st]);
+          }
+        }
+        __syncwarp();
+        return true;
+      };
+      int nk = 0, nv = 0;  // K and V tiles issued
+      int page_v = -1;     // segment pages of the V tile next in line
+      bool ok = true;
+      for (int t = 0; t <= ntiles && ok; ++t) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;  // warp-uniform exit
+        const int page_k = t < ntiles ? seg_page_of(t) : -1;
+        if (t < ntiles) {
+          ok = issue(t, false, page_k);
+          if (ok) ++nk;
+        }
+        if (ok && t > 0) {
+          ok = issue(t - 1, true, page_v);
+          if (ok) ++nv;
+        }
+        page_v = page_k;
       }
-      __syncwarp();
-      return true;
-    };
-    int nk = 0, nv = 0;  // K and V tiles issued
-    int page_v = -1;     // segment pages of the V tile next in line
-    bool ok = true;
-    for (int t = 0; t <= ntiles && ok; ++t) {
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;  // warp-uniform exit
-      const int page_k = t < ntiles ? seg_page_of(t) : -1;
-      if (t < ntiles) {
-        ok = issue(t, false, page_k);
-        if (ok) ++nk;
+      if (!ok) *abort_flag = 1;
+      if (lane == 0 && *abort_flag) {  // let issued loads land before the CTA exits
+        for (int k = nk - kKS; k < nk; ++k)
+          if (k >= 0) mbar_wait(&kfull[k % kKS], (k / kKS) & 1, nullptr);
+        for (int k = nv - kVS; k < nv; ++k)
+          if (k >= 0) mbar_wait(&vfull[k % kVS], (k / kVS) & 1, nullptr);
       }
-      if (ok && t > 0) {
-        ok = issue(t - 1, true, page_v);
-        if (ok) ++nv;
-      }
-      page_v = page_k;
-    }
-    if (!ok) *abort_flag = 1;
-    if (lane == 0 && *abort_flag) {  // let issued loads land before the CTA exits
-      for (int k = nk - kKS; k < nk; ++k)
-        if (k >= 0) mbar_wait(&kfull[k % kKS], (k / kKS) & 1, nullptr);
-      for (int k = nv - kVS; k < nv; ++k)
-        if (k >= 0) mbar_wait(&vfull[k % kVS], (k / kVS) & 1, nullptr);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -719,7 +812,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       mbar_wait(drain, 0, nullptr);
     }
     __syncwarp();
-  } else {
+  } else if (softmax_warp) {
     // ================================================================ softmax (warpgroup qt)
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t o_col = 256 + qt * kD;
@@ -739,7 +832,11 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       __syncwarp();
       if (lane == 0) mbar_arrive(qfull);
     }
-    const float sc = p.qk_scale_log2;
+    // per-tensor scales of 8-bit pages fold into the score scale and the output; per-(token,
+    // head) scales were applied by the converters
+    const bool tensor_scales = p.k_scale != nullptr;  // set only with per-tensor 8-bit pages
+    const float sc = p.qk_scale_log2 * (tensor_scales ? __ldg(p.k_scale) : 1.0f);
+    const float out_scale = tensor_scales ? __ldg(p.v_scale) : 1.0f;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     // page of segment `lane` of tile t (0 past the CTA's last kv token), looked up one
@@ -908,7 +1005,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       // V rows past the last visible token of every row may hold anything (the page's
       // other tokens or never-written memory): zero them so that 0 * V stays 0. Query
       // tile 0 does it, before its PV product, which is issued before tile 1's.
-      if (qt == 0 && t0 + kTile > nkv) {
+      if (!kByte && qt == 0 && t0 + kTile > nkv) {
         const int st = i % kVS;
         ok = __all_sync(0xffffffffu, mbar_wait(&vfull[st], (i / kVS) & 1, abort_flag));
         if (!ok) break;
@@ -935,7 +1032,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       if (!ok) *abort_flag = 1;
       tc_fence_after_sync();
     }
-    const float inv = 1.0f / l;
+    const float inv = out_scale / l;
     QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)(qrow >= 0 ? qrow : 0) * p.o_st + (int64_t)hrow * p.o_sh;
 #pragma unroll 1
     for (int c = 0; c < kD / 16; ++c) {
@@ -954,6 +1051,74 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         *reinterpret_cast<uint4*>(dst + 16 * c + 8) = make_uint4(w[4], w[5], w[6], w[7]);
       }
     }
+  } else if constexpr (kByte) {
+    // ================================================================ converters (warps 6-9)
+    // Thread r converts row r (kv token t0 + r) of each K and V tile from the raw 8-bit
+    // stage (128-byte swizzle) into the 16-bit tiles the MMAs read, multiplying by the
+    // token's scales in the per-(token, head) modes. Rows of missing pages and rows past
+    // the CTA's last kv token become zeros (P is 0 there, and 0 * V must stay 0).
+    const int r = 32 * (warp - kSoftmaxEnd) + lane;
+    auto page_of = [&](int t) -> int {
+      const int tok = t * kTile + r;
+      return tok < nkv ? pf_page(p, seq, tok / p.block_size) : -1;
+    };
+    auto convert_row = [&](const uint8_t* src_tile, uint8_t* dst_tile, bool valid, float scale) {
+      uint8_t* drow = dst_tile + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+        if (valid) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(src_tile + r * 128 + ((c ^ (r & 7)) << 4));
+          pf_cvt16<QT, CT, kTok>(raw, scale, lo, hi);
+        }
+        const int b = c >> 2, cc = (c & 3) * 2;  // columns 16c .. -> half b, chunks cc, cc + 1
+        *reinterpret_cast<uint4*>(drow + b * BLK + ((cc ^ (r & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4*>(drow + b * BLK + (((cc + 1) ^ (r & 7)) << 4)) = hi;
+      }
+    };
+    // the row's page is looked up two tiles ahead and its scales one tile ahead
+    auto scales_of = [&](int t, int pg, float& ks, float& vs) {
+      ks = vs = 1.0f;
+      if (kTok && pg >= 0) {
+        const int64_t slot = (int64_t)pg * p.block_size + ((t * kTile + r) & (p.block_size - 1));
+        ks = __ldg(p.k_scales + slot * p.num_kv_heads + kvh);
+        vs = __ldg(p.v_scales + slot * p.num_kv_heads + kvh);
+      }
+    };
+    bool ok = true;
+    int pg_cur = ntiles > 0 ? page_of(0) : -1;
+    int pg_nxt = ntiles > 1 ? page_of(1) : -1;
+    float ks_nxt, vs_nxt;
+    scales_of(0, pg_cur, ks_nxt, vs_nxt);
+    for (int i = 0; i < ntiles && ok; ++i) {
+      const int rs = i % kRS, st = i % kKS;  // kKS == kVS
+      const int pg = pg_cur;
+      const float ks = ks_nxt, vs = vs_nxt;
+      pg_cur = pg_nxt;
+      if (i + 2 < ntiles) pg_nxt = page_of(i + 2);
+      if (i + 1 < ntiles) scales_of(i + 1, pg_cur, ks_nxt, vs_nxt);
+      ok = mbar_wait(&rfull[rs], (i / kRS) & 1, abort_flag) &&
+           mbar_wait(&kempty[st], ((i / kKS) & 1) ^ 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* raw = smem + L::R0 + rs * 2 * BLK;
+      convert_row(raw, smem + L::K0 + st * TILE, pg >= 0, ks);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&kfull[st]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&vempty[st], ((i / kVS) & 1) ^ 1, abort_flag));
+      if (!ok) break;
+      convert_row(raw + BLK, smem + L::V0 + st * TILE, pg >= 0, vs);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&vfull[st]);
+        mbar_arrive(&rempty[rs]);
+      }
+    }
+    if (!ok) *abort_flag = 1;
   }
   tc_fence_before_sync();
   __syncthreads();
@@ -980,34 +1145,46 @@ PfEncodeTiledFn pf_encode_fn() {
   return fn;
 }
 
-// tcgen05 path: 16-bit caches, head_dim 128, GQA group <= 128, power-of-two block size
-// >= 8, 16-byte aligned query and output rows.
+// tcgen05 path: head_dim 128, GQA group <= 128, power-of-two block size >= 8, 16-byte
+// aligned output rows, 16-bit queries; the cache in the query dtype, or e4m3 (per-tensor
+// or per-(token, head) scales), or int8 (per-(token, head) scales).
 bool pf05_supported(const PrefillParams& p, int q_dtype, int cache_dtype) {
   if (p.head_dim != pf05::kD || p.group > pf05::kRows || !(p.qk_scale_log2 > 0.0f)) return false;
   if (q_dtype != MKV_DTYPE_BF16 && q_dtype != MKV_DTYPE_F16) return false;
-  if (cache_dtype != q_dtype) return false;
+  const bool same = cache_dtype == q_dtype;
+  const bool fp8 = cache_dtype == MKV_DTYPE_FP8_E4M3 && (p.k_scale != nullptr || p.k_scales != nullptr);
+  const bool int8 = cache_dtype == MKV_DTYPE_INT8 && p.k_scales != nullptr;
+  if (!same && !fp8 && !int8) return false;
   if (p.block_size < 8 || (p.block_size & (p.block_size - 1)) != 0) return false;
   if (((uintptr_t)p.out & 15u) || (p.o_st * 2) % 16 != 0 || (p.o_sh * 2) % 16 != 0) return false;
   return pf_encode_fn() != nullptr;
 }
 
-template <typename QT, int NQ>
+template <typename QT, int NQ, typename CT, bool kTok = false>
 int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t stream) {
-  using L = pf05::Layout<NQ>;
+  constexpr bool kByte = sizeof(CT) == 1;
+  using L = pf05::Layout<NQ, kByte>;
   PfEncodeTiledFn enc = pf_encode_fn();
+  // rows of the cache = (page, offset) slots; a row holds KVH heads of head_dim elements.
+  // 16-bit tiles are loaded as two 64-column halves, 8-bit tiles as one 128-byte box.
+  const int64_t map_pages = p.scratch ? (int64_t)p.num_seqs * p.max_blocks : p.num_blocks;
+  const uint8_t* kbase = p.scratch ? p.scratch_k : p.k_cache;
+  const uint8_t* vbase = p.scratch ? p.scratch_v : p.v_cache;
   const cuuint64_t dims[2] = {(cuuint64_t)p.num_kv_heads * pf05::kD,
-                              (cuuint64_t)p.num_blocks * (cuuint64_t)p.block_size};
-  const cuuint64_t strides[1] = {(cuuint64_t)p.num_kv_heads * pf05::kD * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)(p.block_size < pf05::kTile ? p.block_size : pf05::kTile)};
+                              (cuuint64_t)map_pages * (cuuint64_t)p.block_size};
+  const cuuint64_t strides[1] = {(cuuint64_t)p.num_kv_heads * pf05::kD * sizeof(CT)};
+  const cuuint32_t box[2] = {kByte ? 128u : 64u,
+                             (cuuint32_t)(p.block_size < pf05::kTile ? p.block_size : pf05::kTile)};
   const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType dt = cache_dtype == MKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt = kByte ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                       : (cache_dtype == MKV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
   CUtensorMap km, vm;
-  CUresult r = enc(&km, dt, 2, const_cast<uint8_t*>(p.k_cache), dims, strides, box, estr,
+  CUresult r = enc(&km, dt, 2, const_cast<uint8_t*>(kbase), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r == CUDA_SUCCESS)
-    r = enc(&vm, dt, 2, const_cast<uint8_t*>(p.v_cache), dims, strides, box, estr,
+    r = enc(&vm, dt, 2, const_cast<uint8_t*>(vbase), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(MKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -1015,7 +1192,7 @@ int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t st
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc05_kernel<QT, NQ>,
+    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc05_kernel<QT, NQ, CT, kTok>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill tc05 smem)");
     configured[dev] = true;
@@ -1024,25 +1201,110 @@ int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t st
   q.qb = NQ * pf05::kRows / p.group;  // query tokens per CTA: 128 NQ rows
   const int64_t units = (int64_t)q.total_q / q.qb + q.num_seqs;
   dim3 grid((unsigned)units, q.num_kv_heads, 1);
-  paged_prefill_tc05_kernel<QT, NQ><<<grid, L::kThreads, L::BYTES, stream>>>(q, km, vm, (int)units);
+  paged_prefill_tc05_kernel<QT, NQ, CT, kTok><<<grid, L::kThreads, L::BYTES, stream>>>(q, km, vm, (int)units);
   return cuda_status(cudaGetLastError(), "paged_prefill_tc05 launch");
 }
 
 // Two query tiles per CTA keep the tensor core busy while a tile's softmax runs, but
 // leave more rows idle when sequences contribute few rows. They are used when the
 // average sequence holds at least two CTAs' worth of rows and the grid still fills the
-// GPU twice over.
-// MKV_PREFILL_QTILES=1 or 2 in the environment overrides the choice (tests, tuning).
+// GPU twice over. 8-bit caches always use one (their converter warps take the other
+// tile's share of the register file).
+// MKV_PREFILL_QTILES=1 or 2 in the environment overrides the choice for 16-bit caches
+// (tests, tuning).
 template <typename QT>
 int launch_prefill_tc05_auto(const PrefillParams& p, int cache_dtype, cudaStream_t stream) {
+  if (cache_dtype == MKV_DTYPE_FP8_E4M3)
+    return p.k_scales != nullptr ? launch_prefill_tc05<QT, 1, fp8, true>(p, cache_dtype, stream)
+                                 : launch_prefill_tc05<QT, 1, fp8, false>(p, cache_dtype, stream);
+  if (cache_dtype == MKV_DTYPE_INT8) return launch_prefill_tc05<QT, 1, int8_t, true>(p, cache_dtype, stream);
   const char* force = getenv("MKV_PREFILL_QTILES");
-  if (force != nullptr && force[0] == '1') return launch_prefill_tc05<QT, 1>(p, cache_dtype, stream);
-  if (force != nullptr && force[0] == '2') return launch_prefill_tc05<QT, 2>(p, cache_dtype, stream);
+  if (force != nullptr && force[0] == '1') return launch_prefill_tc05<QT, 1, QT>(p, cache_dtype, stream);
+  if (force != nullptr && force[0] == '2') return launch_prefill_tc05<QT, 2, QT>(p, cache_dtype, stream);
   const int64_t rows = (int64_t)p.total_q * p.group;
   const int64_t ctas2 = (rows + 2 * pf05::kRows - 1) / (2 * pf05::kRows) * p.num_kv_heads;
   if (rows >= (int64_t)p.num_seqs * 4 * pf05::kRows && ctas2 >= 2 * kNumSMs)
-    return launch_prefill_tc05<QT, 2>(p, cache_dtype, stream);
-  return launch_prefill_tc05<QT, 1>(p, cache_dtype, stream);
+    return launch_prefill_tc05<QT, 2, QT>(p, cache_dtype, stream);
+  return launch_prefill_tc05<QT, 1, QT>(p, cache_dtype, stream);
+}
+
+// ============================================================ 8-bit pages -> 16-bit scratch
+// For long chunks the tcgen05 kernel reads 16-bit copies of the 8-bit pages, made once
+// per call, instead of converting every tile again in each of the many CTAs that share a
+// sequence and kv head. Page blk of sequence seq (its tokens below context_lens[seq]) is
+// converted into scratch page seq * max_blocks + blk, with the cache's row layout
+// (block_size rows of KVH x 128 values); per-(token, head) scales are applied here, and
+// per-tensor scales stay with the attention kernel. Missing pages are skipped: the
+// attention kernel masks their tokens and zero-fills their V rows.
+template <typename QT, typename CT, bool kTok>
+__global__ void __launch_bounds__(256) prefill_dequant_pages_kernel(const PrefillParams p, QT* sk, QT* sv) {
+  const int blk = blockIdx.x, seq = blockIdx.y;
+  const int64_t ctx = pf_ctx(p, seq);
+  const int64_t t0 = (int64_t)blk * p.block_size;
+  if (t0 >= ctx) return;
+  const int page = pf_page(p, seq, blk);
+  if (page < 0) return;
+  constexpr int kChunks = pf05::kD / 16;  // 16-byte raw chunks per (token, head)
+  const int per_tok = p.num_kv_heads * kChunks;
+  const int ntok = (int)(ctx - t0 < p.block_size ? ctx - t0 : p.block_size);
+  const int64_t row_elems = (int64_t)p.num_kv_heads * pf05::kD;
+  const int64_t src_row0 = (int64_t)page * p.block_size;
+  const int64_t dst_row0 = ((int64_t)seq * p.max_blocks + blk) * p.block_size;
+  for (int c = threadIdx.x; c < ntok * per_tok; c += blockDim.x) {
+    const int tok = c / per_tok, hc = c - tok * per_tok;  // hc = head * kChunks + chunk
+    const int64_t src = (src_row0 + tok) * row_elems + hc * 16;
+    const int64_t dst = (dst_row0 + tok) * row_elems + hc * 16;
+    float ks = 1.0f, vs = 1.0f;
+    if constexpr (kTok) {
+      const int64_t si = (src_row0 + tok) * p.num_kv_heads + hc / kChunks;
+      ks = __ldg(p.k_scales + si);
+      vs = __ldg(p.v_scales + si);
+    }
+    uint4 lo, hi;
+    pf_cvt16<QT, CT, kTok>(__ldg(reinterpret_cast<const uint4*>(p.k_cache + src)), ks, lo, hi);
+    *reinterpret_cast<uint4*>(sk + dst) = lo;
+    *reinterpret_cast<uint4*>(sk + dst + 8) = hi;
+    pf_cvt16<QT, CT, kTok>(__ldg(reinterpret_cast<const uint4*>(p.v_cache + src)), vs, lo, hi);
+    *reinterpret_cast<uint4*>(sv + dst) = lo;
+    *reinterpret_cast<uint4*>(sv + dst + 8) = hi;
+  }
+}
+
+constexpr size_t kScratchCap = (size_t)1 << 30;  // largest scratch the library asks for
+
+// Bytes of the 16-bit page scratch for a call, or 0 when the converter kernel is used:
+// 8-bit cache, 16-bit queries, head_dim 128, GQA group <= 128, power-of-two block size
+// >= 8, sequences with at least 512 query rows (query tokens x GQA group) on average, and
+// at most kScratchCap.
+size_t prefill_scratch_bytes(int32_t num_seqs, int64_t total_q, int32_t num_heads,
+                             int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                             int32_t max_num_blocks, int32_t q_dtype, int32_t cache_dtype) {
+  if (cache_dtype != MKV_DTYPE_FP8_E4M3 && cache_dtype != MKV_DTYPE_INT8) return 0;
+  if (q_dtype != MKV_DTYPE_BF16 && q_dtype != MKV_DTYPE_F16) return 0;
+  if (head_dim != pf05::kD || num_seqs <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads != 0) return 0;
+  const int64_t group = num_heads / num_kv_heads;
+  if (group > pf05::kRows || block_size < 8 || (block_size & (block_size - 1)) != 0) return 0;
+  if (max_num_blocks <= 0 || total_q * group < (int64_t)num_seqs * 4 * pf05::kRows) return 0;
+  const double bytes = 2.0 * num_seqs * (double)max_num_blocks * block_size * num_kv_heads * head_dim * 2.0;
+  if (bytes > (double)kScratchCap) return 0;
+  return (size_t)bytes;
+}
+
+template <typename QT, typename CT, bool kTok>
+int launch_prefill_scratch(const PrefillParams& p, int q_dtype, void* workspace, cudaStream_t s) {
+  const size_t half = (size_t)p.num_seqs * p.max_blocks * p.block_size * p.num_kv_heads * pf05::kD;
+  QT* sk = reinterpret_cast<QT*>(workspace);
+  QT* sv = sk + half;
+  dim3 grid((unsigned)p.max_blocks, (unsigned)p.num_seqs, 1);
+  prefill_dequant_pages_kernel<QT, CT, kTok><<<grid, 256, 0, s>>>(p, sk, sv);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "prefill_dequant_pages launch");
+  PrefillParams q = p;
+  q.scratch = 1;
+  q.scratch_k = reinterpret_cast<const uint8_t*>(sk);
+  q.scratch_v = reinterpret_cast<const uint8_t*>(sv);
+  q.k_scales = q.v_scales = nullptr;  // per-token scales were applied by the conversion
+  return launch_prefill_tc05_auto<QT>(q, q_dtype, s);
 }
 
 // ============================================================ CUDA-core kernel
@@ -1174,9 +1436,20 @@ int launch_prefill_generic(const PrefillParams& p, cudaStream_t stream) {
 
 template <typename QT>
 int dispatch_prefill(const PrefillParams& p, int cache_dtype, int64_t units, cudaStream_t s,
-                     int q_dtype) {
+                     int q_dtype, void* ws, size_t ws_bytes) {
   if constexpr (!std::is_same<QT, float>::value) {
-    if (pf05_supported(p, q_dtype, cache_dtype)) return launch_prefill_tc05_auto<QT>(p, cache_dtype, s);
+    if (pf05_supported(p, q_dtype, cache_dtype)) {
+      const size_t need = prefill_scratch_bytes(p.num_seqs, p.total_q, p.num_heads, p.num_kv_heads,
+                                                p.head_dim, p.block_size, p.max_blocks, q_dtype,
+                                                cache_dtype);
+      if (need > 0 && ws != nullptr && ws_bytes >= need && ((uintptr_t)ws & 15u) == 0) {
+        if (cache_dtype == MKV_DTYPE_FP8_E4M3)
+          return p.k_scales != nullptr ? launch_prefill_scratch<QT, fp8, true>(p, q_dtype, ws, s)
+                                       : launch_prefill_scratch<QT, fp8, false>(p, q_dtype, ws, s);
+        return launch_prefill_scratch<QT, int8_t, true>(p, q_dtype, ws, s);
+      }
+      return launch_prefill_tc05_auto<QT>(p, cache_dtype, s);
+    }
     if ((p.head_dim == 128 || p.head_dim == 64) && p.group <= kPRows) {
       if (cache_dtype == MKV_DTYPE_FP8_E4M3)
         return p.head_dim == 128 ? launch_prefill_tc<QT, fp8, 128>(p, units, s)
@@ -1207,7 +1480,8 @@ extern "C" int mkv_paged_prefill(
     int32_t context_lens_index_type, const void* cu_seqlens_q, int32_t cu_seqlens_index_type,
     const void* positions, int32_t positions_index_type, int32_t num_seqs, int64_t total_q,
     int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
-    int64_t out_stride_token, int64_t out_stride_head, void* stream) {
+    int64_t out_stride_token, int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+    void* stream) {
   clear_error();
   const char* fn = "mkv_paged_prefill";
   if (num_seqs < 0 || total_q < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
@@ -1289,14 +1563,23 @@ extern "C" int mkv_paged_prefill(
   p.out = out;
   p.o_st = out_stride_token;
   p.o_sh = out_stride_head;
+  p.scratch = 0;
+  p.scratch_k = p.scratch_v = nullptr;
   // query blocks: at most one partial block per sequence beyond total_q / qb full ones
   const int64_t units = total_q / p.qb + num_seqs;
   cudaStream_t s = (cudaStream_t)stream;
   switch (q_dtype) {
-    case MKV_DTYPE_F32: return dispatch_prefill<float>(p, cache_dtype, units, s, q_dtype);
-    case MKV_DTYPE_F16: return dispatch_prefill<f16>(p, cache_dtype, units, s, q_dtype);
-    default: return dispatch_prefill<bf16>(p, cache_dtype, units, s, q_dtype);
+    case MKV_DTYPE_F32: return dispatch_prefill<float>(p, cache_dtype, units, s, q_dtype, workspace, workspace_bytes);
+    case MKV_DTYPE_F16: return dispatch_prefill<f16>(p, cache_dtype, units, s, q_dtype, workspace, workspace_bytes);
+    default: return dispatch_prefill<bf16>(p, cache_dtype, units, s, q_dtype, workspace, workspace_bytes);
   }
+}
+
+extern "C" size_t mkv_paged_prefill_workspace_bytes(
+    int32_t num_seqs, int64_t total_q, int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+    int32_t block_size, int32_t max_num_blocks, int32_t q_dtype, int32_t cache_dtype) {
+  return prefill_scratch_bytes(num_seqs, total_q, num_heads, num_kv_heads, head_dim, block_size,
+                               max_num_blocks, q_dtype, cache_dtype);
 }
 
 #ifdef MKV_PREFILL_TRACE

@@ -31,6 +31,7 @@ calibrated on the device.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 from torch import nn
@@ -451,6 +452,14 @@ def paged_attention_prefill(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
             raise ValueError(f"{fn}: cache dtype {k_cache.dtype} must equal the query dtype {query.dtype}")
         cache_code = _DTYPES[k_cache.dtype]
     lib = _lib.load()
+    # 8-bit caches with long chunks: scratch for the pages converted to 16 bits once per call
+    # (MKV_PREFILL_WORKSPACE=0 disables it, for tests and tuning)
+    ws_n = lib.mkv_paged_prefill_workspace_bytes(num_seqs, total_q, num_heads, num_kv_heads, head_dim,
+                                                 block_size, block_tables.shape[1], _DTYPES[query.dtype],
+                                                 cache_code)
+    if os.environ.get("MKV_PREFILL_WORKSPACE", "1") == "0":
+        ws_n = 0
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=query.device) if ws_n else None
     with _on_device(dev):
         st = lib.mkv_paged_prefill(
             query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
@@ -459,7 +468,7 @@ def paged_attention_prefill(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
             block_tables.shape[1], lens.data_ptr(), _INDEX[lens.dtype], cu.data_ptr(),
             _INDEX[cu.dtype], pos.data_ptr(), _INDEX[pos.dtype], num_seqs, total_q, num_heads,
             num_kv_heads, head_dim, float(scale), output.data_ptr(), output.stride(0),
-            output.stride(1), _stream(dev))
+            output.stride(1), ws.data_ptr() if ws is not None else None, ws_n, _stream(dev))
     _lib.check(fn, st)
     return output
 

@@ -79,6 +79,24 @@ def test_workspace_bytes_balanced():
         (n16 * 128 * 4 + 255) // 256 * 256 + (n16 * 8 + 255) // 256 * 256 + ctr16
 
 
+def test_prefill_workspace_bytes():
+    """The prefill scratch (8-bit pages converted to 16 bits once per call): two 16-bit
+    copies of num_seqs x max_num_blocks pages for long chunks of an 8-bit cache, else 0."""
+    f = lib_mod.load().mkv_paged_prefill_workspace_bytes
+    BF16, F16, F32 = lib_mod.DTYPE_BF16, lib_mod.DTYPE_F16, lib_mod.DTYPE_F32
+    FP8, INT8 = lib_mod.DTYPE_FP8_E4M3, lib_mod.DTYPE_INT8
+    full = 2 * 8 * 24 * 256 * 8 * 128 * 2
+    assert f(8, 8 * 2048, 32, 8, 128, 256, 24, BF16, FP8) == full
+    assert f(8, 8 * 2048, 32, 8, 128, 256, 24, F16, INT8) == full
+    assert f(8, 8 * 2048, 32, 8, 128, 256, 24, BF16, BF16) == 0      # 16-bit cache
+    assert f(8, 8 * 2048, 32, 8, 128, 256, 24, F32, FP8) == 0        # fp32 queries
+    assert f(8, 8 * 2048, 32, 8, 64, 256, 24, BF16, FP8) == 0        # head_dim 64
+    assert f(8, 8 * 100, 32, 8, 128, 256, 24, BF16, FP8) == 0        # 400 rows per sequence
+    assert f(8, 8 * 128, 32, 8, 128, 256, 24, BF16, FP8) == full     # 512 rows per sequence
+    assert f(64, 64 * 2048, 32, 8, 128, 256, 128, BF16, FP8) == 0    # 4 GiB: above the 1 GiB cap
+    assert f(8, 8 * 2048, 32, 8, 128, 48, 24, BF16, FP8) == 0        # block size not a power of two
+
+
 def test_workspace_bytes_fixed_splits():
     lib = lib_mod.load()
     n = 256 * 32 * 8                      # (seq, head, split) partials

@@ -107,13 +107,49 @@ def test_prefill_other_head_dims(D):
     close(out, ref, torch.bfloat16)
 
 
-@pytest.mark.parametrize("cache", ["fp8_per_tensor", "fp8_per_token_head", "int8_per_token_head"])
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_prefill_quantised_caches(cache, dtype):
-    """Quantised caches dequantised in the kernel (the reference's TODO)."""
-    case = make_case(CTX, CHUNK, 16, 4, 128, 16, dtype, seed=7, cache=cache)
-    out, ref = run(case, 16, 4, 128, 16, 0.0883, cache=cache)
+QUANT = ["fp8_per_tensor", "fp8_per_token_head", "int8_per_token_head"]
+
+
+@pytest.fixture(params=["scratch", "in-kernel"])
+def page_conversion(request, monkeypatch):
+    """8-bit caches with long chunks: pages converted once into the workspace (the
+    default), or tile by tile inside the attention kernel (MKV_PREFILL_WORKSPACE=0)."""
+    monkeypatch.setenv("MKV_PREFILL_WORKSPACE", "1" if request.param == "scratch" else "0")
+    return request.param
+
+
+@pytest.mark.parametrize("cache", QUANT)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("BS", [16, 256])
+def test_prefill_quantised_caches(cache, dtype, BS):
+    """Quantised caches dequantised in the kernel (the reference's TODO): 16-bit queries
+    take the tcgen05 kernel (8-bit tiles converted in shared memory), fp32 queries the
+    CUDA-core kernel."""
+    case = make_case(CTX, CHUNK, 16, 4, 128, BS, dtype, seed=7 + BS, cache=cache)
+    out, ref = run(case, 16, 4, 128, BS, 0.0883, cache=cache)
     close(out, ref, dtype)
+
+
+@pytest.mark.parametrize("cache", QUANT)
+@pytest.mark.parametrize("BS", [16, 64, 256])
+def test_prefill_quantised_missing_pages(cache, BS, page_conversion):
+    """Missing and out-of-range pages with 8-bit caches: their rows convert to zeros."""
+    case = list(make_case([700, 600], [300, 600], 16, 4, 128, BS, torch.bfloat16, seed=BS + 1, cache=cache))
+    bt = case[3].clone()
+    bt[0, 1] = -1
+    bt[1, 0] = 10 ** 6
+    case[3] = bt
+    out, ref = run(tuple(case), 16, 4, 128, BS, 0.09, cache=cache)
+    assert torch.isnan(ref).any()
+    close(out, ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("cache", QUANT)
+def test_prefill_quantised_long_chunk(cache, page_conversion):
+    """A 2048-token chunk after a 4096-token prefix over an 8-bit cache, GQA 4."""
+    case = make_case([6144, 900], [2048, 900], 32, 8, 128, 256, torch.bfloat16, seed=13, cache=cache)
+    out, ref = run(case, 32, 8, 128, 256, 1.0 / math.sqrt(128), cache=cache)
+    close(out, ref, torch.bfloat16)
 
 
 def test_prefill_invalid_pages_and_empty_rows(qtiles):
