@@ -328,6 +328,48 @@ MKV_API int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq, in
                                      int64_t out_stride_seq, int64_t out_stride_head,
                                      int32_t num_splits, int32_t* invalid_count, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Tensor-parallel all-reduce fused with residual add + RMSNorm (decode step, after
+ * o_proj and down_proj). Replaces dist.all_reduce in RowParallelLinear.forward
+ * (linear.py:222-225) followed by LayerNorm.residual_rms_forward (layernorm.py:25-27):
+ *   x = sum over ranks of partial;  s = x + residual;  residual_out <- s;
+ *   out = s / sqrt(mean(s^2) + eps) * weight
+ * (residual NULL: s = x; residual_out NULL: s is not stored; residual_out may equal
+ * residual)
+ * with x and s rounded to the data type as the reference's tensor ops round them, sums in
+ * fp32 in rank order (every rank computes the same bits).
+ * partial: this rank's (num_tokens, hidden) partial, in any device memory. Each rank owns
+ * two exchange buffers of at least num_tokens x hidden values, buf_stride bytes apart,
+ * and a flag array (MKV_AR_FLAG_BYTES), all in memory the other ranks map with CUDA IPC
+ * (mkv_ipc_alloc / mkv_ipc_open, which zero-fill); peer_bufs[r] / peer_flags[r] are rank
+ * r's as this process sees them. state: this rank's 8 bytes, zeroed once; the kernel keeps
+ * the call count there (call e uses exchange buffer e % 2), so calls need no host-side
+ * counter and can be captured in a CUDA graph. Every rank makes the same calls in the
+ * same order with the same num_tokens. A wait longer than timeout_cycles (0: about a
+ * second) sets *error_flag to 1 and leaves out undefined; no host wait is involved.
+ * world_size 1: residual add + RMSNorm of partial (peer arguments and error flag unused).
+ * hidden a multiple of 8, at most 8192; bf16 or f16; 16-byte aligned buffers.
+ * ---------------------------------------------------------------------------------- */
+#define MKV_AR_MAX_RANKS 8
+#define MKV_AR_MAX_BLOCKS 128
+#define MKV_AR_FLAG_BYTES (MKV_AR_MAX_BLOCKS * MKV_AR_MAX_RANKS * 4)
+#define MKV_IPC_HANDLE_BYTES 64
+
+MKV_API int mkv_allreduce_residual_rmsnorm(
+    const void* partial, void* const* peer_bufs, int64_t buf_stride, uint32_t* const* peer_flags,
+    int32_t rank, int32_t world_size, uint32_t* state, const void* residual, void* residual_out,
+    const void* weight, void* out,
+    int64_t num_tokens, int32_t hidden, int32_t dtype, float eps, int32_t* error_flag,
+    int64_t timeout_cycles, void* stream);
+
+/* Device memory another process can map: cudaMalloc + zero fill + its IPC handle
+ * (MKV_IPC_HANDLE_BYTES written to handle_out). */
+MKV_API int mkv_ipc_alloc(size_t bytes, void** ptr, void* handle_out);
+MKV_API int mkv_ipc_free(void* ptr);
+/* Maps another process's mkv_ipc_alloc buffer into this one (peer access enabled). */
+MKV_API int mkv_ipc_open(const void* handle, void** ptr);
+MKV_API int mkv_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,6 +19,8 @@ INDEX_I32, INDEX_I64 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 FP8_CALIB_WORK_BYTES = 16
 NOALLOC_SCRATCH_BYTES = 16 << 20
+AR_MAX_RANKS, AR_MAX_BLOCKS, IPC_HANDLE_BYTES = 8, 128, 64
+AR_FLAG_BYTES = AR_MAX_BLOCKS * AR_MAX_RANKS * 4
 
 # Every symbol include/mkv.h declares, with (restype, argtypes).
 _p, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -51,6 +53,12 @@ SIGNATURES: dict[str, tuple] = {
         _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _p, _i32, _p, _i32, _i32, _i64, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _p]),
     "mkv_paged_prefill_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32]),
+    "mkv_allreduce_residual_rmsnorm": (ctypes.c_int, [
+        _p, _p, _i64, _p, _i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _i64, _p]),
+    "mkv_ipc_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_p), _p]),
+    "mkv_ipc_free": (ctypes.c_int, [_p]),
+    "mkv_ipc_open": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),
+    "mkv_ipc_close": (ctypes.c_int, [_p]),
     "mkv_paged_decode_fp8": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),

@@ -2,8 +2,9 @@
 
 This package restates, on the CPU with torch, the reference algorithm of
 heart1128/mini-kvllm for the KV append (bf16/fp16/fp32, FP8 E4M3 per-tensor, FP8 and
-INT8 per-(token, head)), the paged-attention decode and the chunked-prefill / extend
-attention over the paged cache. It is the checker, never the product: only
+INT8 per-(token, head)), the paged-attention decode, the chunked-prefill / extend
+attention over the paged cache, and the tensor-parallel all-reduce + residual add +
+RMSNorm that ends each projection. It is the checker, never the product: only
 tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may import it.
 The CUDA library (libmkv.so) never calls into it and has no CPU fallback.
 
@@ -15,6 +16,7 @@ them. See kv_oracle.py for the per-function reference citations.
 """
 from .kv_oracle import (  # noqa: F401
     FP8_E4M3_MAX,
+    allreduce_residual_rmsnorm_ref,
     INT8_MAX,
     INT8_MIN,
     decode_torch_optimized,

@@ -284,3 +284,21 @@ def paged_prefill_ref(query, k_cache, v_cache, block_tables, context_lens, cu_se
             p = torch.softmax(s, dim=-1)
             out[q] = torch.einsum("hgt,thd->hgd", p, V).reshape(num_heads, head_dim)
     return out
+
+
+def allreduce_residual_rmsnorm_ref(partials, residual, weight, eps, dtype=torch.bfloat16):
+    """The tensor-parallel all-reduce of RowParallelLinear.forward (linear.py:222-225)
+    followed by LayerNorm.residual_rms_forward (layernorm.py:25-27):
+      x = sum of the ranks' partials (rounded to dtype, as the all-reduced tensor is);
+      s = x + residual (a dtype add: rounded); out = s / sqrt(mean(s^2) + eps) * weight,
+    the normalisation in fp32 with one final rounding, as the reference's torch.compile'd
+    rms_forward computes it on the GPU. partials: (N, T, H); residual may be None.
+    Returns (out, s) in dtype."""
+    x = partials[0].float()
+    for i in range(1, partials.shape[0]):  # rank order, one fp32 add at a time
+        x = x + partials[i].float()
+    if partials.shape[0] > 1:
+        x = x.to(dtype).float()
+    s = x if residual is None else (x + residual.float()).to(dtype).float()
+    out = s / torch.sqrt(s.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
+    return out.to(dtype), s.to(dtype)

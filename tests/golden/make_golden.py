@@ -31,6 +31,8 @@ What runs, per fixture (all on the CPU):
   decode_int8      'int8_per_token_head' (the tile kernel, attention.py:1124-1210)
   prefill          paged_attention_prefill_triton (attention.py:852-892; kernel 704-849),
                    chunked prefill over cached prefixes with a -1 page inside one context
+  residual_rmsnorm LayerNorm.residual_rms_forward (layernorm.py:25-27) after a summed
+                   all-reduce (linear.py:222-225), run eagerly (see the function)
 """
 from __future__ import annotations
 
@@ -301,6 +303,30 @@ def make_decode_config1(decode_torch_optimized):
                 context_lens=inp["context_lens"], out=out.numpy())
 
 
+def make_residual_rmsnorm(src, rng):
+    """LayerNorm.residual_rms_forward (layernorm.py:25-27) of the reference, the op that
+    follows RowParallelLinear's all-reduce (linear.py:222-225). Its rms_forward is wrapped
+    in torch.compile, whose CPU backend needs OpenMP (absent here), so it runs eagerly
+    (dynamo disabled): s = x + residual is a bf16 add either way; the normalisation is
+    computed in bf16 steps here and in fp32 by the compiled GPU code, so `out` pins the
+    formula to bf16 accuracy. x is the bf16 rounding of the fp32 sum of four partials."""
+    import torch
+    import torch._dynamo
+    torch._dynamo.config.disable = True
+    sys.path.insert(0, src)
+    from myvllm.layers.layernorm import LayerNorm
+    T, H, N = 8, 1024, 4
+    partials = torch.from_numpy(rng.standard_normal((N, T, H)).astype(np.float32)).bfloat16()
+    residual = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32) * 2).bfloat16()
+    weight = torch.from_numpy(rng.uniform(0.5, 1.5, H).astype(np.float32)).bfloat16()
+    x = partials.float().sum(0).bfloat16()
+    ln = LayerNorm(weight, eps=1e-6)
+    with torch.no_grad():
+        out, s = ln(x, residual)
+    return dict(partials=_bf16_bits(partials), residual=_bf16_bits(residual), weight=_bf16_bits(weight),
+                eps=np.float64(1e-6), x=_bf16_bits(x), s=_bf16_bits(s), out=_bf16_bits(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", default="/root/reference/src")
@@ -318,6 +344,7 @@ def main():
         ("decode_fp8_pth", lambda: make_decode_pth(ref_attn, np.random.default_rng(707), "fp8")),
         ("decode_int8", lambda: make_decode_pth(ref_attn, np.random.default_rng(808), "int8")),
         ("prefill", lambda: make_prefill(ref_attn, np.random.default_rng(909))),
+        ("residual_rmsnorm", lambda: make_residual_rmsnorm(args.reference_src, np.random.default_rng(1010))),
     ]
     only = set(args.only.split(",")) if args.only else None
     for name, job in jobs:

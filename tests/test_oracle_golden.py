@@ -5,7 +5,8 @@ import pytest
 import torch
 
 from conftest import golden
-from oracle import (decode_torch_optimized, e4m3_encode_reference, fp8_scale_ref,
+from oracle import (
+    allreduce_residual_rmsnorm_ref,decode_torch_optimized, e4m3_encode_reference, fp8_scale_ref,
                     paged_decode_ref, paged_prefill_ref, per_token_head_scales_ref,
                     quantize_fp8_ref,
                     store_kvcache_fp8_ref, store_kvcache_quant_per_token_head_ref,
@@ -219,3 +220,17 @@ def test_prefill_oracle_matches_reference(which):
                             int(g["block_size"]))
     ref = torch.from_numpy(g["out"] if which == "triton" else g["out_torch"]).double()
     assert torch.allclose(out, ref, atol=2e-6, rtol=1e-5)
+
+
+# ------------------------------------------------- all-reduce + residual add + RMSNorm
+def test_residual_rmsnorm_oracle_matches_reference():
+    """The fused all-reduce + residual + RMSNorm oracle against the reference's
+    LayerNorm.residual_rms_forward (run eagerly, in bf16 steps): the all-reduced sum and
+    the residual output bit-exact, the normalised output to bf16 accuracy (the reference
+    computes it in fp32 on the GPU, under torch.compile)."""
+    g = golden("residual_rmsnorm")
+    b = lambda k: torch.from_numpy(g[k].astype(np.int16)).view(torch.bfloat16)
+    out, s = allreduce_residual_rmsnorm_ref(b("partials"), b("residual"), b("weight"), float(g["eps"]))
+    assert torch.equal(b("partials").float().sum(0).bfloat16(), b("x"))
+    assert torch.equal(s, b("s"))
+    assert torch.allclose(out.float(), b("out").float(), atol=2e-2, rtol=1e-2)
