@@ -370,6 +370,19 @@ MKV_API int mkv_ipc_free(void* ptr);
 MKV_API int mkv_ipc_open(const void* handle, void** ptr);
 MKV_API int mkv_ipc_close(void* ptr);
 
+/* ------------------------------------------------------------------------------------
+ * Decode-step metadata on the device (replaces the per-step Python loops and three host
+ * tensors of ModelRunner.prepare_decode, model_runner.py:631-671). packed (device, int32):
+ * [seq_lens (num_seqs)] [block tables (num_seqs x max_blocks), -1 padded], the lengths
+ * including the token being decoded. Writes context_lens[b] = seq_lens[b] and
+ * slot_mapping[b] = page * block_size + (seq_lens[b] - 1) % block_size for the page
+ * holding position seq_lens[b] - 1 (-1 when that page is missing), both int64. The block
+ * tables are used in place as the decode's (num_seqs, max_blocks) int32 table.
+ * ---------------------------------------------------------------------------------- */
+MKV_API int mkv_decode_metadata(const int32_t* packed, int32_t num_seqs, int32_t max_blocks,
+                                int32_t block_size, int64_t* slot_mapping, int64_t* context_lens,
+                                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

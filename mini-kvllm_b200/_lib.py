@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple] = {
     "mkv_paged_prefill_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "mkv_allreduce_residual_rmsnorm": (ctypes.c_int, [
         _p, _p, _i64, _p, _i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _i64, _p]),
+    "mkv_decode_metadata": (ctypes.c_int, [_p, _i32, _i32, _i32, _p, _p, _p]),
     "mkv_ipc_alloc": (ctypes.c_int, [_sz, ctypes.POINTER(_p), _p]),
     "mkv_ipc_free": (ctypes.c_int, [_p]),
     "mkv_ipc_open": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),

@@ -650,3 +650,43 @@ extern "C" int mkv_store_kvcache_quant_per_token_head(
   }
 #undef MKV_PTH
 }
+
+// ============================================================ decode-step metadata
+// Per-step decode metadata of ModelRunner.prepare_decode (model_runner.py:631-671) from a
+// packed table kept on the device: packed = [seq_lens (B)] [block tables (B x W), -1
+// padded], int32. Sequence b decodes its token at position seq_lens[b] - 1:
+//   context_lens[b] = seq_lens[b]; slot_mapping[b] = page * block_size + offset of that
+//   position (the reference's block_table[-1] * block_size + last_block_num_tokens - 1),
+//   -1 when the page is missing (the append then skips the token).
+namespace mkv {
+namespace {
+__global__ void decode_metadata_kernel(const int32_t* packed, int B, int W, int block_size,
+                                       int64_t* slot_mapping, int64_t* context_lens) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int n = packed[b];
+  context_lens[b] = n;
+  int64_t slot = -1;
+  if (n > 0) {
+    const int blk = (n - 1) / block_size;
+    const int page = blk < W ? packed[B + (int64_t)b * W + blk] : -1;
+    if (page >= 0) slot = (int64_t)page * block_size + (n - 1) % block_size;
+  }
+  slot_mapping[b] = slot;
+}
+}  // namespace
+}  // namespace mkv
+
+extern "C" int mkv_decode_metadata(const int32_t* packed, int32_t num_seqs, int32_t max_blocks,
+                                   int32_t block_size, int64_t* slot_mapping, int64_t* context_lens,
+                                   void* stream) {
+  clear_error();
+  if (num_seqs < 0 || max_blocks < 0 || block_size <= 0)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "mkv_decode_metadata: bad sizes");
+  if (num_seqs == 0) return MKV_OK;
+  if (!packed || !slot_mapping || !context_lens)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "mkv_decode_metadata: null pointer argument");
+  mkv::decode_metadata_kernel<<<(num_seqs + 127) / 128, 128, 0, (cudaStream_t)stream>>>(
+      packed, num_seqs, max_blocks, block_size, slot_mapping, context_lens);
+  return cuda_status(cudaGetLastError(), "decode_metadata launch");
+}

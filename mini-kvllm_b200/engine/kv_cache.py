@@ -7,6 +7,8 @@ Reference (heart1128/mini-kvllm, src/myvllm/engine/model_runner.py):
                                float8_e4m3fn (247); per-tensor scales ones(2, L, 1) fp32
                                (324-329); layer l gets views [0, l] / [1, l] (376-395)
   prepare_decode      631-671  context_lens = len(seq) (includes the new token),
+                               (decode_metadata restates it; DecodeMetadataBuilder
+                               computes it with one copy and one kernel per step)
                                slot = block_table[-1] * BS + last_block_num_tokens - 1,
                                block_tables padded with -1 to the longest table; int64
                                slots and lengths, int32 tables
@@ -104,6 +106,82 @@ def decode_metadata(block_tables: Sequence[Sequence[int]], seq_lens: Sequence[in
         slot_mapping=to(torch.tensor(slots, dtype=torch.int64)),
         context_lens=to(torch.tensor(lens, dtype=torch.int64)),
         block_tables=to(torch.tensor(padded, dtype=torch.int32).reshape(len(padded), width)))
+
+
+class DecodeMetadataBuilder:
+    """Decode metadata with one host-to-device copy and one kernel per step, instead of
+    prepare_decode's per-sequence Python loops and three host tensors
+    (model_runner.py:631-671).
+
+    Block tables live in a host mirror indexed by a persistent sequence slot. The block
+    manager reports only their changes: `set_table` when a sequence takes a slot,
+    `append` when it takes a block. Each step then packs [lengths | tables] into a pinned
+    buffer, copies it once, and `mkv_decode_metadata` derives the int64 slot mapping and
+    context lengths on the device. The table width is max_blocks, fixed, so every step
+    has the same shapes (capturable decode graphs). Two pinned buffers alternate, each
+    reused only after its previous copy has completed. The returned tensors are
+    overwritten by the next step."""
+
+    def __init__(self, max_seqs: int, max_blocks: int, block_size: int,
+                 device: torch.device | str = "cuda"):
+        import numpy as np
+        from .. import _lib
+        self._np, self._lib_mod = np, _lib
+        self._lib = _lib.load()
+        self.max_seqs, self.max_blocks, self.block_size = max_seqs, max_blocks, block_size
+        self.device = torch.device(device)
+        n = max_seqs * (1 + max_blocks)
+        self._host = [torch.empty(n, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._host_np = [h.numpy() for h in self._host]
+        self._copied = [None, None]
+        self._k = 0
+        self._tables = np.full((max_seqs, max_blocks), -1, dtype=np.int32)
+        self._nblocks = np.zeros(max_seqs, dtype=np.int64)
+        self._packed = torch.empty(n, dtype=torch.int32, device=self.device)
+        self._slots = torch.empty(max_seqs, dtype=torch.int64, device=self.device)
+        self._lens = torch.empty(max_seqs, dtype=torch.int64, device=self.device)
+
+    def set_table(self, seq: int, table: Sequence[int]) -> None:
+        if len(table) > self.max_blocks:
+            raise ValueError(f"a table of {len(table)} blocks exceeds max_blocks {self.max_blocks}")
+        row = self._tables[seq]
+        row[:] = -1
+        row[:len(table)] = table
+        self._nblocks[seq] = len(table)
+
+    def append(self, seq: int, block: int) -> None:
+        n = int(self._nblocks[seq])
+        if n >= self.max_blocks:
+            raise ValueError(f"sequence slot {seq} already holds max_blocks {self.max_blocks}")
+        self._tables[seq, n] = block
+        self._nblocks[seq] = n + 1
+
+    def step(self, seqs: Sequence[int], seq_lens: Sequence[int]) -> DecodeMetadata:
+        """Metadata of one decode step over sequence slots `seqs` (batch order), with
+        lengths including the token being decoded."""
+        np = self._np
+        B, W = len(seqs), self.max_blocks
+        if B > self.max_seqs or len(seq_lens) != B:
+            raise ValueError("one length per sequence, at most max_seqs sequences")
+        k = self._k
+        if self._copied[k] is not None:
+            self._copied[k].synchronize()  # the copy that last read this buffer is done
+        hv = self._host_np[k]
+        idx = np.asarray(seqs, dtype=np.int64)
+        hv[:B] = seq_lens
+        hv[B:B + B * W].reshape(B, W)[:] = self._tables[idx]
+        stream = torch.cuda.current_stream(self.device)
+        self._packed[:B * (1 + W)].copy_(self._host[k][:B * (1 + W)], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._copied[k] = ev
+        self._k ^= 1
+        st = self._lib.mkv_decode_metadata(self._packed.data_ptr(), B, W, self.block_size,
+                                           self._slots.data_ptr(), self._lens.data_ptr(),
+                                           stream.cuda_stream)
+        self._lib_mod.check("mkv_decode_metadata", st)
+        return DecodeMetadata(slot_mapping=self._slots[:B], context_lens=self._lens[:B],
+                              block_tables=self._packed[B:B + B * W].view(B, W))
 
 
 def kv_head_shard(num_heads: int, num_kv_heads: int, rank: int, world_size: int):
