@@ -560,20 +560,32 @@ __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
   // (r & 7) is the same for all of this thread's rows r = ld_r0 + i * RPP
   const uint32_t soff0 = ld_r0 * ROWB + ((ld_c ^ (ld_r0 & 7)) << 4);
   const uint32_t kd0 = smem_u32(kd) + soff0, vd0 = smem_u32(vd) + soff0;
-  // per-token scales of 8-bit pages: thread r < TILE copies row r's K scale, thread
-  // TILE + r its V scale (zero for rows that are not loaded)
-  if (rs != nullptr && tid < 2 * TILE) {
-    const int r = tid < TILE ? tid : tid - TILE;
-    const float* src = tid < TILE ? p.k_scales : p.v_scales;
-    const int t = t0 + r;
-    int page = -1, boff = 0;
-    if (t < rng.end) {
-      int blk;
-      split_token(p, t, blk, boff);
-      page = slice_page(p, seq, slice, bt_s, blk);
+  // per-token scales of 8-bit pages: entry r < TILE is row r's K scale, TILE + r its V
+  // scale (zero for rows that are not loaded)
+  if (rs != nullptr && one_page_per_tile) {  // one page: row r's scales are r * KVH apart
+    const int page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
+    const int nrows = page >= 0 ? min(TILE, rng.end - t0) : 0;
+    const int64_t base =
+        ((int64_t)(page >= 0 ? page : 0) * p.block_size + (t0 & ((1 << p.bs_shift) - 1))) * p.num_kv_heads + kvh;
+    for (int i = tid; i < 2 * TILE; i += kThreads) {
+      const int r = i < TILE ? i : i - TILE;
+      const float* src = (i < TILE ? p.k_scales : p.v_scales) + base + (int64_t)r * p.num_kv_heads;
+      cp_async_4(smem_u32(rs + i), r < nrows ? src : p.k_scales, r < nrows ? 4 : 0);
     }
-    const int64_t idx = page >= 0 ? ((int64_t)page * p.block_size + boff) * p.num_kv_heads + kvh : 0;
-    cp_async_4(smem_u32(rs + tid), src + idx, page >= 0 ? 4 : 0);
+  } else if (rs != nullptr) {
+    for (int i = tid; i < 2 * TILE; i += kThreads) {
+      const int r = i < TILE ? i : i - TILE;
+      const float* src = i < TILE ? p.k_scales : p.v_scales;
+      const int t = t0 + r;
+      int page = -1, boff = 0;
+      if (t < rng.end) {
+        int blk;
+        split_token(p, t, blk, boff);
+        page = slice_page(p, seq, slice, bt_s, blk);
+      }
+      const int64_t idx = page >= 0 ? ((int64_t)page * p.block_size + boff) * p.num_kv_heads + kvh : 0;
+      cp_async_4(smem_u32(rs + i), src + idx, page >= 0 ? 4 : 0);
+    }
   }
   if (one_page_per_tile) {
     const int page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
@@ -1339,13 +1351,18 @@ constexpr size_t f8_front_bytes() {
   constexpr size_t ring = (size_t)STAGES * 2 * kF8Tile * kTcD;
   return ring > f8_epilogue_bytes<NT>() ? ring : f8_epilogue_bytes<NT>();
 }
-template <int NT, int STAGES>
-constexpr size_t f8_smem_bytes() {  // + valid flags + staged block table + query rows
+template <int NT, int STAGES, bool kPT = false>
+constexpr size_t f8_smem_bytes() {  // + valid flags + staged block table + query rows (+ row scales)
   return f8_front_bytes<NT, STAGES>() + (size_t)STAGES * kF8Tile + kMaxBtSmem * 4 +
-         (size_t)8 * NT * kTcD * 2;
+         (size_t)8 * NT * kTcD * 2 + (kPT ? (size_t)STAGES * 2 * kF8Tile * 4 : 0);
 }
 
-template <typename QT, int NT, int STAGES, int MINB>
+// kPT: e4m3 pages with a scale per (page, row, kv head). S^T rows are multiplied by
+// their token's K scale. P is multiplied by its token's V scale divided by 2^e, where
+// 2^e bounds the tile's largest V scale, so that P stays in e4m3's range. O is kept in
+// units of 2^e (rescaled by a power of two when a tile's e differs from the last one)
+// and multiplied by 2^e in the merge. The softmax denominator uses the unscaled P.
+template <typename QT, int NT, int STAGES, int MINB, bool kPT = false>
 __global__ void __launch_bounds__(kThreads, MINB)
 paged_decode_fp8mma_kernel(const DecodeParams p) {
   constexpr int D = kTcD;
@@ -1358,6 +1375,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
   uint8_t* valid = smem + FRONT;                                  // [STAGES][kF8Tile]
   int* bt_s = reinterpret_cast<int*>(valid + STAGES * kF8Tile);   // [kMaxBtSmem]
   QT* q_s = reinterpret_cast<QT*>(bt_s + kMaxBtSmem);              // [8 * NT][D]
+  float* rs_s = reinterpret_cast<float*>(q_s + 8 * NT * D);        // kPT: [STAGES][2][kF8Tile]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, tig = lane & 3;
@@ -1393,7 +1411,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
     uint8_t* kd = smem + stage * STAGE_BYTES;
     load_kv_tile<kF8Tile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kF8Tile, kd,
                                 kd + TILE_BYTES, valid + stage * kF8Tile, row_stride, head_off,
-                                one_page_per_tile);
+                                one_page_per_tile, kPT ? rs_s + stage * 2 * kF8Tile : nullptr, kvh);
   };
 
   if (!prefetched) {
@@ -1439,7 +1457,8 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
         for (int i = 0; i < 4; ++i) x[i] = qval(nt * 8 + g, 32 * kq + 16 * half + 4 * tig + i) * qs;
         split_e4m3x4(x, qh[nt][kq][half], ql[nt][kq][half]);
       }
-  const float sc = p.qk_scale_log2 * __ldg(p.k_scale) / qs;
+  const float sc = p.qk_scale_log2 * (kPT ? 1.0f : __ldg(p.k_scale)) / qs;
+  int v_exp = 0;  // kPT: O is held in units of 2^v_exp
 
   // per-warp state for heads nt*8 + 2tig + e: running max, accumulator reference, l
   float m_run[NT][2], q_ref[NT][2], l_run[NT][2];
@@ -1499,6 +1518,29 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       vt[mt][0] = vld[warp * 32 + mt * 16 + g] != 0;
       vt[mt][1] = vld[warp * 32 + mt * 16 + g + 8] != 0;
     }
+    // kPT: this thread's tokens' K scales and V scales / 2^e (e from the tile's largest)
+    float ksv[2][2], vsv[2][2];
+    float o_rescale = 1.0f;
+    if constexpr (kPT) {
+      const float* rs = rs_s + stage * 2 * kF8Tile;
+      float vm = fmaxf(fmaxf(rs[kF8Tile + lane], rs[kF8Tile + 32 + lane]),
+                       fmaxf(rs[kF8Tile + 64 + lane], rs[kF8Tile + 96 + lane]));
+      vm = warp_max(vm);  // every warp finds the same tile maximum
+      int e = v_exp;
+      if (vm > 0.0f && isfinite(vm)) frexpf(vm, &e);  // vm < 2^e
+      if (it == 0) v_exp = e;  // O is still zero
+      o_rescale = ldexpf(1.0f, v_exp - e);
+      v_exp = e;
+      const float inv = ldexpf(1.0f, -e);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int tok = warp * 32 + mt * 16 + g + 8 * rr;
+          ksv[mt][rr] = rs[tok];
+          vsv[mt][rr] = rs[kF8Tile + tok] * inv;
+        }
+    }
     uint32_t ph[NT][2], pl[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -1512,7 +1554,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
             const int i = e + 2 * rr;
-            const float v = vt[mt][rr] ? s[nt][mt][i] * sc : -INFINITY;
+            const float v = vt[mt][rr] ? s[nt][mt][i] * (kPT ? sc * ksv[mt][rr] : sc) : -INFINITY;
             x[mt][i] = v;
             mx = fmaxf(mx, v);
           }
@@ -1531,10 +1573,11 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
           for (int rr = 0; rr < 2; ++rr) {
             const int i = e + 2 * rr;
             const float pv = x[mt][i] == -INFINITY ? 0.0f : exp2f(x[mt][i] - q_new + 8.0f);
-            x[mt][i] = pv;
+            x[mt][i] = kPT ? pv * vsv[mt][rr] : pv;
             lsum += pv;
           }
         l_run[nt][e] = fmaf(l_run[nt][e], f[e], lsum);
+        if (kPT) f[e] *= o_rescale;  // O into the units of this tile's V scales
       }
       if (f[0] != 1.0f || f[1] != 1.0f) {
 #pragma unroll
@@ -1604,7 +1647,8 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
           uint8_t* kd = smem + ((gt + s) % STAGES) * STAGE_BYTES;
           load_kv_tile<kF8Tile, ROWB>(p, sched.cur.seq, slice, bt_s, nr, nr.begin + s * kF8Tile,
                                       kd, kd + TILE_BYTES, valid + ((gt + s) % STAGES) * kF8Tile,
-                                      row_stride, (int64_t)nkvh * ROWB, one_page_per_tile);
+                                      row_stride, (int64_t)nkvh * ROWB, one_page_per_tile,
+                                      kPT ? rs_s + ((gt + s) % STAGES) * 2 * kF8Tile : nullptr, nkvh);
         }
         cp_async_commit();
       }
@@ -1664,7 +1708,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
 #pragma unroll
     for (int w = 0; w < 4; ++w)
       O = fmaf(exp2f(red_m[w * HC + h] - base), red_acc[(w * HC + h) * RP + d], O);
-    red_acc[h * RP + d] = O;
+    red_acc[h * RP + d] = kPT ? ldexpf(O, v_exp) : O;
   }
   __syncthreads();
   finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s);
@@ -1868,19 +1912,19 @@ int launch_tc_nt(const DecodeParams& p, cudaStream_t stream, int device) {
 #define MKV_F8_STAGES 2
 #define MKV_F8_MINB 3
 #endif
-template <typename QT, int NT>
+template <typename QT, int NT, bool kPT>
 int launch_fp8mma_nt(const DecodeParams& p, cudaStream_t stream, int device) {
   constexpr int S = MKV_F8_STAGES, MB = MKV_F8_MINB;
-  constexpr size_t smem = f8_smem_bytes<NT, S>();
-  int st = ensure_smem<paged_decode_fp8mma_kernel<QT, NT, S, MB>>(smem, device);
+  constexpr size_t smem = f8_smem_bytes<NT, S, kPT>();
+  int st = ensure_smem<paged_decode_fp8mma_kernel<QT, NT, S, MB, kPT>>(smem, device);
   if (st != MKV_OK) return st;
-  return launch_decode<paged_decode_fp8mma_kernel<QT, NT, S, MB>>(
+  return launch_decode<paged_decode_fp8mma_kernel<QT, NT, S, MB, kPT>>(
       p, kF8Tile, smem, stream, device, "paged_decode_fp8mma launch");
 }
-template <typename QT>
+template <typename QT, bool kPT = false>
 int launch_fp8mma(const DecodeParams& p, cudaStream_t stream, int device) {
-  return p.heads_per_cta > 8 ? launch_fp8mma_nt<QT, 2>(p, stream, device)
-                             : launch_fp8mma_nt<QT, 1>(p, stream, device);
+  return p.heads_per_cta > 8 ? launch_fp8mma_nt<QT, 2, kPT>(p, stream, device)
+                             : launch_fp8mma_nt<QT, 1, kPT>(p, stream, device);
 }
 
 template <typename QT, typename CT, bool kPT = false>
@@ -2039,10 +2083,11 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   const bool tc_ok = head_dim == kTcD && q_dtype != MKV_DTYPE_F32;
   if (per_token) {  // 8-bit pages with per-(page, row, kv head) scales
     const bool i8 = cache_dtype == MKV_DTYPE_INT8;
+    // e4m3: FP8 MMAs with the scales applied to S and P; int8: pages converted to f16
     if (tc_ok && q_dtype == MKV_DTYPE_BF16)
-      return i8 ? launch_tc<bf16, int8_t, true>(p, s, device) : launch_tc<bf16, fp8, true>(p, s, device);
+      return i8 ? launch_tc<bf16, int8_t, true>(p, s, device) : launch_fp8mma<bf16, true>(p, s, device);
     if (tc_ok && q_dtype == MKV_DTYPE_F16)
-      return i8 ? launch_tc<f16, int8_t, true>(p, s, device) : launch_tc<f16, fp8, true>(p, s, device);
+      return i8 ? launch_tc<f16, int8_t, true>(p, s, device) : launch_fp8mma<f16, true>(p, s, device);
     switch (q_dtype) {
       case MKV_DTYPE_F32:
         return i8 ? launch_generic<float, int8_t>(p, s, device) : launch_generic<float, fp8>(p, s, device);
