@@ -507,36 +507,40 @@ constexpr int kD = 128;
 constexpr uint32_t kTmemCols = 512;  // S buffers (P over their first 64 columns) at 0 / 128, O at 256 (+128)
 constexpr int BLK = 128 * 128;       // 128 rows x 128 bytes: one 64-column half
 constexpr int TILE = 2 * BLK;        // 128 rows x 256 bytes
-template <int NQ, bool kByte = false>
+template <int NQ, bool kByte = false, bool kSplit = false>
 struct Layout {
+  // kSplit: one query tile, two softmax warpgroups, each taking half of S's columns
+  static constexpr int kSoftmaxWarps = 4 * NQ * (kSplit ? 2 : 1);
   static constexpr int kConvWarps = kByte ? 4 : 0;  // 8-bit pages: converter warpgroup
-  static constexpr int kThreads = 64 + 128 * NQ + 32 * kConvWarps;
+  static constexpr int kThreads = 64 + 32 * kSoftmaxWarps + 32 * kConvWarps;
   static constexpr int kKStages = kByte ? 2 : 3;
-  static constexpr int kVStages = kByte ? 2 : (NQ == 1 ? 3 : 2);
+  static constexpr int kVStages = kByte ? 2 : (NQ == 1 && !kSplit ? 3 : 2);
   static constexpr int kRStages = kByte ? 2 : 0;
   static constexpr int Q0 = 0;                           // [NQ] query tiles
   static constexpr int K0 = Q0 + NQ * TILE;              // [stage] K tile (16-bit)
   static constexpr int V0 = K0 + kKStages * TILE;        // [stage] V tile (16-bit)
   static constexpr int R0 = V0 + kVStages * TILE;        // [stage][K, V] 8-bit tiles, 128 x 128 B
-  static constexpr int BAR0 = R0 + kRStages * 2 * BLK;
-  // K full/empty, V full/empty, raw full/empty, q, s[2], p[2], o[NQ], drain
-  static constexpr int NBAR = 2 * kKStages + 2 * kVStages + 2 * kRStages + 1 + 2 + 2 + NQ + 1;
+  static constexpr int X0 = R0 + kRStages * 2 * BLK;     // kSplit: row maxima [2][2][128], sums [2][128]
+  static constexpr int BAR0 = X0 + (kSplit ? 6 * kRows * 4 : 0);
+  // K full/empty, V full/empty, raw full/empty, q, s[2], p[2], o[NQ], drain (+ x[2], l)
+  static constexpr int NBAR = 2 * kKStages + 2 * kVStages + 2 * kRStages + 1 + 2 + 2 + NQ + 1 + (kSplit ? 3 : 0);
   static constexpr int MISC0 = BAR0 + NBAR * 8;          // tmem base, abort flag, nkv
   static constexpr int BYTES = MISC0 + 16 + 1024;        // + alignment slack
   static_assert(BYTES <= 232448, "shared memory per CTA");
   static_assert(!kByte || NQ == 1, "8-bit pages: one query tile (the converters take the other's warps)");
+  static_assert(!kSplit || (NQ == 1 && !kByte), "split softmax: one query tile, 16-bit tiles");
 };
 }  // namespace pf05
 
-template <typename QT, int NQ, typename CT, bool kTok>
-__global__ void __launch_bounds__(pf05::Layout<NQ, sizeof(CT) == 1>::kThreads, 1)
+template <typename QT, int NQ, typename CT, bool kTok, bool kSplit = false>
+__global__ void __launch_bounds__(pf05::Layout<NQ, sizeof(CT) == 1, kSplit>::kThreads, 1)
 paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap vmap, int units) {
   using namespace pf05;
   constexpr bool kByte = sizeof(CT) == 1;  // e4m3 or int8 pages, converted by warps 6-9
-  using L = Layout<NQ, kByte>;
+  using L = Layout<NQ, kByte, kSplit>;
   constexpr int kKS = L::kKStages, kVS = L::kVStages, kRS = L::kRStages;
-  constexpr int kSoftmaxEnd = 2 + 4 * NQ;  // softmax warps 2 .. kSoftmaxEnd - 1
+  constexpr int kSoftmaxEnd = 2 + L::kSoftmaxWarps;  // softmax warps 2 .. kSoftmaxEnd - 1
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR0);
@@ -551,6 +555,8 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
   uint64_t* pfull = sfull + 2;
   uint64_t* ofull = pfull + 2;
   uint64_t* drain = ofull + NQ;
+  uint64_t* xbar = drain + 1;  // kSplit: row-maximum exchange [2], row-sum exchange
+  float* xch = reinterpret_cast<float*>(smem + L::X0);
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + L::MISC0);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC0 + 4);
   int* nkv_s = reinterpret_cast<int*>(smem + L::MISC0 + 8);
@@ -578,11 +584,13 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       mbar_init(&rfull[s], 1);
       mbar_init(&rempty[s], 4);
     }
-    mbar_init(qfull, 4 * NQ);
+    mbar_init(qfull, L::kSoftmaxWarps);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sfull[b], 1);
-      mbar_init(&pfull[b], 4);
+      mbar_init(&pfull[b], kSplit ? 8 : 4);
     }
+    if (kSplit)
+      for (int b = 0; b < 3; ++b) mbar_init(&xbar[b], 8);
     for (int q = 0; q < NQ; ++q) mbar_init(&ofull[q], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -599,7 +607,9 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
   // the tile's row rt = 32 * (w % 4) + lane, which is also its TMEM lane (warp w reaches
   // lanes 32 (w % 4) ..)
   const bool softmax_warp = warp >= 2 && warp < kSoftmaxEnd;
-  const int qt = softmax_warp ? (warp - 2) >> 2 : 0;
+  // kSplit: warpgroup hh takes S columns 64 hh .. 64 hh + 63 of the one query tile
+  const int hh = (kSplit && softmax_warp) ? (warp - 2) >> 2 : 0;
+  const int qt = (softmax_warp && !kSplit) ? (warp - 2) >> 2 : 0;
   const int rt = 32 * (warp & 3) + lane;
   int vis = 0, qrow = -1, hrow = 0;
   if (softmax_warp) {
@@ -775,7 +785,10 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k) {  // 16 kv tokens per MMA = 8 TMEM columns of P
           const uint64_t b = smem_desc(vaddr + k * 2048, BLK, 1024, kLayoutSw128);
-          mma_f16_ts(tmem + 256 + q * kD, tmem + sb * kTile + 8 * k, b, kIdPV, (j > 0 || k > 0) ? 1u : 0u);
+          // P of tokens 16k..: columns 8k (kSplit: the second half's P sits over its own S
+          // at column 64 + 8(k - 4))
+          const uint32_t pcol = sb * kTile + (kSplit && k >= 4 ? 32 + 8 * k : 8 * k);
+          mma_f16_ts(tmem + 256 + q * kD, tmem + pcol, b, kIdPV, (j > 0 || k > 0) ? 1u : 0u);
         }
         if (q == 0) PF_TRACE(13, j);
         mma_commit(&ofull[q]);
@@ -823,6 +836,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       uint8_t* qdst = smem + L::Q0 + qt * TILE + rt * 128;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
+        if (kSplit && (c >> 3) != hh) continue;  // each warpgroup stages its half of the row
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (qrow >= 0) v = *reinterpret_cast<const uint4*>(src + c * 8);
         const int b = c >> 3, cc = c & 7;
@@ -921,9 +935,13 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         for (int k = 0; k < 4; ++k) acc[k] = f2_pack(0.0f, 0.0f);
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
-        p_half(0, ref, w0, acc, mx8);
-        reg_fence32(w0);
-        p_half(1, ref, w1, acc, mx8);
+        if constexpr (kSplit) {
+          p_half(hh, ref, w0, acc, mx8);  // this warpgroup's half only
+        } else {
+          p_half(0, ref, w0, acc, mx8);
+          reg_fence32(w0);
+          p_half(1, ref, w1, acc, mx8);
+        }
         mxr = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
         float sum = 0.0f;
 #pragma unroll
@@ -942,6 +960,19 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       float lsum, mxr;
       bool need;
       float m_new, alpha;
+      // kSplit: the row maximum of the two halves, exchanged through shared memory
+      // (buffer and barrier alternate by tile; bounded wait)
+      auto combine_max = [&]() -> bool {
+        if constexpr (kSplit) {
+          float* x = xch + (i & 1) * 2 * kRows;
+          x[hh * kRows + rt] = mxr;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&xbar[i & 1]);
+          if (!__all_sync(0xffffffffu, mbar_wait(&xbar[i & 1], (i >> 1) & 1, abort_flag))) return false;
+          mxr = fmaxf(x[rt], x[kRows + rt]);
+        }
+        return true;
+      };
       // lazy reference: move it (and rescale O) only when the maximum grows by > 2^8
       auto new_ref = [&]() {
         const float mx = mxr * sc;  // the scale is > 0
@@ -956,6 +987,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll 1
         for (int h = 0; h < 2; ++h) {
+          if (kSplit && h != hh) continue;
           float v[64];
           tmem_ld64(sa + 64 * h, v);
           apply_mask(v, 64 * h, 64);
@@ -965,11 +997,19 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
             for (int k = 0; k < 8; ++k) mx8[k] = fmax3(mx8[k], v[e + k], v[e + 8 + k]);
         }
         mxr = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        if (!combine_max()) {
+          ok = false;
+          break;
+        }
         new_ref();
         float unused;
         lsum = p_tile(m_new == -INFINITY ? 0.0f : m_new, w0, w1, unused);
       } else {
         lsum = p_tile(m, w0, w1, mxr);
+        if (!combine_max()) {
+          ok = false;
+          break;
+        }
         new_ref();
         if (__any_sync(0xffffffffu, need)) {
           float unused;
@@ -979,9 +1019,14 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       if (warp == 2 && lane == 0) PF_TRACE(5, i);
       m = m_new;
       l = l * alpha + lsum;
-      // P over the first 64 columns of this S buffer
-      tmem_st32(sa, w0);
-      tmem_st32(sa + 32, w1);
+      // P over the first 64 columns of this S buffer (kSplit: each half's P over the first
+      // 32 columns of its own S half)
+      if constexpr (kSplit) {
+        tmem_st32(sa + 64 * hh, w0);
+      } else {
+        tmem_st32(sa, w0);
+        tmem_st32(sa + 32, w1);
+      }
       if (warp == 2 && lane == 0) PF_TRACE(10, i);
       // PV(i-1) done: O may be rescaled, and the next wait on this O barrier is for PV(i)
       if (i > 0) {
@@ -991,7 +1036,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         tc_fence_after_sync();
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-          for (int c = 0; c < kD / 16; ++c) {
+          for (int c = kSplit ? 4 * hh : 0; c < (kSplit ? 4 * hh + 4 : kD / 16); ++c) {
             float v[16];
             tmem_ld16(tmem + lane_base + o_col + 16 * c, v);
 #pragma unroll
@@ -1005,7 +1050,7 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       // V rows past the last visible token of every row may hold anything (the page's
       // other tokens or never-written memory): zero them so that 0 * V stays 0. Query
       // tile 0 does it, before its PV product, which is issued before tile 1's.
-      if (!kByte && qt == 0 && t0 + kTile > nkv) {
+      if (!kByte && qt == 0 && hh == 0 && t0 + kTile > nkv) {
         const int st = i % kVS;
         ok = __all_sync(0xffffffffu, mbar_wait(&vfull[st], (i / kVS) & 1, abort_flag));
         if (!ok) break;
@@ -1032,10 +1077,21 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       if (!ok) *abort_flag = 1;
       tc_fence_after_sync();
     }
+    if constexpr (kSplit) {  // the row sum is split between the halves too
+      float* xl = xch + 4 * kRows;
+      xl[hh * kRows + rt] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[2]);
+      if (!__all_sync(0xffffffffu, mbar_wait(&xbar[2], 0, abort_flag))) {
+        ok = false;
+        *abort_flag = 1;
+      }
+      l = xl[rt] + xl[kRows + rt];
+    }
     const float inv = out_scale / l;
     QT* dst = reinterpret_cast<QT*>(p.out) + (int64_t)(qrow >= 0 ? qrow : 0) * p.o_st + (int64_t)hrow * p.o_sh;
 #pragma unroll 1
-    for (int c = 0; c < kD / 16; ++c) {
+    for (int c = kSplit ? 4 * hh : 0; c < (kSplit ? 4 * hh + 4 : kD / 16); ++c) {
       float v[16];
       if (ntiles > 0 && ok) {
         tmem_ld16(tmem + lane_base + o_col + 16 * c, v);
@@ -1160,10 +1216,10 @@ bool pf05_supported(const PrefillParams& p, int q_dtype, int cache_dtype) {
   return pf_encode_fn() != nullptr;
 }
 
-template <typename QT, int NQ, typename CT, bool kTok = false>
+template <typename QT, int NQ, typename CT, bool kTok = false, bool kSplit = false>
 int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t stream) {
   constexpr bool kByte = sizeof(CT) == 1;
-  using L = pf05::Layout<NQ, kByte>;
+  using L = pf05::Layout<NQ, kByte, kSplit>;
   PfEncodeTiledFn enc = pf_encode_fn();
   // rows of the cache = (page, offset) slots; a row holds KVH heads of head_dim elements.
   // 16-bit tiles are loaded as two 64-column halves, 8-bit tiles as one 128-byte box.
@@ -1192,7 +1248,7 @@ int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t st
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc05_kernel<QT, NQ, CT, kTok>,
+    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc05_kernel<QT, NQ, CT, kTok, kSplit>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill tc05 smem)");
     configured[dev] = true;
@@ -1201,7 +1257,7 @@ int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t st
   q.qb = NQ * pf05::kRows / p.group;  // query tokens per CTA: 128 NQ rows
   const int64_t units = (int64_t)q.total_q / q.qb + q.num_seqs;
   dim3 grid((unsigned)units, q.num_kv_heads, 1);
-  paged_prefill_tc05_kernel<QT, NQ, CT, kTok><<<grid, L::kThreads, L::BYTES, stream>>>(q, km, vm, (int)units);
+  paged_prefill_tc05_kernel<QT, NQ, CT, kTok, kSplit><<<grid, L::kThreads, L::BYTES, stream>>>(q, km, vm, (int)units);
   return cuda_status(cudaGetLastError(), "paged_prefill_tc05 launch");
 }
 
@@ -1219,13 +1275,13 @@ int launch_prefill_tc05_auto(const PrefillParams& p, int cache_dtype, cudaStream
                                  : launch_prefill_tc05<QT, 1, fp8, false>(p, cache_dtype, stream);
   if (cache_dtype == MKV_DTYPE_INT8) return launch_prefill_tc05<QT, 1, int8_t, true>(p, cache_dtype, stream);
   const char* force = getenv("MKV_PREFILL_QTILES");
-  if (force != nullptr && force[0] == '1') return launch_prefill_tc05<QT, 1, QT>(p, cache_dtype, stream);
+  if (force != nullptr && force[0] == '1') return launch_prefill_tc05<QT, 1, QT, false, true>(p, cache_dtype, stream);
   if (force != nullptr && force[0] == '2') return launch_prefill_tc05<QT, 2, QT>(p, cache_dtype, stream);
   const int64_t rows = (int64_t)p.total_q * p.group;
   const int64_t ctas2 = (rows + 2 * pf05::kRows - 1) / (2 * pf05::kRows) * p.num_kv_heads;
   if (rows >= (int64_t)p.num_seqs * 4 * pf05::kRows && ctas2 >= 2 * kNumSMs)
     return launch_prefill_tc05<QT, 2, QT>(p, cache_dtype, stream);
-  return launch_prefill_tc05<QT, 1, QT>(p, cache_dtype, stream);
+  return launch_prefill_tc05<QT, 1, QT, false, true>(p, cache_dtype, stream);
 }
 
 // ============================================================ 8-bit pages -> 16-bit scratch
