@@ -500,38 +500,48 @@ __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
   if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(ctr, 1u) == (unsigned)(active - 1);
   __syncthreads();
   if (!last) return;
-  // OUT outputs per thread at a time, so that their partial loads are in flight together
+  // OUT outputs per thread at a time. Two passes over the partials: their maximum, then
+  // the weighted sums; the loads of up to 8 partials are independent of each other, so
+  // they are in flight together instead of one online step after another.
   constexpr int OUT = 4;
   for (int base = threadIdx.x; base < nh * D; base += OUT * blockDim.x) {
     float M[OUT], L[OUT], O[OUT];
+    int64_t row[OUT];
+    bool live[OUT];
 #pragma unroll
-    for (int i = 0; i < OUT; ++i) M[i] = -INFINITY, L[i] = 0.0f, O[i] = 0.0f;
-#pragma unroll 2
+    for (int i = 0; i < OUT; ++i) {
+      const int idx = base + i * blockDim.x;
+      live[i] = idx < nh * D;
+      const int h = live[i] ? idx / D : 0;
+      row[i] = (int64_t)h;  // head, turned into the partial row below
+      M[i] = -INFINITY, L[i] = 0.0f, O[i] = 0.0f;
+    }
+#pragma unroll 8
+    for (int s = 0; s < active; ++s)
+#pragma unroll
+      for (int i = 0; i < OUT; ++i)
+        if (live[i]) M[i] = fmaxf(M[i], __ldcg(p.part_ml + part_row(p, sg, h0, s, (int)row[i]) * 2));
+#pragma unroll 8
     for (int s = 0; s < active; ++s) {
 #pragma unroll
       for (int i = 0; i < OUT; ++i) {
+        if (!live[i]) continue;
         const int idx = base + i * blockDim.x;
-        if (idx < nh * D) {
-          const int h = idx / D, d = idx - h * D;
-          const int64_t b = part_row(p, sg, h0, s, h);
-          const float m = __ldcg(p.part_ml + b * 2), l = __ldcg(p.part_ml + b * 2 + 1);
-          const float a = __ldcg(p.part_acc + b * D + d);
-          const float mn = fmaxf(M[i], m);
-          const float ref = mn == -INFINITY ? 0.0f : mn;
-          const float c_old = exp2f(M[i] - ref), c_new = exp2f(m - ref);
-          O[i] = fmaf(O[i], c_old, a * c_new);
-          L[i] = fmaf(L[i], c_old, l * c_new);
-          M[i] = mn;
-        }
+        const int h = (int)row[i], d = idx - h * D;
+        const int64_t b = part_row(p, sg, h0, s, h);
+        const float m = __ldcg(p.part_ml + b * 2), l = __ldcg(p.part_ml + b * 2 + 1);
+        const float a = __ldcg(p.part_acc + b * D + d);
+        const float c = m == -INFINITY ? 0.0f : exp2f(m - M[i]);
+        O[i] = fmaf(a, c, O[i]);
+        L[i] = fmaf(l, c, L[i]);
       }
     }
 #pragma unroll
     for (int i = 0; i < OUT; ++i) {
+      if (!live[i]) continue;
       const int idx = base + i * blockDim.x;
-      if (idx < nh * D) {
-        const int h = idx / D, d = idx - h * D;
-        op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O[i] * vs / L[i]);
-      }
+      const int h = idx / D, d = idx - h * D;
+      op[(int64_t)seq * p.o_sb + (int64_t)(h0 + h) * p.o_sh + d] = from_f32<QT>(O[i] * vs / L[i]);
     }
   }
   if (threadIdx.x == 0) *ctr = 0u;
