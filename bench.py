@@ -14,7 +14,9 @@ collective.
 
 One step = what an attention layer does per decode step: append each sequence's new
 K/V token into its page (store_kvcache / store_kvcache_fp8), then decode every
-sequence over its whole context (paged_attention_decode[_quantized]).
+sequence over its whole context (paged_attention_decode[_quantized]). The step is
+captured once in a CUDA graph and replayed, as the reference's model runner replays its
+decode step; `--eager` times the Python calls instead.
 
 Output: one JSON line from rank 0. `value` = algorithmic bytes of all ranks per step /
 max-over-ranks step time, in GB/s (K/V cache reads dominate; the working set of
@@ -64,6 +66,8 @@ def parse_args():
                     help="override the number of sequences (smaller cases for ncu captures)")
     ap.add_argument("--emulate-shard", type=int, default=1,
                     help="run rank 0's KV-head shard of an N-way split on this one GPU")
+    ap.add_argument("--eager", action="store_true",
+                    help="time eager launches instead of CUDA-graph replays of the step")
     return ap.parse_args()
 
 
@@ -214,6 +218,29 @@ def run_ours(args, rank, world, local):
         step()
     torch.cuda.synchronize()
 
+    def replayed(fn):
+        """fn, or a replay of one CUDA graph of fn (the reference's model runner replays
+        its decode step from a captured graph, model_runner.py:690-704, 761-795)."""
+        if args.eager:
+            return fn
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        graphs.append(graph)
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        torch.cuda.synchronize(device)
+        return graph.replay
+
+    graphs = []
+    step_r, decode_r, append_r = replayed(step), replayed(decode), replayed(append)
+
     def barrier():
         if world > 1:
             dist.barrier()
@@ -247,13 +274,13 @@ def run_ours(args, rank, world, local):
     # ---- device-resident step (the headline `value`), clocks sampled meanwhile
     sampler = ClockSampler(local)
     with sampler:
-        step_ms = timed(step, args.steps)
+        step_ms = timed(step_r, args.steps)
     clocks = sampler.summary() if rank == 0 else None
     step_ms_max = max_over_ranks(step_ms)
 
     # ---- the dominant kernel(s) alone: decode (main kernel + split merge)
-    decode_ms = max_over_ranks(timed(decode, args.steps))
-    append_ms = max_over_ranks(timed(append, args.steps))
+    decode_ms = max_over_ranks(timed(decode_r, args.steps))
+    append_ms = max_over_ranks(timed(append_r, args.steps))
 
     step_bytes = w.decode_bytes() + w.append_bytes()
     total_step_bytes = sum_over_ranks(step_bytes)
@@ -265,33 +292,88 @@ def run_ours(args, rank, world, local):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        hq = w.query.cpu().pin_memory()
-        hk, hv = w.new_k.cpu().pin_memory(), w.new_v.cpu().pin_memory()
-        hs = w.slot_mapping.cpu().pin_memory()
-        hbt, hcl = w.block_tables.cpu().pin_memory(), w.context_lens.cpu().pin_memory()
-        hout = torch.empty(w.query.shape, dtype=w.query.dtype).pin_memory()
-        dq, dk, dv = torch.empty_like(w.query), torch.empty_like(w.new_k), torch.empty_like(w.new_v)
-        ds, dbt, dcl = torch.empty_like(w.slot_mapping), torch.empty_like(w.block_tables), torch.empty_like(w.context_lens)
+        # The step's host inputs packed into one pinned buffer (256-byte aligned parts),
+        # so that each step makes one host-to-device copy into a device buffer whose
+        # views are the step's input tensors. Two such buffers (each with its own
+        # captured step and output) let step i+1's input copy and step i-1's output copy
+        # run on copy streams while step i computes; every step still copies its inputs
+        # in and its output out inside the timed region.
+        srcs = (w.query, w.new_k, w.new_v, w.slot_mapping, w.block_tables, w.context_lens)
+        offs, n = [], 0
+        for t in srcs:
+            offs.append(n)
+            n += (t.numel() * t.element_size() + 255) // 256 * 256
+        hbuf = torch.empty(n, dtype=torch.uint8).pin_memory()
 
-        def e2e_step():
-            dq.copy_(hq, non_blocking=True)
-            dk.copy_(hk, non_blocking=True)
-            dv.copy_(hv, non_blocking=True)
-            ds.copy_(hs, non_blocking=True)
-            dbt.copy_(hbt, non_blocking=True)
-            dcl.copy_(hcl, non_blocking=True)
-            if fp8:
-                attn.store_kvcache_fp8(dk, dv, w.k_cache, w.v_cache, ks, vs, ds, w.block_size, "fp8_per_tensor")
-            else:
-                attn.store_kvcache(dk, dv, w.k_cache, w.v_cache, ds, w.block_size)
-            out = decode(dq, dbt, dcl)
-            hout.copy_(out, non_blocking=True)
+        def part(buf, t, off):
+            nb = t.numel() * t.element_size()
+            return buf[off:off + nb].view(t.dtype).view(t.shape)
 
-        for _ in range(2):
-            e2e_step()
-        e2e_ms = max_over_ranks(timed(e2e_step, args.steps))
-        h2d = sum_over_ranks(sum(t.numel() * t.element_size() for t in (hq, hk, hv, hs, hbt, hcl)))
-        d2h = sum_over_ranks(hout.numel() * hout.element_size())
+        for t, off in zip(srcs, offs):
+            part(hbuf, t, off).copy_(t.cpu())
+
+        def make_slot():
+            dbuf = torch.empty(n, dtype=torch.uint8, device=device)
+            dq, dk, dv, ds, dbt, dcl = (part(dbuf, t, off) for t, off in zip(srcs, offs))
+            dout = []
+
+            def device_part():  # append + decode on this slot's device input views
+                if fp8:
+                    attn.store_kvcache_fp8(dk, dv, w.k_cache, w.v_cache, ks, vs, ds, w.block_size,
+                                           "fp8_per_tensor")
+                else:
+                    attn.store_kvcache(dk, dv, w.k_cache, w.v_cache, ds, w.block_size)
+                dout[:] = [decode(dq, dbt, dcl)]
+
+            dbuf.copy_(hbuf)
+            run = replayed(device_part)
+            hout = torch.empty(w.query.shape, dtype=w.query.dtype).pin_memory()
+            return dbuf, run, dout, hout
+
+        slots = [make_slot() for _ in range(2)]
+        copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_used = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+
+        def e2e_steps(n_steps):
+            """n_steps end-to-end steps; returns the device ms per step (events on the
+            launching stream around all of them, copy streams joined before the end)."""
+            barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            copy_in.wait_stream(stream)
+            copy_out.wait_stream(stream)
+            for i in range(n_steps):
+                k = i % 2
+                dbuf, run, dout, hout = slots[k]
+                if i >= 2:
+                    copy_in.wait_event(ev_used[k])  # step i-2 no longer reads this buffer
+                with torch.cuda.stream(copy_in):
+                    dbuf.copy_(hbuf, non_blocking=True)
+                ev_in[k].record(copy_in)
+                stream.wait_event(ev_in[k])
+                if i >= 2:
+                    stream.wait_event(ev_out[k])  # step i-2's output has been copied out
+                run()
+                ev_used[k].record(stream)
+                copy_out.wait_event(ev_used[k])
+                with torch.cuda.stream(copy_out):
+                    hout.copy_(dout[0], non_blocking=True)
+                if args.eager:  # a fresh output each call: keep it alive for the copy stream
+                    dout[0].record_stream(copy_out)
+                ev_out[k].record(copy_out)
+            stream.wait_stream(copy_out)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier()
+            return e0.elapsed_time(e1) / n_steps
+
+        e2e_steps(4)
+        e2e_ms = max_over_ranks(e2e_steps(args.steps))
+        h2d = sum_over_ranks(hbuf.numel())
+        d2h = sum_over_ranks(slots[0][3].numel() * slots[0][3].element_size())
         e2e = {"value": round(total_step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e2e_ms, 4), "decode_tokens_per_s": round(batch / (e2e_ms * 1e-3), 1),
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
@@ -306,6 +388,8 @@ def run_ours(args, rank, world, local):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(args.config, reps=5)
 
+    graphs.clear()
+    torch.cuda.synchronize(device)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -325,7 +409,10 @@ def run_ours(args, rank, world, local):
                                    f"rank 0 of a {args.emulate_shard}-way kv-head split, one GPU"
                                    if args.emulate_shard > 1 else "single GPU"),
                    "l2": "working set >> 126 MB L2 (no flush needed)",
-                   "step": "append 1 token/seq + paged decode"},
+                   "step": "append 1 token/seq + paged decode",
+                   "launch": "eager" if args.eager else
+                             "CUDA-graph replay of the step (e2e: one pinned H2D copy, replay, D2H copy per step, "
+                             "copies of neighbouring steps overlapped on two copy streams)"},
         "decode_tokens_per_s": round(tokens_per_s, 1),
         "append_ms": round(append_ms, 4), "decode_ms": round(decode_ms, 4),
         "e2e": e2e,
