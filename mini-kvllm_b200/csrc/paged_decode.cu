@@ -470,9 +470,15 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* ctr, unsigned
 // the last to arrive (per-unit counter) merges all partials in one online pass (running
 // maximum with rescaling, the same arithmetic as the softmax) and writes the output; it
 // also zeroes the counter for the next launch.
+// wbuf (wcap floats of shared memory the CTA no longer needs, or nullptr) holds the
+// merge's per-(partial, head) weights. The merge then computes each weight once, one
+// warp per head, and its output loop is one independent load and one FMA per partial,
+// so a unit split over many CTAs (small batches of long contexts) merges in a few L2
+// round trips instead of one per partial.
 template <typename QT>
 __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
-                           const float* o_s, int ld, const float* m_s, const float* l_s) {
+                           const float* o_s, int ld, const float* m_s, const float* l_s,
+                           float* wbuf = nullptr, int wcap = 0) {
   const int D = p.head_dim;
   const int seq = sg.seq, active = sg.nparts;
   const float vs = p.v_scale != nullptr ? __ldg(p.v_scale) : 1.0f;
@@ -500,10 +506,62 @@ __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
   if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(ctr, 1u) == (unsigned)(active - 1);
   __syncthreads();
   if (!last) return;
-  // OUT outputs per thread at a time. Two passes over the partials: their maximum, then
+  constexpr int OUT = 4;
+  if (wbuf != nullptr && (active + 1) * nh <= wcap) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    // wbuf[s * nh + h] = exp2(m_s,h - M_h) (0 for a partial without visible tokens);
+    // wbuf[active * nh + h] = L_h = sum_s l_s,h * wbuf[s * nh + h]
+    for (int h = warp; h < nh; h += nwarps) {
+      float mx = -INFINITY;
+      for (int s = lane; s < active; s += 32)
+        mx = fmaxf(mx, __ldcg(p.part_ml + part_row(p, sg, h0, s, h) * 2));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float l = 0.0f;
+      for (int s = lane; s < active; s += 32) {
+        const int64_t b = part_row(p, sg, h0, s, h);
+        const float m = __ldcg(p.part_ml + b * 2), lv = __ldcg(p.part_ml + b * 2 + 1);
+        const float c = m == -INFINITY ? 0.0f : exp2f(m - mx);
+        wbuf[s * nh + h] = c;
+        l = fmaf(lv, c, l);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      if (lane == 0) wbuf[active * nh + h] = l;
+    }
+    __syncthreads();
+    for (int base = threadIdx.x; base < nh * D; base += OUT * blockDim.x) {
+      float O[OUT];
+      int hh[OUT], dd[OUT];
+#pragma unroll
+      for (int i = 0; i < OUT; ++i) {
+        const int idx = base + i * blockDim.x;
+        const bool live = idx < nh * D;
+        hh[i] = live ? idx / D : 0;
+        dd[i] = live ? idx - hh[i] * D : 0;
+        O[i] = 0.0f;
+      }
+#pragma unroll 8
+      for (int s = 0; s < active; ++s)
+#pragma unroll
+        for (int i = 0; i < OUT; ++i)
+          O[i] = fmaf(__ldcg(p.part_acc + part_row(p, sg, h0, s, hh[i]) * D + dd[i]),
+                      wbuf[s * nh + hh[i]], O[i]);
+#pragma unroll
+      for (int i = 0; i < OUT; ++i) {
+        const int idx = base + i * blockDim.x;
+        if (idx < nh * D)
+          op[(int64_t)seq * p.o_sb + (int64_t)(h0 + hh[i]) * p.o_sh + dd[i]] =
+              from_f32<QT>(O[i] * vs / wbuf[active * nh + hh[i]]);
+      }
+    }
+    if (threadIdx.x == 0) *ctr = 0u;
+    return;
+  }
+  // Without a weight buffer (CUDA-core kernel): OUT outputs per thread at a time, two
+  // passes over the partials: their maximum, then
   // the weighted sums; the loads of up to 8 partials are independent of each other, so
   // they are in flight together instead of one online step after another.
-  constexpr int OUT = 4;
   for (int base = threadIdx.x; base < nh * D; base += OUT * blockDim.x) {
     float M[OUT], L[OUT], O[OUT];
     int64_t row[OUT];
@@ -1295,7 +1353,8 @@ paged_decode_tc_kernel(const DecodeParams p) {
   }
   __syncthreads();
   MKV_DTRACE(9 + 10 * nseg);
-  finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s);
+  // slots 1-3 of red_acc are free once the warps' results are merged into slot 0
+  finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s, red_acc + HC * RP, 3 * HC * RP);
   MKV_DTRACE(10 + 10 * nseg);
   ++nseg;
   if (!kPrefetch) has = sched_next<kTcTile>(p, sched);
@@ -1721,7 +1780,8 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
     red_acc[h * RP + d] = kPT ? ldexpf(O, v_exp) : O;
   }
   __syncthreads();
-  finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s);
+  // slots 1-3 of red_acc are free once the warps' results are merged into slot 0
+  finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s, red_acc + HC * RP, 3 * HC * RP);
   if (!kPrefetch) has = sched_next<kF8Tile>(p, sched);
   }
 }
