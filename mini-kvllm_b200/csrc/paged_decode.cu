@@ -939,6 +939,9 @@ template <> struct TcTraits<fp8> {
   static constexpr bool kByte = true;
   static __device__ __forceinline__ uint32_t to_f16x2(uint16_t v) { return e4m3x2_to_f16x2(v); }
 };
+// int8 pages enter the f16 MMAs as x + kInt8Bias (exact in f16), and the kernel takes the
+// bias back out of S and O.
+constexpr float kInt8Bias = 1152.0f;
 template <> struct TcTraits<int8_t> {
   using MT = f16;
   static constexpr bool kByte = true;
@@ -980,6 +983,7 @@ paged_decode_tc_kernel(const DecodeParams p) {
   using Tr = TcTraits<CT>;
   using MT = typename Tr::MT;
   constexpr bool kFp8 = Tr::kByte;  // 8-bit pages (e4m3 or int8), converted to f16
+  constexpr bool kBias = std::is_same<CT, int8_t>::value;  // int8 pages as x + 1152 (below)
   constexpr int D = kTcD;
   constexpr int EB = sizeof(CT);
   constexpr int ROWB = D * EB;    // 256 (16-bit) or 128 (e4m3) bytes per token row
@@ -1090,17 +1094,42 @@ paged_decode_tc_kernel(const DecodeParams p) {
       qb[nt][ks][0] = pack2<MT>(qval(row, qcol(ks, 0, 0)) * qpow2, qval(row, qcol(ks, 0, 1)) * qpow2);
       qb[nt][ks][1] = pack2<MT>(qval(row, qcol(ks, 1, 0)) * qpow2, qval(row, qcol(ks, 1, 1)) * qpow2);
     }
+  // int8 pages enter the MMAs as the exact f16 values x + 1152 (bit pattern 0x64XX with
+  // XX = x ^ 0x80), so S^T = K Q^T comes out as S + 1152 * sum_d q[h][d]. qbias holds that
+  // offset for heads 2tig + e, from the f16 query values the MMAs use.
+  float qbias[NT][2];
+  if (kBias) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float sq = 0.0f;  // head g over this lane's k subset
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const uint32_t w = qb[nt][ks][r];
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+          sq += f.x + f.y;
+        }
+      sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+      sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        qbias[nt][e] = kInt8Bias * __shfl_sync(0xffffffffu, sq, (2 * tig + e) * 4);
+    }
+  }
   MKV_DTRACE(5 + 10 * nseg);
   const float ksc = (kFp8 && !kPT) ? __ldg(p.k_scale) : 1.0f;
   const float sc = p.qk_scale_log2 * ksc / qpow2;
 
   // ---- per-warp softmax state for heads nt*8 + 2tig + e, and O^T accumulators
   float m_run[NT][2], l_run[NT][2];
+  float w_run[NT][2];  // int8 pages: sum of the f16 P^T values fed to the PV MMAs, per head
   float o[NT][D / 16][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     m_run[nt][0] = m_run[nt][1] = -INFINITY;
     l_run[nt][0] = l_run[nt][1] = 0.0f;
+    w_run[nt][0] = w_run[nt][1] = 0.0f;
 #pragma unroll
     for (int j = 0; j < D / 16; ++j) o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.0f;
   }
@@ -1155,10 +1184,18 @@ paged_decode_tc_kernel(const DecodeParams p) {
 #pragma unroll
           for (int hc = 0; hc < 2; ++hc) {
             uint32_t a[4];
-            a[0] = Tr::to_f16x2((uint16_t)(x[2 * hc] & 0xffffu));
-            a[1] = Tr::to_f16x2((uint16_t)(x[2 * hc + 1] & 0xffffu));
-            a[2] = Tr::to_f16x2((uint16_t)(x[2 * hc] >> 16));
-            a[3] = Tr::to_f16x2((uint16_t)(x[2 * hc + 1] >> 16));
+            if (kBias) {  // bytes 0,1 / 2,3 -> f16x2 of x + 1152
+              const uint32_t xa = x[2 * hc] ^ 0x80808080u, xb = x[2 * hc + 1] ^ 0x80808080u;
+              a[0] = __byte_perm(xa, 0x64646464u, 0x5140);
+              a[1] = __byte_perm(xb, 0x64646464u, 0x5140);
+              a[2] = __byte_perm(xa, 0x64646464u, 0x5342);
+              a[3] = __byte_perm(xb, 0x64646464u, 0x5342);
+            } else {
+              a[0] = Tr::to_f16x2((uint16_t)(x[2 * hc] & 0xffffu));
+              a[1] = Tr::to_f16x2((uint16_t)(x[2 * hc + 1] & 0xffffu));
+              a[2] = Tr::to_f16x2((uint16_t)(x[2 * hc] >> 16));
+              a[3] = Tr::to_f16x2((uint16_t)(x[2 * hc + 1] >> 16));
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
               Mma<MT>::run(s[nt], a, qb[nt][2 * kq + hc][0], qb[nt][2 * kq + hc][1]);
@@ -1168,6 +1205,15 @@ paged_decode_tc_kernel(const DecodeParams p) {
     }
 
     // ---- per-token scales (kPT): K scale on S^T rows, V scale kept for P
+    if (kBias) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        s[nt][0] -= qbias[nt][0];
+        s[nt][1] -= qbias[nt][1];
+        s[nt][2] -= qbias[nt][0];
+        s[nt][3] -= qbias[nt][1];
+      }
+    }
     float vsc0 = 1.0f, vsc1 = 1.0f;
     if (kPT) {
       const float* rs = rs_s + stage * 2 * kTcTile;
@@ -1216,8 +1262,16 @@ paged_decode_tc_kernel(const DecodeParams p) {
         }
       }
       // P^T as the B operand (K = tokens, N = heads): transpose the 8x8 blocks
-      pb[nt][0] = movmatrix_trans(pack2<MT>(s[nt][0] * vsc0, s[nt][1] * vsc0));  // tokens 0-7
-      pb[nt][1] = movmatrix_trans(pack2<MT>(s[nt][2] * vsc1, s[nt][3] * vsc1));  // tokens 8-15
+      const uint32_t u0 = pack2<MT>(s[nt][0] * vsc0, s[nt][1] * vsc0);  // token g, heads 2tig(+1)
+      const uint32_t u1 = pack2<MT>(s[nt][2] * vsc1, s[nt][3] * vsc1);  // token g + 8
+      if (kBias) {
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&u0));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&u1));
+        w_run[nt][0] = fmaf(w_run[nt][0], alpha[0], f0.x + f1.x);
+        w_run[nt][1] = fmaf(w_run[nt][1], alpha[1], f0.y + f1.y);
+      }
+      pb[nt][0] = movmatrix_trans(u0);  // tokens 0-7
+      pb[nt][1] = movmatrix_trans(u1);  // tokens 8-15
     }
 
     // ---- O^T += V^T P^T, one 16-row (head_dim) M tile per MMA
@@ -1245,13 +1299,21 @@ paged_decode_tc_kernel(const DecodeParams p) {
         ldmatrix_x4_trans(vbase + r * ROWB + ((lc ^ lrow) << 4), x[0], x[1], x[2], x[3]);
 #pragma unroll
         for (int hc = 0; hc < 2; ++hc) {
-          const uint32_t ya = __byte_perm(x[2 * hc], 0u, 0x3120);      // tokens 0-7
-          const uint32_t yb = __byte_perm(x[2 * hc + 1], 0u, 0x3120);  // tokens 8-15
           uint32_t a[4];
-          a[0] = Tr::to_f16x2((uint16_t)(ya & 0xffffu));
-          a[1] = Tr::to_f16x2((uint16_t)(ya >> 16));
-          a[2] = Tr::to_f16x2((uint16_t)(yb & 0xffffu));
-          a[3] = Tr::to_f16x2((uint16_t)(yb >> 16));
+          if (kBias) {  // the same byte order as below, straight to f16x2 of x + 1152
+            const uint32_t xa = x[2 * hc] ^ 0x80808080u, xb = x[2 * hc + 1] ^ 0x80808080u;
+            a[0] = __byte_perm(xa, 0x64646464u, 0x5240);
+            a[1] = __byte_perm(xa, 0x64646464u, 0x5341);
+            a[2] = __byte_perm(xb, 0x64646464u, 0x5240);
+            a[3] = __byte_perm(xb, 0x64646464u, 0x5341);
+          } else {
+            const uint32_t ya = __byte_perm(x[2 * hc], 0u, 0x3120);      // tokens 0-7
+            const uint32_t yb = __byte_perm(x[2 * hc + 1], 0u, 0x3120);  // tokens 8-15
+            a[0] = Tr::to_f16x2((uint16_t)(ya & 0xffffu));
+            a[1] = Tr::to_f16x2((uint16_t)(ya >> 16));
+            a[2] = Tr::to_f16x2((uint16_t)(yb & 0xffffu));
+            a[3] = Tr::to_f16x2((uint16_t)(yb >> 16));
+          }
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) Mma<MT>::run(o[nt][2 * cq + hc], a, pb[nt][0], pb[nt][1]);
         }
@@ -1316,13 +1378,21 @@ paged_decode_tc_kernel(const DecodeParams p) {
       l += __shfl_xor_sync(0xffffffffu, l, 16);
       const int head = nt * 8 + 2 * tig + e;
       float* ra = red_acc + (warp * HC + head) * RP;
+      float obias = 0.0f;  // int8 pages: O^T came out as O + 1152 * (sum of P^T values)
+      if (kBias) {
+        float wsum = w_run[nt][e];
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 4);
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 8);
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 16);
+        obias = kInt8Bias * wsum;
+      }
 #pragma unroll
       for (int j = 0; j < D / 16; ++j) {
         // O^T rows: 16-bit pages d = 16j + g / 16j + 8 + g; e4m3 pages d = 16j + 2g / + 1
         const int d0 = kFp8 ? 16 * j + 2 * g : 16 * j + g;
         const int d1 = kFp8 ? d0 + 1 : d0 + 8;
-        ra[d0] = o[nt][j][e];
-        ra[d1] = o[nt][j][e + 2];
+        ra[d0] = o[nt][j][e] - obias;
+        ra[d1] = o[nt][j][e + 2] - obias;
       }
       if (g == 0) {
         red_m[warp * HC + head] = m_run[nt][e];
