@@ -631,14 +631,21 @@ __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
   // per-token scales of 8-bit pages: entry r < TILE is row r's K scale, TILE + r its V
   // scale (zero for rows that are not loaded)
   if (rs != nullptr && one_page_per_tile) {  // one page: row r's scales are r * KVH apart
+    static_assert(TILE == kThreads || 2 * TILE == kThreads, "one K or V row scale pair per thread");
     const int page = slice_page(p, seq, slice, bt_s, t0 >> p.bs_shift);
     const int nrows = page >= 0 ? min(TILE, rng.end - t0) : 0;
     const int64_t base =
         ((int64_t)(page >= 0 ? page : 0) * p.block_size + (t0 & ((1 << p.bs_shift) - 1))) * p.num_kv_heads + kvh;
-    for (int i = tid; i < 2 * TILE; i += kThreads) {
-      const int r = i < TILE ? i : i - TILE;
-      const float* src = (i < TILE ? p.k_scales : p.v_scales) + base + (int64_t)r * p.num_kv_heads;
-      cp_async_4(smem_u32(rs + i), r < nrows ? src : p.k_scales, r < nrows ? 4 : 0);
+    if constexpr (TILE == kThreads) {  // row tid: its K scale and its V scale
+      const int64_t off = base + (int64_t)tid * p.num_kv_heads;
+      const bool ok = tid < nrows;
+      cp_async_4(smem_u32(rs + tid), ok ? p.k_scales + off : p.k_scales, ok ? 4 : 0);
+      cp_async_4(smem_u32(rs + TILE + tid), ok ? p.v_scales + off : p.v_scales, ok ? 4 : 0);
+    } else {  // threads [0, TILE): K scales; [TILE, 2 TILE): V scales (whole warps each)
+      const int r = tid < TILE ? tid : tid - TILE;
+      const float* src = (tid < TILE ? p.k_scales : p.v_scales);
+      const bool ok = r < nrows;
+      cp_async_4(smem_u32(rs + tid), ok ? src + base + (int64_t)r * p.num_kv_heads : src, ok ? 4 : 0);
     }
   } else if (rs != nullptr) {
     for (int i = tid; i < 2 * TILE; i += kThreads) {
@@ -1665,12 +1672,16 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       float vm = fmaxf(fmaxf(rs[kF8Tile + lane], rs[kF8Tile + 32 + lane]),
                        fmaxf(rs[kF8Tile + 64 + lane], rs[kF8Tile + 96 + lane]));
       vm = warp_max(vm);  // every warp finds the same tile maximum
+      // e with vm < 2^e from the exponent field (scales are >= 0), kept in [-126, 126]
+      // so that 2^-e and the power-of-two rescales below are built from bits directly
       int e = v_exp;
-      if (vm > 0.0f && isfinite(vm)) frexpf(vm, &e);  // vm < 2^e
+      const uint32_t vb = __float_as_uint(vm);
+      if (vb != 0u && (vb >> 23) < 0xffu) e = min((int)(vb >> 23) - 126, 126);
       if (it == 0) v_exp = e;  // O is still zero
-      o_rescale = ldexpf(1.0f, v_exp - e);
+      const int d = max(min(v_exp - e, 127), -126);
+      o_rescale = __uint_as_float((uint32_t)(d + 127) << 23);  // 2^(v_exp - e)
       v_exp = e;
-      const float inv = ldexpf(1.0f, -e);
+      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
