@@ -90,6 +90,7 @@ struct DecodeParams {
   int balanced;
   int sched_ctas;
   int min_tiles;
+  int unit_cost;  // balanced: items charged per unit before its tiles (segment overhead)
   int q_vec16;  // query rows start on 16-byte boundaries (base and both strides)
   int32_t* invalid;
 };
@@ -245,11 +246,12 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
 #pragma unroll
     for (int j = 0; j < kScanCache; ++j) {
       const int sq = tid * kScanCache + j;
-      tl[j] = sq < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, sq)) : 0;
+      tl[j] = sq < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, sq)) + p.unit_cost : 0;
       part += tl[j];
     }
   } else {
-    for (int sq = tid; sq < p.num_seqs; sq += kThreads) part += unit_tiles<TILE>(eff_ctx(p, sq));
+    for (int sq = tid; sq < p.num_seqs; sq += kThreads)
+      part += unit_tiles<TILE>(eff_ctx(p, sq)) + p.unit_cost;
   }
   // inclusive block scan of the per-thread sums (cached layout: sequence order)
   long long x = part;
@@ -300,7 +302,7 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
       long long carry = 0;
       for (int base = 0; base < p.num_seqs; base += kThreads) {
         const int sq = base + tid;
-        const long long t = sq < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, sq)) : 0;
+        const long long t = sq < p.num_seqs ? unit_tiles<TILE>(eff_ctx(p, sq)) + p.unit_cost : 0;
         long long y = t;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -345,8 +347,8 @@ __device__ void sched_init(const DecodeParams& p, SchedState& st) {
         st.unit_start = found[1];
       } else {
         const long long r = w - found[1] * U;
-        st.y = (int)(r / st.nt);
-        st.unit_start = found[1] * U + (long long)st.y * st.nt;
+        st.y = (int)(r / (st.nt + p.unit_cost));
+        st.unit_start = found[1] * U + (long long)st.y * (st.nt + p.unit_cost);
       }
     }
   }
@@ -379,33 +381,41 @@ __device__ bool sched_next(const DecodeParams& p, SchedState& st) {
         }
       }
     } else if (st.w < st.w_end) {
-      has = 1;
+      // A unit's items are unit_cost charge items, then its nt tiles: the charge stands
+      // for the fixed cost of a segment, so a rank whose range crosses into a new unit
+      // streams that many fewer tiles.
       const int nt = st.nt;
-      const int tb = (int)(st.w - st.unit_start);
-      const long long rem = st.w_end - st.unit_start;
-      const int te = rem < nt ? (int)rem : nt;
-      sg.seq = st.seq;
-      sg.y = st.y;
-      sg.begin = tb * TILE;
-      sg.end = min(te * TILE, st.eff);
-      const long long c_first = cta_of(st, st.unit_start);
-      const long long c_last = cta_of(st, st.unit_start + nt - 1);
-      sg.nparts = (int)(c_last - c_first + 1);
-      sg.part = (int)(st.rank - c_first);
-      sg.c_first = (int)c_first;
-      sg.first_off = (st.W * c_first / st.G) < st.unit_start ? 1 : 0;
-      sg.cta_base = st.lanes ? st.y : 0;
-      sg.cta_stride = st.lanes ? st.U : 1;
-      st.w = st.unit_start + te;
-      if (te == nt) {
-        st.unit_start += nt;
-        const bool next_seq = st.lanes || ++st.y == st.U;
-        if (next_seq) {
-          if (!st.lanes) st.y = 0;
-          ++st.seq;
-          if (st.w < st.w_end) {
-            st.eff = eff_ctx(p, st.seq);
-            st.nt = unit_tiles<TILE>(st.eff);
+      const long long first = st.unit_start + p.unit_cost;  // item of the unit's tile 0
+      const long long tb = st.w > first ? st.w - first : 0;
+      const long long rem = st.w_end - first;
+      const long long te = rem < nt ? rem : nt;
+      if (te <= tb) {
+        st.w = st.w_end;  // the range ends inside the unit's charge items
+      } else {
+        has = 1;
+        sg.seq = st.seq;
+        sg.y = st.y;
+        sg.begin = (int)tb * TILE;
+        sg.end = min((int)te * TILE, st.eff);
+        const long long c_first = cta_of(st, first);
+        const long long c_last = cta_of(st, first + nt - 1);
+        sg.nparts = (int)(c_last - c_first + 1);
+        sg.part = (int)(st.rank - c_first);
+        sg.c_first = (int)c_first;
+        sg.first_off = (st.W * c_first / st.G) < st.unit_start ? 1 : 0;
+        sg.cta_base = st.lanes ? st.y : 0;
+        sg.cta_stride = st.lanes ? st.U : 1;
+        st.w = first + te;
+        if (te == nt) {
+          st.unit_start = first + nt;
+          const bool next_seq = st.lanes || ++st.y == st.U;
+          if (next_seq) {
+            if (!st.lanes) st.y = 0;
+            ++st.seq;
+            if (st.w < st.w_end) {
+              st.eff = eff_ctx(p, st.seq);
+              st.nt = unit_tiles<TILE>(st.eff);
+            }
           }
         }
       }
@@ -1913,13 +1923,22 @@ int head_groups_for(int group) { return (group + kMaxHeadsPerCta - 1) / kMaxHead
 // Balanced schedule bound: at most kMaxResident CTAs (B200: 148 SMs x 4).
 constexpr int kMaxResident = kNumSMs * 4;
 
+// Items charged per unit in the balanced schedule of the tensor-core kernels, ahead of
+// its tiles: a segment's fixed cost (hand-over, the 4 warps' merge, the partial write)
+// is about that many tiles of streaming, so ranks that cross into more units get fewer
+// tiles and all ranks finish together.
+#ifndef MKV_DECODE_UNIT_COST
+#define MKV_DECODE_UNIT_COST 3
+#endif
+constexpr int kUnitCost = MKV_DECODE_UNIT_COST;
+
 // The balanced schedule serves num_splits = 0 unless its work-item arithmetic
 // (W * G < 2^62 with W <= units * (cap / 32 + 1)) could overflow.
 bool use_balanced(int num_seqs, int num_kv_heads, int head_groups, int block_size,
                   int max_blocks, int num_splits) {
   if (num_splits != 0) return false;
   const double units = (double)num_seqs * num_kv_heads * head_groups;
-  const double items = units * ((double)max_blocks * block_size / 32.0 + 1.0);
+  const double items = units * ((double)max_blocks * block_size / 32.0 + 1.0 + kUnitCost);
   return items * kMaxResident < 4.0e18;
 }
 
@@ -2013,6 +2032,7 @@ int launch_decode(DecodeParams p, int tile, size_t smem, cudaStream_t stream, in
     if (st != MKV_OK) return st;
     p.sched_ctas = g;
     p.min_tiles = min_tiles_for(tile, p.block_size, p.max_blocks);
+    p.unit_cost = tile == kGenTile ? 0 : kUnitCost;
     grid = dim3(g, 1, 1);
   }
   Kernel<<<grid, kThreads, smem, stream>>>(p);
@@ -2198,6 +2218,7 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.balanced = balanced ? 1 : 0;
   p.sched_ctas = 0;  // set at launch from the kernel's occupancy
   p.min_tiles = 1;
+  p.unit_cost = 0;
   uint8_t* ws = (uint8_t*)workspace;
   p.part_acc = wl.total ? (float*)(ws + wl.acc) : nullptr;
   p.part_ml = wl.total ? (float*)(ws + wl.ml) : nullptr;
