@@ -1,9 +1,10 @@
 """Generates tests/golden/*.npz by running the reference's own code on seeded inputs.
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py [--reference-src DIR]
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py --reference-src DIR
 
-DIR is the reference's `src` directory (heart1128/mini-kvllm; default
-/root/reference/src); its parent must hold benchmark_decoding.py. The script needs
+DIR is the `src` directory of a checkout of the reference (heart1128/mini-kvllm), or
+MKV_REFERENCE_SRC when the option is not given; its parent must hold
+benchmark_decoding.py. The script needs
 the reference only while it runs: the fixtures it writes carry the inputs (or the
 seed and a SHA-256 of them) and the reference's outputs, and the tests read only
 those files.
@@ -329,7 +330,8 @@ def make_residual_rmsnorm(src, rng):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--reference-src", default=os.environ.get("MKV_REFERENCE_SRC"),
+                    required="MKV_REFERENCE_SRC" not in os.environ)
     ap.add_argument("--only", default="", help="comma-separated fixture names")
     args = ap.parse_args()
     ref_attn, dto = _load_reference(args.reference_src)
