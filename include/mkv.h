@@ -71,6 +71,10 @@ extern "C" {
 /* Library version string ("major.minor.patch"). */
 MKV_API const char* mkv_version(void);
 
+/* 16 hex digits identifying the sources and compiler flags the library was built from,
+   so that every measurement can name the exact binary it ran. No reference counterpart. */
+MKV_API const char* mkv_source_hash(void);
+
 /* Human-readable name of a status code. */
 MKV_API const char* mkv_status_string(int status);
 
@@ -310,8 +314,11 @@ MKV_API size_t mkv_paged_prefill_workspace_bytes(int32_t num_seqs, int64_t total
  * that loads the library keeps until the process exits. A shape whose split scratch
  * (mkv_paged_decode_workspace_bytes with the same num_splits) exceeds that size is
  * rejected with MKV_ERR_WORKSPACE; num_splits = 1 needs no scratch at all.
- * The first call on a device looks up the array's device address (once per device,
- * with that device current); make that first call before any stream capture.
+ * The first call in a CUDA context looks up the array's device address in that context
+ * (cudaGetSymbolAddress, with the caller's device current) and caches it for that
+ * context only, keyed on the context's unique ID (cuCtxGetId): an address is never
+ * reused in another context, nor after cudaDeviceReset. Make the first call in each
+ * context before any stream capture.
  * All calls on a device share the one array: the part that must start at zero is
  * cleared on the stream at each call, but calls that overlap on the GPU (other streams,
  * other host threads) race on it and must be serialised by the caller.

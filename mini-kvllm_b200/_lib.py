@@ -27,6 +27,7 @@ _p, _i32, _i64, _f32, _sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, cty
 _cstr = ctypes.c_char_p
 SIGNATURES: dict[str, tuple] = {
     "mkv_version": (_cstr, []),
+    "mkv_source_hash": (_cstr, []),
     "mkv_status_string": (_cstr, [ctypes.c_int]),
     "mkv_last_error": (_cstr, []),
     "mkv_store_kvcache": (ctypes.c_int, [
@@ -96,6 +97,11 @@ def load() -> ctypes.CDLL:
                 fn.argtypes = args
             _lib = lib
     return _lib
+
+
+def source_hash() -> str:
+    """Hash of the sources the loaded libmkv.so was built from (see build.py)."""
+    return load().mkv_source_hash().decode()
 
 
 def check(fn: str, status: int) -> None:

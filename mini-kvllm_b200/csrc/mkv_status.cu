@@ -26,7 +26,13 @@ int cuda_status(cudaError_t err, const char* what) {
 
 }  // namespace mkv
 
-extern "C" const char* mkv_version(void) { return "0.1.0"; }
+extern "C" const char* mkv_version(void) { return "0.2.0"; }
+
+// Hash of the sources and compiler flags this library was built from (set by build.py).
+#ifndef MKV_SOURCE_HASH
+#define MKV_SOURCE_HASH "unknown"
+#endif
+extern "C" const char* mkv_source_hash(void) { return MKV_SOURCE_HASH; }
 
 extern "C" const char* mkv_status_string(int status) {
   switch (status) {

@@ -35,11 +35,11 @@
 //     num_splits > 0 instead splits every unit into fixed token chunks (flash-decoding)
 //     with the same epilogue. Nothing on the host depends on device data (graph-safe).
 // A CUDA-core kernel with the same tiling and epilogue covers fp32 and other head dims.
+#include <cuda.h>
 #include <mutex>
 #include <type_traits>
 
 #include "mkv_common.cuh"
-#include "paged_decode_tc05.cuh"
 
 namespace mkv {
 namespace {
@@ -138,25 +138,6 @@ __device__ __forceinline__ SplitRange split_range(const DecodeParams& p, int seq
   return r;
 }
 
-// Optional per-CTA event timestamps (globaltimer, ns) for studying the schedule; compiled
-// only with -DMKV_DECODE_TRACE and read back with mkv_debug_decode_trace.
-#ifdef MKV_DECODE_TRACE
-constexpr int kTraceEvents = 96;
-__device__ unsigned long long g_dtrace[kNumSMs * 4][kTraceEvents];
-#define MKV_DTRACE(ev)                                                              \
-  do {                                                                              \
-    if (threadIdx.x == 0 && (ev) < kTraceEvents && blockIdx.x < kNumSMs * 4) {      \
-      unsigned long long t_;                                                        \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                        \
-      g_dtrace[blockIdx.x][(ev)] = t_;                                              \
-    }                                                                               \
-  } while (0)
-constexpr int kTraceEventsLast = kTraceEvents - 1;
-#else
-#define MKV_DTRACE(ev) \
-  do {                 \
-  } while (0)
-#endif
 
 // ---------------------------------------------------------------- work schedule
 // A unit is (sequence, KV head, head group): y = kv_head * head_groups + head group.
@@ -198,12 +179,6 @@ __device__ __forceinline__ int eff_ctx(const DecodeParams& p, int seq) {
 // that its output (0/0 = NaN, as in the reference) is written.
 template <int TILE>
 __device__ __forceinline__ int unit_tiles(int eff) { return eff > 0 ? (eff + TILE - 1) / TILE : 1; }
-
-__device__ __forceinline__ long long warp_sum_ll(long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 
 // Schedule state, uniform across the CTA, kept in shared memory so the kernels' inner
 // loops carry none of it in registers. Thread 0 advances it between two barriers.
@@ -935,9 +910,9 @@ size_t generic_smem_bytes(int head_dim, int elem_bytes) {
 
 // ============================================================ tensor-core kernel
 // head_dim = 128; query bf16 with bf16 pages, f16 with f16 pages, or bf16/f16 with
-// e4m3 pages (f16 MMAs). NT = query heads of the CTA in units of 8 (MMA N tiles).
-// MMA operand type of a page type; 8-bit pages (e4m3, int8) are converted to f16 in
-// registers, two elements per conversion.
+// int8 pages (f16 MMAs). NT = query heads of the CTA in units of 8 (MMA N tiles).
+// MMA operand type of a page type; int8 pages are converted to f16 in registers, two
+// elements per conversion (e4m3 pages take the FP8-MMA kernel below).
 template <typename CT> struct TcTraits;
 template <> struct TcTraits<bf16> {
   using MT = bf16;
@@ -950,11 +925,6 @@ template <> struct TcTraits<f16> {
   static constexpr bool kByte = false;
   // 16-bit pages feed the MMA as they are; the 8-bit branch that calls this is dead
   static __device__ __forceinline__ uint32_t to_f16x2(uint16_t) { return 0u; }
-};
-template <> struct TcTraits<fp8> {
-  using MT = f16;
-  static constexpr bool kByte = true;
-  static __device__ __forceinline__ uint32_t to_f16x2(uint16_t v) { return e4m3x2_to_f16x2(v); }
 };
 // int8 pages enter the f16 MMAs as x + kInt8Bias (exact in f16), and the kernel takes the
 // bias back out of S and O.
@@ -1025,11 +995,8 @@ paged_decode_tc_kernel(const DecodeParams p) {
   // A tile never straddles a page when block_size is a power of two >= the tile.
   const bool one_page_per_tile = p.bs_shift >= 6;
   __shared__ SchedState sched;
-  MKV_DTRACE(0);
   sched_init<kTcTile>(p, sched);
-  MKV_DTRACE(1);
   bool has = sched_next<kTcTile>(p, sched);
-  int nseg = 0;
   bool prefetched = false;
   int gt = 0;
   BlockSlice slice{0, 0};
@@ -1043,12 +1010,10 @@ paged_decode_tc_kernel(const DecodeParams p) {
   const bool count_invalid = (kvh == 0 && hgrp == 0);
 
   const int ntiles = (rng.end - rng.begin + kTcTile - 1) / kTcTile;  // 0 when empty
-  MKV_DTRACE(2 + 10 * nseg);
   if (!prefetched) {
     slice = stage_block_table(p, seq, rng, bt_s, count_invalid);
     __syncthreads();
   }
-  MKV_DTRACE(3 + 10 * nseg);
 
   // ---- producer: all threads issue 16-byte cp.async for their rows/chunks
   const int64_t head_off = (int64_t)kvh * ROWB;
@@ -1071,7 +1036,6 @@ paged_decode_tc_kernel(const DecodeParams p) {
     }
   }
 
-  MKV_DTRACE(4 + 10 * nseg);
   // ---- Q^T fragments (B operand: K = head_dim, N = query heads of this CTA)
   cp_async_wait<STAGES - 1>();  // the query rows' group (older than the tiles')
   __syncthreads();
@@ -1134,7 +1098,6 @@ paged_decode_tc_kernel(const DecodeParams p) {
         qbias[nt][e] = kInt8Bias * __shfl_sync(0xffffffffu, sq, (2 * tig + e) * 4);
     }
   }
-  MKV_DTRACE(5 + 10 * nseg);
   const float ksc = (kFp8 && !kPT) ? __ldg(p.k_scale) : 1.0f;
   const float sc = p.qk_scale_log2 * ksc / qpow2;
 
@@ -1158,7 +1121,6 @@ paged_decode_tc_kernel(const DecodeParams p) {
     __syncthreads();
     if (it + STAGES - 1 < ntiles) load_tile(it + STAGES - 1);
     cp_async_commit();
-    if (it == 0) MKV_DTRACE(6 + 10 * nseg);
 
     const int stage = (gt + it) % STAGES;
     const uint32_t kbase = smem_u32(smem + stage * STAGE_BYTES);
@@ -1338,7 +1300,6 @@ paged_decode_tc_kernel(const DecodeParams p) {
     }
   }
   gt += ntiles;
-  MKV_DTRACE(7 + 10 * nseg);
 
   // ---- hand over to the next segment, then merge this one
   const Seg done = sched.cur;
@@ -1376,7 +1337,6 @@ paged_decode_tc_kernel(const DecodeParams p) {
     __syncthreads();
   }
 
-  MKV_DTRACE(8 + 10 * nseg);
   // ---- merge the 4 warps' states through shared memory (in a free ring stage)
   constexpr int RP = D + 4;     // padded row pitch (floats)
   constexpr int HC = 8 * NT;    // head slots of this CTA
@@ -1439,14 +1399,10 @@ paged_decode_tc_kernel(const DecodeParams p) {
     red_acc[h * RP + d] = O;  // in place: this thread alone reads and writes (h, d)
   }
   __syncthreads();
-  MKV_DTRACE(9 + 10 * nseg);
   // slots 1-3 of red_acc are free once the warps' results are merged into slot 0
   finish_cta<QT>(p, done, h0, nh, red_acc, RP, m_s, l_s, red_acc + HC * RP, 3 * HC * RP);
-  MKV_DTRACE(10 + 10 * nseg);
-  ++nseg;
   if (!kPrefetch) has = sched_next<kTcTile>(p, sched);
   }
-  MKV_DTRACE(kTraceEventsLast);
 }
 
 // ============================================================ FP8 tensor-core kernel
@@ -2065,7 +2021,6 @@ int launch_generic(const DecodeParams& p, cudaStream_t stream, int device) {
 template <typename CT> struct TcConfig;
 template <> struct TcConfig<bf16> { static constexpr int kStages = MKV_TC16_STAGES, kMinBlocks = MKV_TC16_MINB; };
 template <> struct TcConfig<f16> { static constexpr int kStages = MKV_TC16_STAGES, kMinBlocks = MKV_TC16_MINB; };
-template <> struct TcConfig<fp8> { static constexpr int kStages = MKV_TC8_STAGES, kMinBlocks = MKV_TC8_MINB; };
 template <> struct TcConfig<int8_t> { static constexpr int kStages = MKV_TC8_STAGES, kMinBlocks = MKV_TC8_MINB; };
 
 template <typename QT, typename CT, int NT, bool kPT>
@@ -2234,24 +2189,6 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
     if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(arrival counters)");
   }
 
-  // The tcgen05 kernel (compiled in with MKV_ENABLE_TC05) runs fixed split plans only.
-  if (!balanced && !per_token && tc05::supported(q_dtype, cache_dtype, head_dim, block_size, hpc)) {
-    tc05::Params t;
-    t.q = query; t.q_sb = q_sb; t.q_sh = q_sh;
-    t.num_blocks = num_blocks; t.block_size = block_size; t.bs_shift = p.bs_shift;
-    t.bt = bt; t.bt_sb = bt_sb; t.max_blocks = max_blocks; t.bt_i64 = p.bt_i64;
-    t.ctx = ctx; t.ctx_i64 = p.ctx_i64;
-    t.num_seqs = num_seqs; t.num_heads = num_heads; t.num_kv_heads = num_kv_heads;
-    t.group = group; t.heads_per_cta = hpc; t.head_groups = hgs;
-    t.qk_scale_log2 = p.qk_scale_log2; t.k_scale = p.k_scale; t.v_scale = p.v_scale;
-    t.out = out; t.o_sb = o_sb; t.o_sh = o_sh;
-    t.part_acc = p.part_acc; t.part_ml = p.part_ml; t.arrivals = p.arrivals;
-    t.num_splits = sp.num_splits; t.chunk = sp.chunk;
-    t.num_units = (int64_t)num_seqs * num_kv_heads * hgs * sp.num_splits;
-    t.invalid = invalid;
-    return tc05::launch(t, q_dtype, cache_dtype, k_cache, v_cache, s, device);
-  }
-
   const bool tc_ok = head_dim == kTcD && q_dtype != MKV_DTYPE_F32;
   if (per_token) {  // 8-bit pages with per-(page, row, kv head) scales
     const bool i8 = cache_dtype == MKV_DTYPE_INT8;
@@ -2290,26 +2227,92 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
 // ---------------------------------------------------------------- allocation-free entry
 // Built-in decode scratch for callers that cannot allocate device memory. Every device
 // that loads this library holds these MKV_NOALLOC_SCRATCH_BYTES until the process ends.
-// Host code only sees a shadow of this symbol: its device address is looked up once per
-// device below and passed to the kernels like any caller workspace.
+// Host code only sees a shadow of this symbol: its device address is looked up with
+// cudaGetSymbolAddress and passed to the kernels like any caller workspace.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[MKV_NOALLOC_SCRATCH_BYTES];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kMaxDevices] = {};
+// The address belongs to the CUDA context that was current when it was looked up (the
+// module is loaded per context). It is cached per context, keyed on the context's
+// unique ID from cuCtxGetId, which is never reused within a process: a caller's own
+// driver-API context, or the primary context created again after cudaDeviceReset, gets
+// a lookup of its own instead of an address from another or a destroyed context. The
+// two driver calls are resolved through cudaGetDriverEntryPoint, so the library needs
+// no link against libcuda.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Device address of g_noalloc_scratch on the current device (looked up on first use).
-int noalloc_scratch(int device, void** out) {
-  if (device < 0 || device >= kMaxDevices)
-    return set_error(MKV_ERR_UNSUPPORTED, "mkv_paged_decode_noalloc: device id %d >= %d", device,
-                     kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[device] == nullptr) {
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(built-in decode scratch)");
-    g_noalloc_ptr[device] = ptr;
+struct NoallocEntry {
+  unsigned long long ctx_id;
+  void* ptr;
+};
+constexpr int kNoallocCacheEntries = 64;
+std::mutex g_noalloc_mu;
+NoallocEntry g_noalloc_cache[kNoallocCacheEntries] = {};
+int g_noalloc_next = 0;  // round-robin replacement once the cache is full
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+int resolve_ctx_calls() {  // called with g_noalloc_mu held
+  if (g_ctx_get_current && g_ctx_get_id) return MKV_OK;
+  void* f1 = nullptr;
+  void* f2 = nullptr;
+  cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = q1;
+  cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1);
+  if (e != cudaSuccess || q1 != cudaDriverEntryPointSuccess || !f1)
+    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetCurrent is unavailable");
+  e = cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2);
+  if (e != cudaSuccess || q2 != cudaDriverEntryPointSuccess || !f2)
+    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetId is unavailable");
+  g_ctx_get_current = (CtxGetCurrentFn)f1;
+  g_ctx_get_id = (CtxGetIdFn)f2;
+  return MKV_OK;
+}
+
+// The current context's ID; *none = true (and MKV_OK) when no context is current yet.
+int current_ctx_id(unsigned long long* id, bool* none) {  // called with g_noalloc_mu held
+  CUcontext ctx = nullptr;
+  *none = false;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS)
+    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetCurrent failed");
+  if (ctx == nullptr) {
+    *none = true;
+    return MKV_OK;
   }
-  *out = g_noalloc_ptr[device];
+  if (g_ctx_get_id(ctx, id) != CUDA_SUCCESS)
+    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetId failed");
+  return MKV_OK;
+}
+
+// Device address of g_noalloc_scratch in the current context, looked up on the first
+// call in that context.
+int noalloc_scratch(void** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  int st = resolve_ctx_calls();
+  if (st != MKV_OK) return st;
+  unsigned long long id = 0;
+  bool none = false;
+  st = current_ctx_id(&id, &none);
+  if (st != MKV_OK) return st;
+  if (!none) {
+    for (const NoallocEntry& en : g_noalloc_cache)
+      if (en.ptr != nullptr && en.ctx_id == id) {
+        *out = en.ptr;
+        return MKV_OK;
+      }
+  }
+  // First call in this context (or no context current yet: the runtime's lookup below
+  // makes the device's primary context current, and its ID is read afterwards).
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(built-in decode scratch)");
+  if (none) {
+    st = current_ctx_id(&id, &none);
+    if (st != MKV_OK) return st;
+    if (none) return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: no current CUDA context");
+  }
+  g_noalloc_cache[g_noalloc_next] = NoallocEntry{id, ptr};
+  g_noalloc_next = (g_noalloc_next + 1) % kNoallocCacheEntries;
+  *out = ptr;
   return MKV_OK;
 }
 
@@ -2318,15 +2321,6 @@ int noalloc_scratch(int device, void** out) {
 
 using namespace mkv;
 
-#ifdef MKV_DECODE_TRACE
-extern "C" MKV_API int mkv_debug_decode_trace(void* host, int clear) {
-  if (clear) {
-    static unsigned long long zeros[kNumSMs * 4][kTraceEvents];
-    return (int)cudaMemcpyToSymbol(g_dtrace, zeros, sizeof(zeros));
-  }
-  return (int)cudaMemcpyFromSymbol(host, g_dtrace, sizeof(g_dtrace));
-}
-#endif
 
 extern "C" int32_t mkv_paged_decode_num_splits(int32_t num_seqs, int32_t num_heads,
                                                int32_t num_kv_heads, int32_t head_dim,
@@ -2422,10 +2416,7 @@ extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
                      need, (size_t)MKV_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
   if (need > 0) {
-    int device = 0;
-    cudaError_t e = cudaGetDevice(&device);
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
-    int st = noalloc_scratch(device, &scratch);
+    int st = noalloc_scratch(&scratch);
     if (st != MKV_OK) return st;
   }
   return decode_impl("mkv_paged_decode_noalloc", query, q_stride_seq, q_stride_head, q_dtype,

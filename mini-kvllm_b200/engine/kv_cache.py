@@ -4,8 +4,10 @@ ModelRunner.prepare_decode, and the tensor-parallel KV-head split.
 
 Reference (heart1128/mini-kvllm, src/myvllm/engine/model_runner.py):
   allocate_kv_cache   204-395  one zeros(2, L, NB, BS, KVH/world, D) tensor; fp8 caches are
-                               float8_e4m3fn (247); per-tensor scales ones(2, L, 1) fp32
-                               (324-329); layer l gets views [0, l] / [1, l] (376-395)
+                               float8_e4m3fn and int8 caches int8 (247-252); per-tensor
+                               scales ones(2, L, 1) fp32 (324-329); per-(token, head) scales
+                               ones(2, L, NB, BS, KVH/world) fp32 (330-338); layer l gets
+                               views [0, l] / [1, l] (376-395)
   prepare_decode      631-671  context_lens = len(seq) (includes the new token),
                                (decode_metadata restates it; DecodeMetadataBuilder
                                computes it with one copy and one kernel per step)
@@ -23,14 +25,15 @@ from typing import Iterable, Optional, Sequence
 
 import torch
 
-QUANTIZED = ("fp8_per_tensor",)
+PER_TOKEN_HEAD = ("fp8_per_token_head", "int8_per_token_head")
+QUANTIZED = ("fp8_per_tensor",) + PER_TOKEN_HEAD
 KV_CACHE_DTYPES = ("auto",) + QUANTIZED
 
 
 @dataclass
 class KVCache:
     kv: torch.Tensor                      # (2, L, NB, BS, KVH, D)
-    k_scale: Optional[torch.Tensor]       # (L, 1) fp32 views, or None
+    k_scale: Optional[torch.Tensor]       # (L, 1) or (L, NB, BS, KVH) fp32 views, or None
     v_scale: Optional[torch.Tensor]
     kv_cache_dtype: str
     block_size: int
@@ -46,16 +49,28 @@ def allocate_kv_cache(num_layers: int, num_blocks: int, block_size: int, num_kv_
                       head_dim: int, kv_cache_dtype: str = "auto",
                       default_dtype: torch.dtype = torch.bfloat16,
                       device: torch.device | str = "cuda") -> KVCache:
-    """One zero-initialised (2, L, NB, BS, KVH, D) cache; FP8 per-tensor scales start
-    at the calibration sentinel 1.0 (model_runner.py:311-329)."""
+    """One zero-initialised (2, L, NB, BS, KVH, D) cache (model_runner.py:311-314).
+    'fp8_per_tensor': float8_e4m3fn pages and (2, L, 1) float32 scales at the calibration
+    sentinel 1.0 (324-329). 'fp8_per_token_head' / 'int8_per_token_head': float8_e4m3fn /
+    int8 pages and one float32 scale per (page, row, kv head), (2, L, NB, BS, KVH), set to
+    1.0 (330-338); the append writes each row's scale."""
     if kv_cache_dtype not in KV_CACHE_DTYPES:
         raise NotImplementedError(f"kv_cache_dtype {kv_cache_dtype!r} is not implemented")
-    data_dtype = torch.float8_e4m3fn if kv_cache_dtype in QUANTIZED else default_dtype
+    if kv_cache_dtype == "int8_per_token_head":
+        data_dtype = torch.int8
+    elif kv_cache_dtype in QUANTIZED:
+        data_dtype = torch.float8_e4m3fn
+    else:
+        data_dtype = default_dtype
     kv = torch.zeros(2, num_layers, num_blocks, block_size, num_kv_heads, head_dim,
                      dtype=data_dtype, device=device)
     ks = vs = None
     if kv_cache_dtype == "fp8_per_tensor":
         buf = torch.ones(2, num_layers, 1, dtype=torch.float32, device=device)
+        ks, vs = buf[0], buf[1]
+    elif kv_cache_dtype in PER_TOKEN_HEAD:
+        buf = torch.ones(2, num_layers, num_blocks, block_size, num_kv_heads, dtype=torch.float32,
+                         device=device)
         ks, vs = buf[0], buf[1]
     return KVCache(kv, ks, vs, kv_cache_dtype, block_size)
 

@@ -1,6 +1,6 @@
 """Paged-attention decode on the GPU through the C ABI against the CPU oracle
-(token-level restatement of the reference kernel, float64) and, at the BASELINE
-configurations' full sizes, against a float32 torch reference on the GPU.
+(token-level restatement of the reference kernel, float64), the BASELINE
+configurations 3 and 4 at full size included (every sequence).
 
 Tolerances: bf16/fp16 outputs atol 2e-2 / rtol 1e-2 (the BASELINE bar, fp32
 accumulation); fp32 outputs atol 2e-5 / rtol 1e-4."""
@@ -211,18 +211,50 @@ def _decode_w(w, splits=0):
                                        w.head_dim, w.block_size, num_splits=splits)
 
 
+def oracle_over_batch(w, chunk):
+    """The float64 oracle (paged_decode_ref) over every sequence of a workload, `chunk`
+    sequences at a time: each chunk's pages are gathered into a compact CPU cache and
+    its block tables renumbered, so host memory stays bounded at full size."""
+    B, BS = w.query.shape[0], w.block_size
+    out = torch.empty(B, w.num_heads, w.head_dim, dtype=torch.float64)
+    for s in range(0, B, chunk):
+        e = min(B, s + chunk)
+        bt = w.block_tables[s:e]
+        pages = torch.unique(bt[bt >= 0])
+        remap = torch.full((w.k_cache.shape[0],), -1, dtype=torch.int32, device=bt.device)
+        remap[pages.long()] = torch.arange(pages.numel(), dtype=torch.int32, device=bt.device)
+        bt_c = torch.where(bt >= 0, remap[bt.clamp(min=0).long()], bt).cpu()
+        kc, vc = w.k_cache[pages.long()].cpu(), w.v_cache[pages.long()].cpu()
+        ks = w.k_scale.cpu() if w.fp8 else None
+        vs = w.v_scale.cpu() if w.fp8 else None
+        out[s:e] = paged_decode_ref(w.query[s:e].cpu(), kc, vc, bt_c, w.context_lens[s:e].cpu(),
+                                    w.scale, w.num_heads, w.num_kv_heads, w.head_dim, BS,
+                                    k_scale=ks, v_scale=vs)
+    return out
+
+
+def tolerance_margin(got, ref, atol, rtol):
+    """max over elements of |got - ref| / (atol + rtol |ref|): <= 1 passes allclose."""
+    return float(((got.double() - ref).abs() / (atol + rtol * ref.abs())).max())
+
+
 @pytest.mark.parametrize("cfg", ["config3", "config4"])
 def test_full_size_config(cfg):
+    """Configs 3 (bf16, 256 sequences) and 4 (FP8, 64 x 32768 tokens) at full size:
+    every sequence against the float64 oracle, and the whole batch for split-count
+    invariance. Prints the worst error as a fraction of the tolerance."""
     w = getattr(wl, cfg)(seed=1, with_append=False)
     out = _decode_w(w)
     torch.cuda.synchronize()
     assert not torch.isnan(out).any()
-    g = torch.Generator().manual_seed(2)
-    seqs = torch.randperm(w.query.shape[0], generator=g)[:12].tolist()
-    seqs += [int(w.context_lens.argmax()), int(w.context_lens.argmin())]
-    ref = torch_reference(w, seqs)
+    ref = oracle_over_batch(w, 16 if cfg == "config3" else 2)
     atol, rtol = TOL[torch.bfloat16]
-    assert torch.allclose(out[seqs].float(), ref, atol=atol, rtol=rtol)
+    got = out.cpu()
+    margin = tolerance_margin(got, ref, atol, rtol)
+    err = float((got.double() - ref).abs().max())
+    print(f"\nFULL_SIZE_PARITY {cfg}: {w.query.shape[0]} sequences, max |err| {err:.3e}, "
+          f"worst err/tol {margin:.4f} (atol {atol}, rtol {rtol})")
+    assert margin <= 1.0
     # split-count invariance over the whole batch: one split vs the automatic plan
     one = _decode_w(w, splits=1)
     assert torch.allclose(one.float(), out.float(), atol=atol, rtol=rtol)

@@ -51,7 +51,26 @@ def test_allocate_and_bind_kv_cache():
     assert layers[1].k_cache.data_ptr() == cache.kv[0, 1].data_ptr()
     assert float(layers[2].v_scale[0]) == 1.0 and layers[0].kv_cache_dtype == "fp8_per_tensor"
     with pytest.raises(NotImplementedError):
-        kv.allocate_kv_cache(1, 1, 4, 1, 16, "int8_per_token_head", device="cpu")
+        kv.allocate_kv_cache(1, 1, 4, 1, 16, "kivi_4bit", device="cpu")
+
+
+@pytest.mark.parametrize("mode,dtype", [("fp8_per_token_head", torch.float8_e4m3fn),
+                                        ("int8_per_token_head", torch.int8)])
+def test_allocate_per_token_head_scales(mode, dtype):
+    """Per-(token, head) modes: (2, L, NB, BS, KVH) float32 scales at 1.0 beside the 8-bit
+    pages, and layer l's (NB, BS, KVH) views bound to the l-th attention module
+    (model_runner.py:330-338, 376-395)."""
+    attn_mod = mkv_module("layers.attention")
+    layers = torch.nn.ModuleList([attn_mod.Attention(4, 16, num_kv_heads=2, block_size=4)
+                                  for _ in range(3)])
+    cache = kv.allocate_kv_cache(3, 5, 4, 2, 16, mode, device="cpu")
+    assert cache.kv.shape == (2, 3, 5, 4, 2, 16) and cache.kv.dtype == dtype
+    assert cache.k_scale.shape == (3, 5, 4, 2) and cache.k_scale.dtype == torch.float32
+    assert bool((cache.k_scale == 1).all()) and bool((cache.v_scale == 1).all())
+    assert kv.bind_kv_cache(layers.modules(), cache) == 3
+    assert layers[2].k_scale.shape == (5, 4, 2) and layers[2].k_scale.is_contiguous()
+    assert layers[1].v_scale.data_ptr() == cache.v_scale[1].data_ptr()
+    assert layers[0].kv_cache_dtype == mode
 
 
 def test_kv_head_shard_ranges():

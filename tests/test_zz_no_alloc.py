@@ -101,3 +101,63 @@ def test_no_alloc_rejects_shapes_beyond_its_scratch():
                                       torch.cuda.current_stream().cuda_stream)
     assert st == lib_mod.ERR_WORKSPACE
     assert b"built-in scratch" in lib.mkv_last_error()
+
+
+def test_no_alloc_in_a_second_context():
+    """A caller with its own driver-API context (a cgo/JNI host that created the context
+    itself) gets the scratch address of that context, not the one cached for the
+    primary context, and the primary context's calls stay correct afterwards."""
+    drv = pytest.importorskip("cuda.bindings.driver")
+
+    def ok(res):
+        res = res if isinstance(res, tuple) else (res,)
+        assert res[0] == drv.CUresult.CUDA_SUCCESS, res[0]
+        return res[1] if len(res) == 2 else res[1:]
+
+    lib = lib_mod.load()
+    H, KVH, D, BS, splits = 32, 8, 128, 16, 7
+    inputs = paged_inputs(24, H, KVH, D, BS, [1, 2000, 17, 640, 0, 1500] * 4, torch.bfloat16, seed=3)
+    q, kc, vc, bt, cl = inputs
+    ref = decode_with_workspace(lib, inputs, H, KVH, D, BS, splits)
+    first = decode_no_alloc(lib, inputs, H, KVH, D, BS, splits)  # caches the primary's address
+    torch.cuda.synchronize()
+    host = [t.view(torch.uint8).cpu().numpy() if t.dtype != torch.bfloat16 else
+            t.view(torch.int16).cpu().numpy() for t in (q, kc, vc, bt, cl)]
+
+    ok(drv.cuInit(0))
+    dev = ok(drv.cuDeviceGet(torch.cuda.current_device()))
+    ctx = ok(drv.cuCtxCreate(0, dev))  # now current on this thread
+    ptrs = []
+    try:
+        for h in host:
+            p = ok(drv.cuMemAlloc(h.nbytes))
+            ok(drv.cuMemcpyHtoD(p, h.ctypes.data, h.nbytes))
+            ptrs.append(p)
+        out_bytes = q.numel() * 2
+        optr = ok(drv.cuMemAlloc(out_bytes))
+        ptrs.append(optr)
+        dq, dk, dv, dbt, dcl = (int(p) for p in ptrs[:5])
+        results = []
+        for _ in range(2):  # two calls in a row in this context
+            st = lib.mkv_paged_decode_noalloc(
+                dq, q.stride(0), q.stride(1), lib_mod.DTYPE_BF16, dk, dv, lib_mod.DTYPE_BF16,
+                kc.shape[0], BS, dbt, lib_mod.INDEX_I32, bt.stride(0), bt.shape[1], dcl,
+                lib_mod.INDEX_I64, q.shape[0], H, KVH, D, 1.0 / math.sqrt(D), int(optr), q.stride(0),
+                q.stride(1), splits, None, None)
+            assert st == 0, lib.mkv_last_error()
+            ok(drv.cuCtxSynchronize())
+            buf = torch.empty(q.shape, dtype=torch.bfloat16)
+            ok(drv.cuMemcpyDtoH(buf.data_ptr(), optr, out_bytes))
+            results.append(buf)
+    finally:
+        for p in ptrs:
+            drv.cuMemFree(p)
+        drv.cuCtxDestroy(ctx)
+    torch.cuda.set_device(torch.cuda.current_device())
+    again = decode_no_alloc(lib, inputs, H, KVH, D, BS, splits)  # primary context again
+    torch.cuda.synchronize()
+    atol, rtol = TOL[torch.bfloat16]
+    ok_rows = ~torch.isnan(ref.cpu())
+    for got in results + [first.cpu(), again.cpu()]:
+        assert torch.equal(torch.isnan(got), ~ok_rows)
+        assert torch.allclose(got[ok_rows].float(), ref.cpu()[ok_rows].float(), atol=atol, rtol=rtol)
