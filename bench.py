@@ -309,16 +309,19 @@ def decode_step_fns(attn, w, ks, vs):
         else:
             attn.store_kvcache(k, v, w.k_cache, w.v_cache, slots, w.block_size)
 
-    def decode(q=None, bt=None, cl=None):
+    def decode(q=None, bt=None, cl=None, after_append=False):
+        """after_append: the decode directly follows this step's append, so its prologue
+        may overlap it (as Attention.forward runs them)."""
         q = w.query if q is None else q
         bt = w.block_tables if bt is None else bt
         cl = w.context_lens if cl is None else cl
         if fp8:
             return attn.paged_attention_decode_quantized(
                 q, w.k_cache, w.v_cache, ks, vs, bt, cl, w.scale, w.num_heads, w.num_kv_heads,
-                w.head_dim, w.block_size, "fp8_per_tensor")
+                w.head_dim, w.block_size, "fp8_per_tensor", overlap_previous=after_append)
         return attn.paged_attention_decode(q, w.k_cache, w.v_cache, bt, cl, w.scale, w.num_heads,
-                                           w.num_kv_heads, w.head_dim, w.block_size)
+                                           w.num_kv_heads, w.head_dim, w.block_size,
+                                           overlap_previous=after_append)
 
     return append, decode
 
@@ -354,7 +357,7 @@ def measure_e2e(args, w, append, decode, ranks, replay, total_step_bytes):
 
         def device_part():  # append + decode on this slot's device input views
             append(dk, dv, ds)
-            dout[:] = [decode(dq, dbt, dcl)]
+            dout[:] = [decode(dq, dbt, dcl, after_append=True)]
 
         dbuf.copy_(hbuf)
         run = replay(device_part)
@@ -423,7 +426,7 @@ def measure_decode(args, cfg, rank, world, ranks, replay, attn, lib, headline: b
 
     def step():
         append()
-        return decode()
+        return decode(after_append=True)
 
     for _ in range(max(3, args.warmup)):
         step()

@@ -141,6 +141,26 @@ MKV_API int mkv_store_kvcache_fp8(const void* key, const void* value,
                           int32_t dtype, int32_t* invalid_count, void* stream);
 
 /*
+ * The whole of store_kvcache_fp8's per-tensor path in one launch (attention.py:281-333):
+ * the calibration of mkv_calibrate_fp8_scales (315-323) for each scale that still holds
+ * the sentinel 1.0, then the quantising store of mkv_store_kvcache_fp8 (118-191) with
+ * the scales as they then are. Results are bit-identical to those two calls in a row.
+ * In the steady state (both scales calibrated) the kernel reads the scales and stores;
+ * while a scale is the sentinel, every CTA adds its share of the batch's amax into
+ * `calib_work` and the last CTA to finish writes the scale(s) and quantises the batch.
+ * No CTA ever waits for another. `calib_work`: MKV_FP8_CALIB_WORK_BYTES of device
+ * memory, zero before the first call and left zero by every call; calls sharing it
+ * must be ordered on one stream. calib_work = NULL quantises with the scales as they
+ * are (no calibration), like mkv_store_kvcache_fp8 (which takes the same kernel).
+ */
+MKV_API int mkv_store_kvcache_fp8_calibrating(
+    const void* key, const void* value, int64_t key_stride_token, int64_t key_stride_head,
+    int64_t value_stride_token, int64_t value_stride_head, void* k_cache, void* v_cache,
+    float* k_scale, float* v_scale, int64_t num_blocks, int32_t block_size,
+    const void* slot_mapping, int32_t slot_index_type, int64_t num_tokens, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype, void* calib_work, int32_t* invalid_count, void* stream);
+
+/*
  * KV append with a dynamic scale per (token, kv head) row, into an FP8 E4M3 or INT8
  * cache (cache_dtype MKV_DTYPE_FP8_E4M3 or MKV_DTYPE_INT8). Replaces store_kvcache_fp8
  * with kv_cache_dtype "fp8_per_token_head" (attention.py:281-333 with the kernel
@@ -298,6 +318,40 @@ MKV_API size_t mkv_paged_prefill_workspace_bytes(int32_t num_seqs, int64_t total
                                                  int32_t head_dim, int32_t block_size,
                                                  int32_t max_num_blocks, int32_t q_dtype,
                                                  int32_t cache_dtype);
+
+/*
+ * Every decode mode behind one entry point, with launch options. The arguments mean
+ * what they mean for mkv_paged_decode; the cache mode follows from cache_dtype and the
+ * scale pointers: an FP8_E4M3 cache with k_scale/v_scale (one float32 each) is the
+ * per-tensor mode of mkv_paged_decode_fp8; an FP8_E4M3 or INT8 cache with
+ * k_scales/v_scales (num_blocks, block_size, num_kv_heads) is the per-(token, head)
+ * mode of mkv_paged_decode_quant_per_token_head; no scales is mkv_paged_decode.
+ * No reference counterpart (the reference launches one Triton kernel per mode).
+ * flags (bitwise or):
+ *   MKV_DECODE_WORKSPACE_ZEROED  the workspace's arrival counters are already zero, so
+ *       the call skips clearing them (one cudaMemsetAsync). Every decode leaves them at
+ *       zero, so a caller that zeroes its workspace once and keeps it for decodes that
+ *       are ordered on one stream may always pass this flag.
+ *   MKV_DECODE_OVERLAP_PREVIOUS  programmatic dependent launch: the decode may start
+ *       while the previous kernel on the stream still runs. Its prologue (the
+ *       schedule's scan of context_lens, the block-table slice, the query rows) then
+ *       overlaps that kernel, and it reads K/V pages (and per-token scales) only after
+ *       that kernel has completed. Pass it only when that previous kernel writes none of
+ *       query, block_tables and context_lens, e.g. when it is this library's KV append
+ *       of the same step (whose kernels let a dependent start early).
+ */
+#define MKV_DECODE_WORKSPACE_ZEROED 1u
+#define MKV_DECODE_OVERLAP_PREVIOUS 2u
+MKV_API int mkv_paged_decode_ex(
+    const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t cache_dtype, const float* k_scale,
+    const float* v_scale, const float* k_scales, const float* v_scales, int64_t num_blocks,
+    int32_t block_size, const void* block_tables, int32_t block_table_index_type,
+    int64_t block_table_stride_seq, int32_t max_num_blocks, const void* context_lens,
+    int32_t context_lens_index_type, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
+    void* workspace, size_t workspace_bytes, int32_t num_splits, uint32_t flags,
+    int32_t* invalid_count, void* stream);
 
 /*
  * Paged-attention decode that allocates nothing and needs no workspace argument.

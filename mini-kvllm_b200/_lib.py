@@ -18,6 +18,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_FP8_E4M3, DTYPE_INT8 = 0, 1, 2, 3, 4
 INDEX_I32, INDEX_I64 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 FP8_CALIB_WORK_BYTES = 16
+DECODE_WORKSPACE_ZEROED, DECODE_OVERLAP_PREVIOUS = 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
 AR_MAX_RANKS, AR_MAX_BLOCKS, IPC_HANDLE_BYTES = 8, 128, 64
 AR_FLAG_BYTES = AR_MAX_BLOCKS * AR_MAX_RANKS * 4
@@ -36,6 +37,9 @@ SIGNATURES: dict[str, tuple] = {
         _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p, _p, _p, _p]),
     "mkv_store_kvcache_fp8": (ctypes.c_int, [
         _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _i32, _i32, _p, _p]),
+    "mkv_store_kvcache_fp8_calibrating": (ctypes.c_int, [
+        _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _i32, _i32, _p, _p,
+        _p]),
     "mkv_store_kvcache_quant_per_token_head": (ctypes.c_int, [
         _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _i32,
         _i32, _p, _p]),
@@ -47,6 +51,9 @@ SIGNATURES: dict[str, tuple] = {
     "mkv_paged_decode_noalloc": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
+    "mkv_paged_decode_ex": (ctypes.c_int, [
+        _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
+        _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, ctypes.c_uint32, _p, _p]),
     "mkv_paged_decode_quant_per_token_head": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),

@@ -20,6 +20,17 @@ void clear_error();
 // Maps a CUDA error to MKV_ERR_CUDA with a message naming `what`.
 int cuda_status(cudaError_t err, const char* what);
 
+// ---------------------------------------------------------------- per-context state
+// Kernel attributes and module symbols belong to a CUDA context, not to a device: a
+// caller may make its own driver-API context current, and cudaDeviceReset replaces the
+// primary context. Anything cached across calls is therefore keyed on the current
+// context's unique ID (cuCtxGetId; IDs are never reused within a process).
+// *id = 0 when no context is current on the calling thread.
+int current_context_id(unsigned long long* id);
+// cudaFuncSetAttribute(func, MaxDynamicSharedMemorySize, bytes), once per (kernel,
+// context, size); a no-op for bytes <= 48 KB.
+int ensure_dynamic_smem(const void* func, int bytes, const char* what);
+
 // ---------------------------------------------------------------- element types
 using bf16 = __nv_bfloat16;
 using f16 = __half;
@@ -92,6 +103,15 @@ __device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& h01, uin
 template <typename I> __device__ __forceinline__ int64_t load_index(const I* p, int64_t i) {
   return (int64_t)__ldg(p + i);
 }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while the previous
+// kernel on its stream still runs; pdl_wait() returns once that kernel has completed and
+// its memory operations are visible (at once when the launch had no such dependency).
+// pdl_trigger() lets the next kernel launch as soon as every CTA of this one has issued
+// it; without it the next kernel starts when this one ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // ---------------------------------------------------------------- memory ops
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {

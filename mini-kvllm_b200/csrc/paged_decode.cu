@@ -35,7 +35,6 @@
 //     num_splits > 0 instead splits every unit into fixed token chunks (flash-decoding)
 //     with the same epilogue. Nothing on the host depends on device data (graph-safe).
 // A CUDA-core kernel with the same tiling and epilogue covers fp32 and other head dims.
-#include <cuda.h>
 #include <mutex>
 #include <type_traits>
 
@@ -93,6 +92,7 @@ struct DecodeParams {
   int unit_cost;  // balanced: items charged per unit before its tiles (segment overhead)
   int q_vec16;  // query rows start on 16-byte boundaries (base and both strides)
   int32_t* invalid;
+  int pdl;  // host only: launch with programmatic stream serialization
 };
 
 __device__ __forceinline__ int64_t load_ctx(const DecodeParams& p, int seq) {
@@ -749,6 +749,7 @@ paged_decode_generic_kernel(const DecodeParams p) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __shared__ SchedState sched;
   sched_init<kGenTile>(p, sched);
+  pdl_wait();  // pages may have been written by the kernel this launch overlaps
   while (sched_next<kGenTile>(p, sched)) {
   const TokRange rng{sched.cur.begin, sched.cur.end};
   const int seq = sched.cur.seq;
@@ -1029,6 +1030,10 @@ paged_decode_tc_kernel(const DecodeParams p) {
   if (!prefetched) {
     load_q_rows<QT>(p, seq, h0, nh, q_s);
     cp_async_commit();
+    // Everything above (schedule scan, block-table slice, query rows) may overlap the
+    // previous kernel of a programmatic launch; the pages it may have written are read
+    // only after it has completed.
+    pdl_wait();
 #pragma unroll
     for (int s = 0; s < STAGES - 1; ++s) {
       if (s < ntiles) load_tile(s);
@@ -1529,6 +1534,10 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
   if (!prefetched) {
     load_q_rows<QT>(p, seq, h0, nh, q_s);
     cp_async_commit();
+    // Everything above (schedule scan, block-table slice, query rows) may overlap the
+    // previous kernel of a programmatic launch; the pages it may have written are read
+    // only after it has completed.
+    pdl_wait();
 #pragma unroll
     for (int s = 0; s < STAGES - 1; ++s) {
       if (s < ntiles) load_tile(s);
@@ -1930,18 +1939,12 @@ WorkspaceLayout workspace_layout(int num_seqs, int num_heads, int num_kv_heads, 
   return w;
 }
 
-// One cudaFuncSetAttribute per kernel instantiation and device.
+// The kernel's dynamic shared memory opt-in, once per kernel and CUDA context.
 template <auto Kernel>
 int ensure_smem(size_t bytes, int device) {
-  static unsigned long long configured = 0;  // bit per device id < 64
-  if (bytes <= 48 * 1024) return MKV_OK;
-  const unsigned long long bit = device < 64 ? (1ull << device) : 0ull;
-  if (bit && (__atomic_load_n(&configured, __ATOMIC_RELAXED) & bit)) return MKV_OK;
-  cudaError_t e =
-      cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(max dynamic smem)");
-  if (bit) __atomic_fetch_or(&configured, bit, __ATOMIC_RELAXED);
-  return MKV_OK;
+  (void)device;
+  return ensure_dynamic_smem((const void*)Kernel, (int)bytes,
+                             "cudaFuncSetAttribute(max dynamic smem)");
 }
 
 // Resident CTAs of Kernel at `smem` bytes on `device` (occupancy x SMs), cached per device.
@@ -1990,6 +1993,19 @@ int launch_decode(DecodeParams p, int tile, size_t smem, cudaStream_t stream, in
     p.min_tiles = min_tiles_for(tile, p.block_size, p.max_blocks);
     p.unit_cost = tile == kGenTile ? 0 : kUnitCost;
     grid = dim3(g, 1, 1);
+  }
+  if (p.pdl) {  // may start while the previous kernel of the stream still runs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, Kernel, p), what);
   }
   Kernel<<<grid, kThreads, smem, stream>>>(p);
   return cuda_status(cudaGetLastError(), what);
@@ -2066,8 +2082,10 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
                 int bt_type, int64_t bt_sb, int max_blocks, const void* ctx, int ctx_type,
                 int num_seqs, int num_heads, int num_kv_heads, int head_dim, float scale,
                 void* out, int64_t o_sb, int64_t o_sh, void* workspace, size_t ws_bytes,
-                int num_splits, int32_t* invalid, void* stream) {
+                int num_splits, unsigned flags, int32_t* invalid, void* stream) {
   clear_error();
+  if (flags & ~(unsigned)(MKV_DECODE_WORKSPACE_ZEROED | MKV_DECODE_OVERLAP_PREVIOUS))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", fn, flags);
   if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
       max_blocks < 0 || num_blocks < 0 || num_splits < 0)
     return set_error(MKV_ERR_INVALID_ARGUMENT,
@@ -2179,12 +2197,15 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   p.part_ml = wl.total ? (float*)(ws + wl.ml) : nullptr;
   p.arrivals = wl.total ? (unsigned int*)(ws + wl.ctr) : nullptr;
   p.invalid = invalid;
+  p.pdl = (flags & MKV_DECODE_OVERLAP_PREVIOUS) ? 1 : 0;
 
   int device = 0;
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
   cudaStream_t s = (cudaStream_t)stream;
-  if (wl.total) {  // arrival counters start at zero (the kernel leaves them at zero)
+  // Arrival counters start at zero. The kernel leaves them at zero, so a caller that
+  // keeps one workspace (zeroed once) for its decodes can skip this clear.
+  if (wl.total && !(flags & MKV_DECODE_WORKSPACE_ZEROED)) {
     e = cudaMemsetAsync(ws + wl.ctr, 0, wl.total - wl.ctr, s);
     if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(arrival counters)");
   }
@@ -2233,14 +2254,9 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[MKV_NOALLOC_SCR
 
 // The address belongs to the CUDA context that was current when it was looked up (the
 // module is loaded per context). It is cached per context, keyed on the context's
-// unique ID from cuCtxGetId, which is never reused within a process: a caller's own
-// driver-API context, or the primary context created again after cudaDeviceReset, gets
-// a lookup of its own instead of an address from another or a destroyed context. The
-// two driver calls are resolved through cudaGetDriverEntryPoint, so the library needs
-// no link against libcuda.
-typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
-typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
-
+// unique ID (current_context_id): a caller's own driver-API context, or the primary
+// context created again after cudaDeviceReset, gets a lookup of its own instead of an
+// address from another or a destroyed context.
 struct NoallocEntry {
   unsigned long long ctx_id;
   void* ptr;
@@ -2249,51 +2265,15 @@ constexpr int kNoallocCacheEntries = 64;
 std::mutex g_noalloc_mu;
 NoallocEntry g_noalloc_cache[kNoallocCacheEntries] = {};
 int g_noalloc_next = 0;  // round-robin replacement once the cache is full
-CtxGetCurrentFn g_ctx_get_current = nullptr;
-CtxGetIdFn g_ctx_get_id = nullptr;
-
-int resolve_ctx_calls() {  // called with g_noalloc_mu held
-  if (g_ctx_get_current && g_ctx_get_id) return MKV_OK;
-  void* f1 = nullptr;
-  void* f2 = nullptr;
-  cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = q1;
-  cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1);
-  if (e != cudaSuccess || q1 != cudaDriverEntryPointSuccess || !f1)
-    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetCurrent is unavailable");
-  e = cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2);
-  if (e != cudaSuccess || q2 != cudaDriverEntryPointSuccess || !f2)
-    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetId is unavailable");
-  g_ctx_get_current = (CtxGetCurrentFn)f1;
-  g_ctx_get_id = (CtxGetIdFn)f2;
-  return MKV_OK;
-}
-
-// The current context's ID; *none = true (and MKV_OK) when no context is current yet.
-int current_ctx_id(unsigned long long* id, bool* none) {  // called with g_noalloc_mu held
-  CUcontext ctx = nullptr;
-  *none = false;
-  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS)
-    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetCurrent failed");
-  if (ctx == nullptr) {
-    *none = true;
-    return MKV_OK;
-  }
-  if (g_ctx_get_id(ctx, id) != CUDA_SUCCESS)
-    return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: cuCtxGetId failed");
-  return MKV_OK;
-}
 
 // Device address of g_noalloc_scratch in the current context, looked up on the first
 // call in that context.
 int noalloc_scratch(void** out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  int st = resolve_ctx_calls();
-  if (st != MKV_OK) return st;
   unsigned long long id = 0;
-  bool none = false;
-  st = current_ctx_id(&id, &none);
+  int st = current_context_id(&id);
   if (st != MKV_OK) return st;
-  if (!none) {
+  if (id != 0) {
     for (const NoallocEntry& en : g_noalloc_cache)
       if (en.ptr != nullptr && en.ctx_id == id) {
         *out = en.ptr;
@@ -2305,10 +2285,10 @@ int noalloc_scratch(void** out) {
   void* ptr = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(built-in decode scratch)");
-  if (none) {
-    st = current_ctx_id(&id, &none);
+  if (id == 0) {
+    st = current_context_id(&id);
     if (st != MKV_OK) return st;
-    if (none) return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: no current CUDA context");
+    if (id == 0) return set_error(MKV_ERR_CUDA, "mkv_paged_decode_noalloc: no current CUDA context");
   }
   g_noalloc_cache[g_noalloc_next] = NoallocEntry{id, ptr};
   g_noalloc_next = (g_noalloc_next + 1) % kNoallocCacheEntries;
@@ -2366,7 +2346,7 @@ extern "C" int mkv_paged_decode(const void* query, int64_t q_stride_seq, int64_t
                      block_size, block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks, context_lens,
                      context_lens_index_type, num_seqs, num_heads, num_kv_heads, head_dim, scale,
                      out, out_stride_seq, out_stride_head, workspace, workspace_bytes, num_splits,
-                     invalid_count, stream);
+                     0u, invalid_count, stream);
 }
 
 extern "C" int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq,
@@ -2386,7 +2366,7 @@ extern "C" int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq,
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
-                     workspace_bytes, num_splits, invalid_count, stream);
+                     workspace_bytes, num_splits, 0u, invalid_count, stream);
 }
 
 extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
@@ -2425,8 +2405,8 @@ extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, scratch,
-                     scratch ? (size_t)MKV_NOALLOC_SCRATCH_BYTES : 0, num_splits, invalid_count,
-                     stream);
+                     scratch ? (size_t)MKV_NOALLOC_SCRATCH_BYTES : 0, num_splits, 0u,
+                     invalid_count, stream);
 }
 
 extern "C" int mkv_paged_decode_quant_per_token_head(
@@ -2450,5 +2430,34 @@ extern "C" int mkv_paged_decode_quant_per_token_head(
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
-                     workspace_bytes, num_splits, invalid_count, stream);
+                     workspace_bytes, num_splits, 0u, invalid_count, stream);
+}
+
+extern "C" int mkv_paged_decode_ex(
+    const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t cache_dtype, const float* k_scale,
+    const float* v_scale, const float* k_scales, const float* v_scales, int64_t num_blocks,
+    int32_t block_size, const void* block_tables, int32_t block_table_index_type,
+    int64_t block_table_stride_seq, int32_t max_num_blocks, const void* context_lens,
+    int32_t context_lens_index_type, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
+    void* workspace, size_t workspace_bytes, int32_t num_splits, uint32_t flags,
+    int32_t* invalid_count, void* stream) {
+  const char* fn = "mkv_paged_decode_ex";
+  clear_error();
+  const bool per_token = k_scales != nullptr || v_scales != nullptr;
+  if (per_token && (k_scale != nullptr || v_scale != nullptr))
+    return set_error(MKV_ERR_INVALID_ARGUMENT,
+                     "%s: give either per-tensor scales or per-(token, head) scales", fn);
+  if (per_token && cache_dtype != MKV_DTYPE_FP8_E4M3 && cache_dtype != MKV_DTYPE_INT8)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: per-token scales need an FP8_E4M3 or INT8 cache", fn);
+  if (!per_token && cache_dtype != MKV_DTYPE_FP8_E4M3 && (k_scale != nullptr || v_scale != nullptr))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: scales given for an unquantised cache", fn);
+  return decode_impl(fn, query, q_stride_seq, q_stride_head, q_dtype, k_cache, v_cache,
+                     cache_dtype, per_token ? nullptr : k_scale, per_token ? nullptr : v_scale,
+                     k_scales, v_scales, num_blocks, block_size, block_tables,
+                     block_table_index_type, block_table_stride_seq, max_num_blocks, context_lens,
+                     context_lens_index_type, num_seqs, num_heads, num_kv_heads, head_dim, scale,
+                     out, out_stride_seq, out_stride_head, workspace, workspace_bytes, num_splits,
+                     flags, invalid_count, stream);
 }

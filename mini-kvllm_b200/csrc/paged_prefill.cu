@@ -1244,14 +1244,10 @@ int launch_prefill_tc05(const PrefillParams& p, int cache_dtype, cudaStream_t st
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(MKV_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc05_kernel<QT, NQ, CT, kTok, kSplit>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::BYTES);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill tc05 smem)");
-    configured[dev] = true;
+  {  // the shared-memory opt-in, once per kernel and CUDA context
+    const int st = ensure_dynamic_smem((const void*)paged_prefill_tc05_kernel<QT, NQ, CT, kTok, kSplit>,
+                                       (int)L::BYTES, "cudaFuncSetAttribute(prefill tc05 smem)");
+    if (st != MKV_OK) return st;
   }
   PrefillParams q = p;
   q.qb = NQ * pf05::kRows / p.group;  // query tokens per CTA: 128 NQ rows
@@ -1466,14 +1462,10 @@ paged_prefill_generic_kernel(const PrefillParams p) {
 template <typename QT, typename CT, int D>
 int launch_prefill_tc(const PrefillParams& p, int64_t units, cudaStream_t stream) {
   constexpr size_t smem = pf_smem_bytes<CT, D>();
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (smem > 48 * 1024 && dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(paged_prefill_tc_kernel<QT, CT, D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(prefill smem)");
-    configured[dev] = true;
+  {  // the shared-memory opt-in, once per kernel and CUDA context
+    const int st = ensure_dynamic_smem((const void*)paged_prefill_tc_kernel<QT, CT, D>, (int)smem,
+                                       "cudaFuncSetAttribute(prefill smem)");
+    if (st != MKV_OK) return st;
   }
   dim3 grid((unsigned)units, p.num_kv_heads, 1);
   paged_prefill_tc_kernel<QT, CT, D><<<grid, kPThreads, smem, stream>>>(p);

@@ -10,10 +10,15 @@
 //   store_kvcache_int8_kernel  attention.py:195-252 scale = max(amax / 127, 1e-6), round half away
 //
 // B200 design: the append is pure HBM traffic (one read of the new rows, one write
-// into the pages). Each thread moves one 16-byte chunk of a (token, head) row for
-// both K and V with a streaming vector load and a vector store; a token's row of
-// all heads is contiguous in both the source and the page, so each warp touches
-// whole 128-byte lines. The grid is sized in multiples of the SM count.
+// into the pages) over a few MB, so it is bound by how many bytes are in flight and by
+// the launch itself. Each thread owns CHUNKS 16-byte chunks of K and of V (or 16-element
+// groups for the quantisers), issues every load of them before its first store, and
+// the chunk index advances by the grid's thread count, so each warp instruction touches
+// whole 128-byte lines. One wave of CTAs then holds the whole batch in flight. A
+// token's row of all heads is contiguous in both the source and the page.
+// The FP8 per-tensor store reads the scale itself and calibrates it in the same launch
+// while it still holds the 1.0 sentinel (the last CTA to finish the amax reduction
+// quantises the batch), so a calibrated step is one launch.
 #include <cstdio>
 
 #include "mkv_common.cuh"
@@ -31,8 +36,64 @@ inline int grid_for(int64_t work_items, int threads) {
   return (int)blocks;
 }
 
+// Items per thread: as many as keep at least two CTAs of work per SM, up to 4 (one wave
+// then holds a config-2 batch of 4096 tokens entirely in flight); small batches (a
+// decode step's few hundred tokens) spread one item per thread over more SMs.
+inline int per_thread_items(int64_t items) {
+  const int64_t min_threads = (int64_t)kNumSMs * 2 * kStoreThreads;
+  if (items >= 4 * min_threads) return 4;
+  if (items >= 2 * min_threads) return 2;
+  return 1;
+}
+
 // -------------------------------------------------------------------- same-dtype copy
-// One thread per 16-byte chunk of a (token, head) row, for K and V.
+// CHUNKS 16-byte chunks of K and of V per thread, strided by the grid's thread count:
+// all 2 * CHUNKS loads (and the slot loads) are in flight before the first store.
+// Indices are 32-bit (the host takes this kernel only below 2^31 chunks).
+template <typename SlotT, int CHUNKS>
+__global__ void __launch_bounds__(kStoreThreads)
+store_kv_copy_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
+                     int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
+                     uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
+                     const SlotT* __restrict__ slots, int64_t num_slots, uint32_t total,
+                     uint32_t num_heads, uint32_t row_chunks, int32_t* invalid) {
+  pdl_trigger();  // a dependent decode may begin its prologue now
+  const uint32_t per_token = num_heads * row_chunks;
+  const uint32_t nthreads = gridDim.x * blockDim.x;
+  for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < total;
+       base += nthreads * CHUNKS) {
+    uint4 kv[CHUNKS], vv[CHUNKS];
+    int64_t dst[CHUNKS];
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+      const uint32_t i = base + (uint32_t)j * nthreads;
+      dst[j] = -1;
+      if (i < total) {
+        const uint32_t t = i / per_token;
+        const uint32_t rem = i - t * per_token;
+        const uint32_t h = rem / row_chunks;
+        const uint32_t c = rem - h * row_chunks;
+        const int64_t slot = load_index(slots, (int64_t)t);
+        kv[j] = ld_stream_v4(key + (int64_t)t * k_st + (int64_t)h * k_sh + c * 16u);
+        vv[j] = ld_stream_v4(value + (int64_t)t * v_st + (int64_t)h * v_sh + c * 16u);
+        if (slot >= 0 && slot < num_slots) {
+          dst[j] = ((slot * num_heads + h) * row_chunks + c) * 16;
+        } else if (slot >= num_slots && rem == 0 && invalid != nullptr) {
+          atomicAdd(invalid, 1);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+      if (dst[j] >= 0) {
+        st_v4(k_cache + dst[j], kv[j]);
+        st_v4(v_cache + dst[j], vv[j]);
+      }
+    }
+  }
+}
+
+// One thread per 16-byte chunk of a (token, head) row, for K and V (beyond 2^31 chunks).
 template <typename SlotT>
 __global__ void __launch_bounds__(kStoreThreads)
 store_kv_vec16_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
@@ -40,6 +101,7 @@ store_kv_vec16_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict
                       uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
                       const SlotT* __restrict__ slots, int64_t num_slots, int64_t num_tokens,
                       int num_heads, int row_chunks, int32_t* invalid) {
+  pdl_trigger();  // a dependent decode may begin its prologue now
   const int64_t per_token = (int64_t)num_heads * row_chunks;
   const int64_t total = num_tokens * per_token;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -70,6 +132,7 @@ store_kv_scalar_kernel(const T* __restrict__ key, const T* __restrict__ value, i
                        T* __restrict__ k_cache, T* __restrict__ v_cache,
                        const SlotT* __restrict__ slots, int64_t num_slots, int64_t num_tokens,
                        int num_heads, int head_dim, int32_t* invalid) {
+  pdl_trigger();  // a dependent decode may begin its prologue now
   const int64_t per_token = (int64_t)num_heads * head_dim;
   const int64_t total = num_tokens * per_token;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -130,6 +193,7 @@ store_kv_fp8_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
                     const float* __restrict__ k_scale, const float* __restrict__ v_scale,
                     const SlotT* __restrict__ slots, int64_t num_slots, int64_t num_tokens,
                     int num_heads, int groups_per_row, bool vec, int32_t* invalid) {
+  pdl_trigger();  // a dependent decode may begin its prologue now
   const float ks = __ldg(k_scale);
   const float vs = __ldg(v_scale);
   const int64_t per_token = (int64_t)num_heads * groups_per_row;
@@ -173,6 +237,287 @@ store_kv_fp8_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
   }
 }
 
+// The scale torch computes for `x.abs().amax().clamp(min=1e-8) / 448.0` on a CUDA
+// tensor of dtype T: clamp's bound is first converted to T, and division by a
+// Python (CPU) scalar is a multiplication by the fp32 reciprocal; the result is
+// rounded to T, and `.item()` + `fill_` store it exactly in the fp32 scale.
+template <typename T> __device__ __forceinline__ float torch_fp8_scale(float amax) {
+  const float lower = round_through<T>(1e-8f);
+  const float a = isnan(amax) ? amax : fmaxf(amax, lower);
+  const float inv448 = 1.0f / 448.0f;
+  return round_through<T>(a * inv448);
+}
+
+struct CalibWork {  // MKV_FP8_CALIB_WORK_BYTES bytes, zero between calls
+  unsigned int amax_bits[2];
+  unsigned int arrived[2];
+};
+static_assert(sizeof(CalibWork) == MKV_FP8_CALIB_WORK_BYTES, "calibration work layout");
+
+// Two clamped quotients (finite, within +-448) as e4m3 bytes, element `lo` in the low
+// byte: one saturating round-to-nearest-even conversion for the pair.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return (uint32_t)r;
+}
+
+__device__ __forceinline__ float clamp_quotient(float x, float scale) {
+  return fminf(fmaxf(x / scale, -448.0f), 448.0f);  // NaN -> -448, as quantize_e4m3
+}
+
+// 16 elements quantised with one scale, packed as 16 e4m3 bytes (element 0 lowest).
+__device__ __forceinline__ uint4 quantize16(const float (&x)[16], float scale) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = e4m3x2(clamp_quotient(x[4 * i], scale), clamp_quotient(x[4 * i + 1], scale)) |
+           (e4m3x2(clamp_quotient(x[4 * i + 2], scale), clamp_quotient(x[4 * i + 3], scale)) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The 16-element group of a (token, head) row as raw 16-byte words, converted to float
+// only after every load of the thread is in flight.
+template <typename T> struct Raw16 {
+  static constexpr int kWords = 16 * (int)sizeof(T) / 16;
+  uint4 w[kWords];
+  __device__ __forceinline__ void load(const uint8_t* p) {
+#pragma unroll
+    for (int j = 0; j < kWords; ++j) w[j] = ld_stream_v4(p + 16 * j);
+  }
+  __device__ __forceinline__ float at(int j) const { return to_f32(reinterpret_cast<const T*>(w)[j]); }
+  __device__ __forceinline__ void get(float (&x)[16]) const {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = at(j);
+  }
+  // the 16 elements quantised with one scale as 16 e4m3 bytes, converted pair by pair
+  __device__ __forceinline__ uint4 quantize(float scale) const {
+    uint32_t q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      q[i] = e4m3x2(clamp_quotient(at(4 * i), scale), clamp_quotient(at(4 * i + 1), scale)) |
+             (e4m3x2(clamp_quotient(at(4 * i + 2), scale), clamp_quotient(at(4 * i + 3), scale)) << 16);
+    return make_uint4(q[0], q[1], q[2], q[3]);
+  }
+};
+
+__device__ __forceinline__ float amax_step(float m, float a) {  // NaN wins, as torch.amax
+  return (a > m || isnan(a)) ? a : m;
+}
+
+// FP8 per-tensor append in one launch, calibrating a scale that still holds the 1.0
+// sentinel (attention.py:315-323) before quantising with it (118-191). Each thread owns
+// GROUPS 16-element groups of K and of V, strided by the grid's thread count; their
+// loads and the two scale loads are all issued before anything is computed.
+//   Steady state (both scales calibrated, or work == nullptr): quantise and store.
+//   Calibration (a sentinel seen; every CTA reads the scales before any CTA can write
+//   them, so all agree): each CTA folds |x| of its share of the batch into
+//   work->amax_bits with atomicMax on the IEEE bits and stores nothing; the last CTA to
+//   arrive writes the scale(s), leaves the work words at zero, and quantises and stores
+//   the whole batch itself. No CTA waits for another, so the launch can neither hang nor
+//   depend on how many CTAs are resident; the single-CTA store is paid once per layer.
+// The vector form needs 16-byte aligned rows and strides (kVec); otherwise GROUPS = 1
+// and elements are loaded one by one.
+template <typename T, typename SlotT, int GROUPS, bool kVec>
+__global__ void __launch_bounds__(kStoreThreads)
+store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
+                          int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
+                          uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
+                          float* k_scale, float* v_scale, const SlotT* __restrict__ slots,
+                          int64_t num_slots, uint32_t total, uint32_t num_heads,
+                          uint32_t groups_per_row, CalibWork* work, int32_t* invalid) {
+  pdl_trigger();  // a dependent decode may begin its prologue now
+  const uint32_t per_token = num_heads * groups_per_row;
+  const uint32_t nthreads = gridDim.x * blockDim.x;
+  const uint32_t tid0 = blockIdx.x * blockDim.x + threadIdx.x;
+  constexpr int64_t kGroupBytes = 16 * (int64_t)sizeof(T);
+
+  struct Item {
+    int64_t slot;
+    uint32_t t, h, g;
+  };
+  auto locate = [&](uint32_t i, Item& it) {
+    it.t = i / per_token;
+    const uint32_t rem = i - it.t * per_token;
+    it.h = rem / groups_per_row;
+    it.g = rem - it.h * groups_per_row;
+    it.slot = load_index(slots, (int64_t)it.t);
+  };
+  auto src_k = [&](const Item& it) { return key + (int64_t)it.t * k_st + (int64_t)it.h * k_sh + it.g * kGroupBytes; };
+  auto src_v = [&](const Item& it) { return value + (int64_t)it.t * v_st + (int64_t)it.h * v_sh + it.g * kGroupBytes; };
+  auto load_vals = [&](const uint8_t* p, float (&x)[16]) {  // scalar form (kVec false)
+    const T* e = reinterpret_cast<const T*>(p);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x[j] = to_f32(e[j]);
+  };
+  // quantise + store one group whose values are in xk / xv
+  auto store_group = [&](const Item& it, const float (&xk)[16], const float (&xv)[16], float ks,
+                         float vs, bool count_invalid) {
+    if (it.slot < 0) return;  // -1: nothing to store for this token
+    if (it.slot >= num_slots) {
+      if (count_invalid && it.h == 0 && it.g == 0 && invalid != nullptr) atomicAdd(invalid, 1);
+      return;
+    }
+    const int64_t dst = ((it.slot * num_heads + it.h) * groups_per_row + it.g) * 16;
+    st_v4(k_cache + dst, quantize16(xk, ks));
+    st_v4(v_cache + dst, quantize16(xv, vs));
+  };
+
+  // Destination of a group (-1: nothing to store), counting out-of-range slots once per
+  // token.
+  auto dest = [&](const Item& it) -> int64_t {
+    if (it.slot < 0) return -1;
+    if (it.slot >= num_slots) {
+      if (it.h == 0 && it.g == 0 && invalid != nullptr) atomicAdd(invalid, 1);
+      return -1;
+    }
+    return ((it.slot * num_heads + it.h) * groups_per_row + it.g) * 16;
+  };
+
+  // ---- first stride of groups: loads, then the scales, all in flight together
+  int64_t dst[GROUPS];
+  uint32_t base = tid0;
+  Raw16<T> rk[kVec ? GROUPS : 1], rv[kVec ? GROUPS : 1];
+  Item it1;  // the scalar form's group (GROUPS == 1)
+  auto load_stride = [&]() {
+#pragma unroll
+    for (int j = 0; j < GROUPS; ++j) {
+      const uint32_t i = base + (uint32_t)j * nthreads;
+      dst[j] = -1;
+      if (i < total) {
+        Item it;
+        locate(i, it);
+        if constexpr (kVec) {
+          rk[j].load(src_k(it));
+          rv[j].load(src_v(it));
+        } else {
+          it1 = it;
+        }
+        dst[j] = dest(it);
+      }
+    }
+  };
+  load_stride();
+  const float ks = *reinterpret_cast<volatile const float*>(k_scale);
+  const float vs = *reinterpret_cast<volatile const float*>(v_scale);
+  const bool need_k = work != nullptr && ks == 1.0f;
+  const bool need_v = work != nullptr && vs == 1.0f;
+
+  if (!need_k && !need_v) {  // ------------------------------------ steady state
+    while (true) {
+#pragma unroll
+      for (int j = 0; j < GROUPS; ++j) {
+        if (dst[j] < 0) continue;
+        if constexpr (kVec) {
+          st_v4(k_cache + dst[j], rk[j].quantize(ks));
+          st_v4(v_cache + dst[j], rv[j].quantize(vs));
+        } else {
+          float xk[16], xv[16];
+          load_vals(src_k(it1), xk);
+          load_vals(src_v(it1), xv);
+          store_group(it1, xk, xv, ks, vs, false);
+        }
+      }
+      base += nthreads * GROUPS;
+      if (base >= total) break;
+      load_stride();
+    }
+    return;
+  }
+
+  // ---------------------------------------------------------------- calibration
+  // amax of this thread's share of the whole batch (every token, slot -1 included, as
+  // the reference takes key.abs().amax() over the batch)
+  float mk = 0.0f, mv = 0.0f;
+  for (uint32_t i = tid0; i < total; i += nthreads) {
+    Item c;
+    c.t = i / per_token;
+    const uint32_t rem = i - c.t * per_token;
+    c.h = rem / groups_per_row;
+    c.g = rem - c.h * groups_per_row;
+    float xk[16], xv[16];
+    if constexpr (kVec) {
+      Raw16<T> a, b;
+      a.load(src_k(c));
+      b.load(src_v(c));
+      a.get(xk);
+      b.get(xv);
+    } else {
+      load_vals(src_k(c), xk);
+      load_vals(src_v(c), xv);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      mk = amax_step(mk, fabsf(xk[j]));
+      mv = amax_step(mv, fabsf(xv[j]));
+    }
+  }
+  unsigned int bk = __float_as_uint(mk), bv = __float_as_uint(mv);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    bk = max(bk, __shfl_xor_sync(0xffffffffu, bk, o));
+    bv = max(bv, __shfl_xor_sync(0xffffffffu, bv, o));
+  }
+  __shared__ unsigned int wk[kStoreThreads / 32], wv[kStoreThreads / 32];
+  __shared__ bool is_last;
+  __shared__ float new_scale[2];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+    wk[wid] = bk;
+    wv[wid] = bv;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int a = 0, b = 0;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) {
+      a = max(a, wk[w]);
+      b = max(b, wv[w]);
+    }
+    if (need_k) atomicMax(&work->amax_bits[0], a);
+    if (need_v) atomicMax(&work->amax_bits[1], b);
+    __threadfence();
+    const unsigned int prev = atomicAdd(&work->arrived[0], 1u);
+    is_last = (prev == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int fk = atomicExch(&work->amax_bits[0], 0u);
+    const unsigned int fv = atomicExch(&work->amax_bits[1], 0u);
+    atomicExch(&work->arrived[0], 0u);
+    float sk = ks, sv = vs;
+    if (need_k) {
+      sk = torch_fp8_scale<T>(__uint_as_float(fk));
+      *k_scale = sk;
+    }
+    if (need_v) {
+      sv = torch_fp8_scale<T>(__uint_as_float(fv));
+      *v_scale = sv;
+    }
+    new_scale[0] = sk;
+    new_scale[1] = sv;
+  }
+  __syncthreads();
+  const float sk = new_scale[0], sv = new_scale[1];
+  for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {  // this CTA stores the batch
+    Item c;
+    locate(i, c);
+    float xk[16], xv[16];
+    if constexpr (kVec) {
+      Raw16<T> a, b;
+      a.load(src_k(c));
+      b.load(src_v(c));
+      a.get(xk);
+      b.get(xv);
+    } else {
+      load_vals(src_k(c), xk);
+      load_vals(src_v(c), xv);
+    }
+    store_group(c, xk, xv, sk, sv, true);
+  }
+}
+
 // -------------------------------------------------------------------- per-(token, head) scales
 // clamp(round-half-away(x * (1 / scale)), -128, 127) as int8: the product and the +-0.5
 // are separately rounded (no fused multiply-add), as the reference computes them.
@@ -197,6 +542,7 @@ store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
                     const SlotT* __restrict__ slots, int64_t num_slots, int64_t num_tokens,
                     int num_heads, int groups_per_row, int lpr_shift, bool vec,
                     int32_t* invalid) {
+  pdl_trigger();  // a dependent decode may begin its prologue now
   const int lpr = 1 << lpr_shift;
   const int lane = threadIdx.x & 31;
   const int sub = lane & (lpr - 1);
@@ -217,14 +563,28 @@ store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
     const bool has = ok && sub < groups_per_row;
     const int64_t src_off = (int64_t)sub * 16 * (int64_t)sizeof(T);
     const int64_t dst = ((slot * num_heads + h) * groups_per_row + sub) * 16;
+    // K and V of the lane's 16 elements: all loads in flight before either reduction
+    float xs[2][16];
+    if (has) {
+      const uint8_t* pk = key + t * k_st + h * k_sh + src_off;
+      const uint8_t* pv = value + t * v_st + h * v_sh + src_off;
+      if (vec) {
+        Raw16<T> a, b;
+        a.load(pk);
+        b.load(pv);
+        a.get(xs[0]);
+        b.get(xs[1]);
+      } else {
+        load16<T>(pk, false, xs[0]);
+        load16<T>(pv, false, xs[1]);
+      }
+    }
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
-      const uint8_t* src = which == 0 ? key + t * k_st + h * k_sh : value + t * v_st + h * v_sh;
-      float x[16];
+      const float (&x)[16] = xs[which];
       float amax = 0.0f;
       int nan = 0;
       if (has) {
-        load16<T>(src + src_off, vec, x);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const float a = fabsf(x[j]);
@@ -243,25 +603,21 @@ store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
         scale = (!nan && amax > 0.0f) ? amax / 448.0f : 1.0f;
       }
       if (has) {
-        uint32_t packed[4];
+        uint4 packed;
         if (kInt8) {
           const float inv = 1.0f / scale;
+          uint32_t w[4];
 #pragma unroll
-          for (int w = 0; w < 4; ++w)
-            packed[w] = (uint32_t)(uint8_t)quantize_int8(x[4 * w + 0], inv) |
-                        ((uint32_t)(uint8_t)quantize_int8(x[4 * w + 1], inv) << 8) |
-                        ((uint32_t)(uint8_t)quantize_int8(x[4 * w + 2], inv) << 16) |
-                        ((uint32_t)(uint8_t)quantize_int8(x[4 * w + 3], inv) << 24);
+          for (int i = 0; i < 4; ++i)
+            w[i] = (uint32_t)(uint8_t)quantize_int8(x[4 * i + 0], inv) |
+                   ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 1], inv) << 8) |
+                   ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 2], inv) << 16) |
+                   ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 3], inv) << 24);
+          packed = make_uint4(w[0], w[1], w[2], w[3]);
         } else {
-#pragma unroll
-          for (int w = 0; w < 4; ++w)
-            packed[w] = (uint32_t)quantize_e4m3(x[4 * w + 0], scale) |
-                        ((uint32_t)quantize_e4m3(x[4 * w + 1], scale) << 8) |
-                        ((uint32_t)quantize_e4m3(x[4 * w + 2], scale) << 16) |
-                        ((uint32_t)quantize_e4m3(x[4 * w + 3], scale) << 24);
+          packed = quantize16(x, scale);
         }
-        st_v4((which == 0 ? k_cache : v_cache) + dst,
-              make_uint4(packed[0], packed[1], packed[2], packed[3]));
+        st_v4((which == 0 ? k_cache : v_cache) + dst, packed);
       }
       if (ok && sub == 0) (which == 0 ? k_scales : v_scales)[slot * num_heads + h] = scale;
     }
@@ -269,22 +625,6 @@ store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
 }
 
 // -------------------------------------------------------------------- FP8 calibration
-// The scale torch computes for `x.abs().amax().clamp(min=1e-8) / 448.0` on a CUDA
-// tensor of dtype T: clamp's bound is first converted to T, and division by a
-// Python (CPU) scalar is a multiplication by the fp32 reciprocal; the result is
-// rounded to T, and `.item()` + `fill_` store it exactly in the fp32 scale.
-template <typename T> __device__ __forceinline__ float torch_fp8_scale(float amax) {
-  const float lower = round_through<T>(1e-8f);
-  const float a = isnan(amax) ? amax : fmaxf(amax, lower);
-  const float inv448 = 1.0f / 448.0f;
-  return round_through<T>(a * inv448);
-}
-
-struct CalibWork {  // MKV_FP8_CALIB_WORK_BYTES bytes, zero between calls
-  unsigned int amax_bits[2];
-  unsigned int arrived[2];
-};
-static_assert(sizeof(CalibWork) == MKV_FP8_CALIB_WORK_BYTES, "calibration work layout");
 
 // blockIdx.y selects K (0) or V (1). Every block first checks the sentinel; when the
 // scale is already calibrated all blocks return at once (the steady state: one
@@ -396,7 +736,21 @@ int launch_store(const void* key, const void* value, int64_t k_st, int64_t k_sh,
                    aligned16(k_cache) && aligned16(v_cache) && ((k_st * eb) % 16 == 0) &&
                    ((k_sh * eb) % 16 == 0) && ((v_st * eb) % 16 == 0) &&
                    ((v_sh * eb) % 16 == 0);
-  if (vec) {
+  const int64_t chunks = vec ? num_tokens * num_heads * (row_bytes / 16) : 0;
+  if (vec && chunks < ((int64_t)1 << 31)) {
+    const uint32_t row_chunks = (uint32_t)(row_bytes / 16);
+    const int per = per_thread_items(chunks);
+    const int grid = grid_for((chunks + per - 1) / per, kStoreThreads);
+#define MKV_COPY(C)                                                                            \
+  store_kv_copy_kernel<SlotT, C><<<grid, kStoreThreads, 0, stream>>>(                         \
+      (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb, \
+      (uint8_t*)k_cache, (uint8_t*)v_cache, slots, num_slots, (uint32_t)chunks,               \
+      (uint32_t)num_heads, row_chunks, invalid)
+    if (per == 4) MKV_COPY(4);
+    else if (per == 2) MKV_COPY(2);
+    else MKV_COPY(1);
+#undef MKV_COPY
+  } else if (vec) {
     const int row_chunks = (int)(row_bytes / 16);
     const int grid = grid_for(num_tokens * num_heads * row_chunks, kStoreThreads);
     store_kv_vec16_kernel<SlotT><<<grid, kStoreThreads, 0, stream>>>(
@@ -415,19 +769,41 @@ int launch_store(const void* key, const void* value, int64_t k_st, int64_t k_sh,
 template <typename T, typename SlotT>
 int launch_store_fp8(const void* key, const void* value, int64_t k_st, int64_t k_sh,
                      int64_t v_st, int64_t v_sh, void* k_cache, void* v_cache,
-                     const float* k_scale, const float* v_scale, int64_t num_slots,
+                     float* k_scale, float* v_scale, int64_t num_slots,
                      const SlotT* slots, int64_t num_tokens, int num_heads, int head_dim,
-                     int32_t* invalid, cudaStream_t stream) {
+                     CalibWork* work, int32_t* invalid, cudaStream_t stream) {
   const int64_t eb = sizeof(T);
   const bool vec = aligned16(key) && aligned16(value) && ((k_st * eb) % 16 == 0) &&
                    ((k_sh * eb) % 16 == 0) && ((v_st * eb) % 16 == 0) &&
                    ((v_sh * eb) % 16 == 0);
   const int groups = head_dim / 16;
-  const int grid = grid_for(num_tokens * num_heads * groups, kStoreThreads);
-  store_kv_fp8_kernel<T, SlotT><<<grid, kStoreThreads, 0, stream>>>(
-      (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,
-      (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale, slots, num_slots, num_tokens,
-      num_heads, groups, vec, invalid);
+  const int64_t total = num_tokens * num_heads * groups;
+  if (total >= ((int64_t)1 << 31)) {  // beyond 32-bit group indices: the two-kernel form
+    if (work != nullptr) {
+      int blocks = grid_for(total, kStoreThreads);
+      if (blocks > kNumSMs * 4) blocks = kNumSMs * 4;
+      fp8_calibrate_kernel<T><<<dim3(blocks, 2), kStoreThreads, 0, stream>>>(
+          (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,
+          num_tokens, num_heads, head_dim, vec, k_scale, v_scale, work);
+    }
+    const int grid = grid_for(total, kStoreThreads);
+    store_kv_fp8_kernel<T, SlotT><<<grid, kStoreThreads, 0, stream>>>(
+        (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,
+        (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale, slots, num_slots, num_tokens,
+        num_heads, groups, vec, invalid);
+    return cuda_status(cudaGetLastError(), "store_kvcache_fp8 launch");
+  }
+  const int per = vec ? (per_thread_items(total) >= 2 ? 2 : 1) : 1;
+  const int grid = grid_for((total + per - 1) / per, kStoreThreads);
+#define MKV_FP8(G, V)                                                                            \
+  store_kv_fp8_calib_kernel<T, SlotT, G, V><<<grid, kStoreThreads, 0, stream>>>(                \
+      (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,   \
+      (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale, slots, num_slots, (uint32_t)total, \
+      (uint32_t)num_heads, (uint32_t)groups, work, invalid)
+  if (!vec) MKV_FP8(1, false);
+  else if (per == 2) MKV_FP8(2, true);
+  else MKV_FP8(1, true);
+#undef MKV_FP8
   return cuda_status(cudaGetLastError(), "store_kvcache_fp8 launch");
 }
 
@@ -546,6 +922,57 @@ extern "C" int mkv_calibrate_fp8_scales(const void* key, const void* value,
   }
 }
 
+namespace mkv {
+namespace {
+int store_fp8_impl(const char* fn, const void* key, const void* value, int64_t key_stride_token,
+                   int64_t key_stride_head, int64_t value_stride_token, int64_t value_stride_head,
+                   void* k_cache, void* v_cache, float* k_scale, float* v_scale,
+                   int64_t num_blocks, int32_t block_size, const void* slot_mapping,
+                   int32_t slot_index_type, int64_t num_tokens, int32_t num_kv_heads,
+                   int32_t head_dim, int32_t dtype, void* calib_work, int32_t* invalid_count,
+                   void* stream) {
+  clear_error();
+  int st = check_common(key, value, k_cache, v_cache, slot_mapping, slot_index_type, num_blocks,
+                        block_size, num_tokens, num_kv_heads, head_dim, fn);
+  if (st != MKV_OK) return st;
+  if (head_dim % 16 != 0)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: head_dim must be a multiple of 16 (got %d)", fn,
+                     head_dim);
+  if (!k_scale || !v_scale)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: null scale pointer", fn);
+  if ((((uintptr_t)k_cache) & 15u) || (((uintptr_t)v_cache) & 15u))
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: caches must be 16-byte aligned", fn);
+  if (calib_work != nullptr && ((uintptr_t)calib_work & 7u) != 0)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: calib_work must be 8-byte aligned", fn);
+  if (num_tokens == 0) return MKV_OK;
+  const int64_t num_slots = num_blocks * block_size;
+  cudaStream_t s = (cudaStream_t)stream;
+  CalibWork* work = (CalibWork*)calib_work;
+  const bool i64 = slot_index_type == MKV_INDEX_I64;
+#define MKV_STORE8(T)                                                                          \
+  return i64 ? launch_store_fp8<T, int64_t>(key, value, key_stride_token, key_stride_head,     \
+                                            value_stride_token, value_stride_head, k_cache,    \
+                                            v_cache, k_scale, v_scale, num_slots,              \
+                                            (const int64_t*)slot_mapping, num_tokens,          \
+                                            num_kv_heads, head_dim, work, invalid_count, s)    \
+             : launch_store_fp8<T, int32_t>(key, value, key_stride_token, key_stride_head,     \
+                                            value_stride_token, value_stride_head, k_cache,    \
+                                            v_cache, k_scale, v_scale, num_slots,              \
+                                            (const int32_t*)slot_mapping, num_tokens,          \
+                                            num_kv_heads, head_dim, work, invalid_count, s)
+  switch (dtype) {
+    case MKV_DTYPE_F32: MKV_STORE8(float);
+    case MKV_DTYPE_F16: MKV_STORE8(f16);
+    case MKV_DTYPE_BF16: MKV_STORE8(bf16);
+    default:
+      return set_error(MKV_ERR_UNSUPPORTED, "%s: key dtype must be f32, f16 or bf16 (got %d)", fn,
+                       dtype);
+  }
+#undef MKV_STORE8
+}
+}  // namespace
+}  // namespace mkv
+
 extern "C" int mkv_store_kvcache_fp8(const void* key, const void* value,
                                      int64_t key_stride_token, int64_t key_stride_head,
                                      int64_t value_stride_token, int64_t value_stride_head,
@@ -555,43 +982,25 @@ extern "C" int mkv_store_kvcache_fp8(const void* key, const void* value,
                                      int32_t slot_index_type, int64_t num_tokens,
                                      int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
                                      int32_t* invalid_count, void* stream) {
-  clear_error();
-  int st = check_common(key, value, k_cache, v_cache, slot_mapping, slot_index_type, num_blocks,
-                        block_size, num_tokens, num_kv_heads, head_dim, "mkv_store_kvcache_fp8");
-  if (st != MKV_OK) return st;
-  if (head_dim % 16 != 0)
-    return set_error(MKV_ERR_UNSUPPORTED,
-                     "mkv_store_kvcache_fp8: head_dim must be a multiple of 16 (got %d)",
-                     head_dim);
-  if (!k_scale || !v_scale)
-    return set_error(MKV_ERR_INVALID_ARGUMENT, "mkv_store_kvcache_fp8: null scale pointer");
-  if ((((uintptr_t)k_cache) & 15u) || (((uintptr_t)v_cache) & 15u))
-    return set_error(MKV_ERR_INVALID_ARGUMENT,
-                     "mkv_store_kvcache_fp8: caches must be 16-byte aligned");
-  if (num_tokens == 0) return MKV_OK;
-  const int64_t num_slots = num_blocks * block_size;
-  cudaStream_t s = (cudaStream_t)stream;
-  const bool i64 = slot_index_type == MKV_INDEX_I64;
-#define MKV_STORE8(T)                                                                          \
-  return i64 ? launch_store_fp8<T, int64_t>(key, value, key_stride_token, key_stride_head,     \
-                                            value_stride_token, value_stride_head, k_cache,    \
-                                            v_cache, k_scale, v_scale, num_slots,              \
-                                            (const int64_t*)slot_mapping, num_tokens,          \
-                                            num_kv_heads, head_dim, invalid_count, s)          \
-             : launch_store_fp8<T, int32_t>(key, value, key_stride_token, key_stride_head,     \
-                                            value_stride_token, value_stride_head, k_cache,    \
-                                            v_cache, k_scale, v_scale, num_slots,              \
-                                            (const int32_t*)slot_mapping, num_tokens,          \
-                                            num_kv_heads, head_dim, invalid_count, s)
-  switch (dtype) {
-    case MKV_DTYPE_F32: MKV_STORE8(float);
-    case MKV_DTYPE_F16: MKV_STORE8(f16);
-    case MKV_DTYPE_BF16: MKV_STORE8(bf16);
-    default:
-      return set_error(MKV_ERR_UNSUPPORTED,
-                       "mkv_store_kvcache_fp8: key dtype must be f32, f16 or bf16 (got %d)", dtype);
-  }
-#undef MKV_STORE8
+  // without calibration scratch the kernel only reads the scales
+  return store_fp8_impl("mkv_store_kvcache_fp8", key, value, key_stride_token, key_stride_head,
+                        value_stride_token, value_stride_head, k_cache, v_cache,
+                        const_cast<float*>(k_scale), const_cast<float*>(v_scale), num_blocks,
+                        block_size, slot_mapping, slot_index_type, num_tokens, num_kv_heads,
+                        head_dim, dtype, nullptr, invalid_count, stream);
+}
+
+extern "C" int mkv_store_kvcache_fp8_calibrating(
+    const void* key, const void* value, int64_t key_stride_token, int64_t key_stride_head,
+    int64_t value_stride_token, int64_t value_stride_head, void* k_cache, void* v_cache,
+    float* k_scale, float* v_scale, int64_t num_blocks, int32_t block_size,
+    const void* slot_mapping, int32_t slot_index_type, int64_t num_tokens, int32_t num_kv_heads,
+    int32_t head_dim, int32_t dtype, void* calib_work, int32_t* invalid_count, void* stream) {
+  return store_fp8_impl("mkv_store_kvcache_fp8_calibrating", key, value, key_stride_token,
+                        key_stride_head, value_stride_token, value_stride_head, k_cache, v_cache,
+                        k_scale, v_scale, num_blocks, block_size, slot_mapping, slot_index_type,
+                        num_tokens, num_kv_heads, head_dim, dtype, calib_work, invalid_count,
+                        stream);
 }
 
 extern "C" int mkv_store_kvcache_quant_per_token_head(

@@ -213,19 +213,13 @@ def store_kvcache_fp8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Ten
     lib = _lib.load()
     dt = _DTYPES[key.dtype]
     with _on_device(dev):
-        stream = _stream(dev)
-        work = _calibration_work(dev)
-        if not _calibration_suspended:
-            st = lib.mkv_calibrate_fp8_scales(
-                key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
-                value.stride(1), num_tokens, num_kv_heads, head_dim, dt, k_scale.data_ptr(),
-                v_scale.data_ptr(), work.data_ptr(), stream)
-            _lib.check("mkv_calibrate_fp8_scales", st)
-        st = lib.mkv_store_kvcache_fp8(
+        # one launch: calibration of a sentinel scale (unless suspended) + quantising store
+        work = None if _calibration_suspended else _calibration_work(dev).data_ptr()
+        st = lib.mkv_store_kvcache_fp8_calibrating(
             key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
             value.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), k_scale.data_ptr(),
             v_scale.data_ptr(), num_blocks, block_size, slots.data_ptr(), _INDEX[slots.dtype],
-            num_tokens, num_kv_heads, head_dim, dt, None, stream)
+            num_tokens, num_kv_heads, head_dim, dt, work, None, _stream(dev))
     _lib.check(fn, st)
 
 
@@ -276,9 +270,33 @@ def store_kvcache_int8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Te
 
 
 # ---------------------------------------------------------------------------------- decode
+_decode_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _decode_workspace(dev: torch.device, stream_ptr: int, nbytes: int):
+    """(workspace, flags) for a decode on `stream_ptr`: one buffer per (device, stream),
+    zeroed when it is allocated. The decode leaves its arrival counters at zero, so
+    decodes ordered on that stream reuse it without clearing it again
+    (MKV_DECODE_WORKSPACE_ZEROED). Inside a CUDA-graph capture a buffer that is too
+    small is not replaced: the call takes a fresh one from the capture's pool and lets
+    the library clear its counters."""
+    if nbytes == 0:
+        return None, _lib.DECODE_WORKSPACE_ZEROED
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (idx, stream_ptr)
+    buf = _decode_ws.get(key)
+    if buf is not None and buf.numel() >= nbytes:
+        return buf, _lib.DECODE_WORKSPACE_ZEROED
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=dev), 0
+    buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+    _decode_ws[key] = buf
+    return buf, _lib.DECODE_WORKSPACE_ZEROED
+
+
 def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, context_lens,
             scale, num_heads, num_kv_heads, head_dim, block_size, num_splits: int = 0,
-            per_token_head: bool = False):
+            per_token_head: bool = False, overlap_previous: bool = False):
     if query.dim() != 3 or query.shape[1] != num_heads or query.shape[2] != head_dim:
         raise ValueError(f"{fn}: query must be (batch, {num_heads}, {head_dim}), got {tuple(query.shape)}")
     if query.dtype not in _FLOAT_IO:
@@ -289,6 +307,7 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
     dev = _require_cuda(fn, *tensors)
     batch_size = query.shape[0]
     max_num_blocks = block_tables.shape[1]
+    inputs = (query.data_ptr(), block_tables.data_ptr(), context_lens.data_ptr())
     query = query if query.stride(-1) == 1 else query.contiguous()
     output = torch.empty(query.shape, dtype=query.dtype, device=query.device)
     if batch_size == 0:
@@ -303,38 +322,29 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
     num_blocks = _check_cache(fn, k_cache, v_cache, block_size, num_kv_heads, head_dim)
     if per_token_head:
         _check_row_scales(fn, k_scale, v_scale, num_blocks, block_size, num_kv_heads)
+    # an input copied here was written by the kernel just launched: no overlap with it
+    copied = inputs != (query.data_ptr(), block_tables.data_ptr(), lens.data_ptr())
     lib = _lib.load()
     ws_bytes = lib.mkv_paged_decode_workspace_bytes(batch_size, num_heads, num_kv_heads, head_dim,
                                                     block_size, max_num_blocks, num_splits)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
-    ws_ptr = ws.data_ptr() if ws is not None else None
     with _on_device(dev):
         stream = _stream(dev)
-        if per_token_head:
-            st = lib.mkv_paged_decode_quant_per_token_head(
-                query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
-                k_cache.data_ptr(), v_cache.data_ptr(), _DTYPES[k_cache.dtype], k_scale.data_ptr(),
-                v_scale.data_ptr(), num_blocks, block_size, block_tables.data_ptr(),
-                _INDEX[block_tables.dtype], block_tables.stride(0), max_num_blocks, lens.data_ptr(),
-                _INDEX[lens.dtype], batch_size, num_heads, num_kv_heads, head_dim, float(scale),
-                output.data_ptr(), output.stride(0), output.stride(1), ws_ptr, ws_bytes, num_splits,
-                None, stream)
-        elif k_scale is None:
-            st = lib.mkv_paged_decode(
-                query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
-                k_cache.data_ptr(), v_cache.data_ptr(), _DTYPES[k_cache.dtype], num_blocks,
-                block_size, block_tables.data_ptr(), _INDEX[block_tables.dtype],
-                block_tables.stride(0), max_num_blocks, lens.data_ptr(), _INDEX[lens.dtype],
-                batch_size, num_heads, num_kv_heads, head_dim, float(scale), output.data_ptr(),
-                output.stride(0), output.stride(1), ws_ptr, ws_bytes, num_splits, None, stream)
-        else:
-            st = lib.mkv_paged_decode_fp8(
-                query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
-                k_cache.data_ptr(), v_cache.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(),
-                num_blocks, block_size, block_tables.data_ptr(), _INDEX[block_tables.dtype],
-                block_tables.stride(0), max_num_blocks, lens.data_ptr(), _INDEX[lens.dtype],
-                batch_size, num_heads, num_kv_heads, head_dim, float(scale), output.data_ptr(),
-                output.stride(0), output.stride(1), ws_ptr, ws_bytes, num_splits, None, stream)
+        ws, flags = _decode_workspace(dev, stream.value or 0, ws_bytes)
+        if overlap_previous and not copied:
+            flags |= _lib.DECODE_OVERLAP_PREVIOUS
+        pt = k_scale is not None and not per_token_head  # per-tensor FP8 scales
+        st = lib.mkv_paged_decode_ex(
+            query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
+            k_cache.data_ptr(), v_cache.data_ptr(),
+            _lib.DTYPE_FP8_E4M3 if k_cache.dtype == torch.uint8 else _DTYPES[k_cache.dtype],
+            k_scale.data_ptr() if pt else None, v_scale.data_ptr() if pt else None,
+            k_scale.data_ptr() if per_token_head else None,
+            v_scale.data_ptr() if per_token_head else None,
+            num_blocks, block_size, block_tables.data_ptr(), _INDEX[block_tables.dtype],
+            block_tables.stride(0), max_num_blocks, lens.data_ptr(), _INDEX[lens.dtype],
+            batch_size, num_heads, num_kv_heads, head_dim, float(scale), output.data_ptr(),
+            output.stride(0), output.stride(1), ws.data_ptr() if ws is not None else None,
+            ws.numel() if ws is not None else 0, num_splits, flags, None, stream)
     _lib.check(fn, st)
     return output
 
@@ -342,16 +352,22 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
 def paged_attention_decode(query: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                            block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                            num_heads: int, num_kv_heads: int, head_dim: int,
-                           block_size: int, num_splits: int = 0) -> torch.Tensor:
+                           block_size: int, num_splits: int = 0,
+                           overlap_previous: bool = False) -> torch.Tensor:
     """Decode attention of query (batch, num_heads, head_dim) over the paged K/V of each
     sequence: tokens t < context_lens[b] on pages block_tables[b, t // block_size],
     GQA kv head = h // (num_heads // num_kv_heads). Returns (batch, num_heads, head_dim)
     in the query dtype. Reference: attention.py:895-950 (kernel 517-646).
-    `num_splits` (0 = automatic) forces the split-KV count; it is not in the reference."""
+    `num_splits` (0 = automatic) forces the split-KV count; it is not in the reference.
+    `overlap_previous` (not in the reference) lets the decode start while the previous
+    kernel on the stream runs, reading the pages only once it has completed; pass it only
+    when that kernel writes none of query, block_tables and context_lens, as when it is
+    this step's store_kvcache (Attention.forward does so)."""
     if k_cache.dtype == torch.float8_e4m3fn:
         raise ValueError("paged_attention_decode: FP8 caches go through paged_attention_decode_quantized")
     return _decode("paged_attention_decode", query, k_cache, v_cache, None, None, block_tables,
-                   context_lens, scale, num_heads, num_kv_heads, head_dim, block_size, num_splits)
+                   context_lens, scale, num_heads, num_kv_heads, head_dim, block_size, num_splits,
+                   overlap_previous=overlap_previous)
 
 
 def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
@@ -359,13 +375,15 @@ def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
                                      v_scale: torch.Tensor, block_tables: torch.Tensor,
                                      context_lens: torch.Tensor, scale: float, num_heads: int,
                                      num_kv_heads: int, head_dim: int, block_size: int,
-                                     kv_cache_dtype: str, num_splits: int = 0) -> torch.Tensor:
+                                     kv_cache_dtype: str, num_splits: int = 0,
+                                     overlap_previous: bool = False) -> torch.Tensor:
     """Decode attention over a quantised paged cache, dequantised while the pages are
     loaded: 'fp8_per_tensor' (e4m3 pages, scales of shape (1,)), 'fp8_per_token_head'
     (e4m3) and 'int8_per_token_head' (int8), the last two with a scale per (page, row,
     kv head) in k_scale/v_scale (num_blocks, block_size, num_kv_heads). Reference:
     attention.py:1213-1268 with paged_attention_decode_fp8_kernel (953-1121) and
-    paged_attention_decode_quantized_tile_kernel (1124-1210)."""
+    paged_attention_decode_quantized_tile_kernel (1124-1210). `num_splits` and
+    `overlap_previous` as for paged_attention_decode."""
     fn = "paged_attention_decode_quantized"
     if kv_cache_dtype in _PER_TOKEN_HEAD:
         want = torch.int8 if kv_cache_dtype.startswith("int8") else torch.float8_e4m3fn
@@ -373,7 +391,7 @@ def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
             raise ValueError(f"{fn}: {kv_cache_dtype} needs {want} caches (got {k_cache.dtype})")
         return _decode(fn, query, k_cache, v_cache, k_scale, v_scale, block_tables,
                        context_lens, scale, num_heads, num_kv_heads, head_dim, block_size,
-                       num_splits, per_token_head=True)
+                       num_splits, per_token_head=True, overlap_previous=overlap_previous)
     if kv_cache_dtype != "fp8_per_tensor":
         raise NotImplementedError(
             f"{fn}: kv_cache_dtype {kv_cache_dtype!r} is not implemented "
@@ -383,7 +401,8 @@ def paged_attention_decode_quantized(query: torch.Tensor, k_cache: torch.Tensor,
     if k_scale.dtype != torch.float32 or v_scale.dtype != torch.float32:
         raise ValueError(f"{fn}: k_scale/v_scale must be float32")
     return _decode(fn, query, k_cache, v_cache, k_scale, v_scale, block_tables, context_lens,
-                   scale, num_heads, num_kv_heads, head_dim, block_size, num_splits)
+                   scale, num_heads, num_kv_heads, head_dim, block_size, num_splits,
+                   overlap_previous=overlap_previous)
 
 
 # ---------------------------------------------------------------------------------- prefill
@@ -506,7 +525,9 @@ class Attention(nn.Module):
         quant = mode != "auto"
         if mode not in ("auto", "fp8_per_tensor") + _PER_TOKEN_HEAD:
             raise NotImplementedError(f"kv_cache_dtype {mode!r} is not implemented")
+        appended = False
         if k_cache.numel() > 0 and v_cache.numel() > 0 and context.slot_mapping is not None:
+            appended = True
             if k.dim() == 4:
                 b, n, kvh, d = k.shape
                 k, v = k.reshape(b * n, kvh, d), v.reshape(b * n, kvh, d)
@@ -521,15 +542,20 @@ class Attention(nn.Module):
         scale = self.scale / (self.head_dim ** 0.5)
         if context.is_prefill:
             return self._prefill(q, k_cache, v_cache, context, scale, mode, quant)
+        # The append (if any) was the last kernel launched and writes only the pages (and
+        # scales): the decode's prologue may overlap it. Without an append the previous
+        # kernel may have produced q, so no overlap.
+        overlap = appended
         if quant:
             o = paged_attention_decode_quantized(
                 q, k_cache, v_cache, self.k_scale, self.v_scale, context.block_tables,
                 context.context_lens, scale, self.num_heads, self.num_kv_heads, self.head_dim,
-                self.block_size, self.kv_cache_dtype)
+                self.block_size, self.kv_cache_dtype, overlap_previous=overlap)
         else:
             o = paged_attention_decode(
                 q, k_cache, v_cache, context.block_tables, context.context_lens, scale,
-                self.num_heads, self.num_kv_heads, self.head_dim, self.block_size)
+                self.num_heads, self.num_kv_heads, self.head_dim, self.block_size,
+                overlap_previous=overlap)
         return o.reshape(o.shape[0], self.num_heads * self.head_dim)
 
     def _decode_rows(self, q, k_cache, v_cache, block_tables, context_lens, scale, mode, quant):

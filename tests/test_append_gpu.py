@@ -267,3 +267,75 @@ def test_fp8_capture_warmup_does_not_calibrate():
     graph.replay()
     torch.cuda.synchronize()
     assert float(ks) == want_k  # frozen after the first calibration
+
+
+# ------------------------------------------------------- one-launch FP8 store (calibrating)
+def _fp8_call(lib, fn, key, value, kc, vc, ks, vs, slots, BS, work, invalid=None):
+    T, KVH, D = key.shape
+    nb = kc.shape[0]
+    args = [key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1), value.stride(0),
+            value.stride(1), kc.data_ptr(), vc.data_ptr(), ks.data_ptr(), vs.data_ptr(), nb, BS,
+            slots.data_ptr(), lib_mod.INDEX_I64 if slots.dtype == torch.int64 else lib_mod.INDEX_I32,
+            T, KVH, D, {torch.bfloat16: 2, torch.float16: 1, torch.float32: 0}[key.dtype]]
+    if fn == "mkv_store_kvcache_fp8_calibrating":
+        args.append(work)
+    st = getattr(lib, fn)(*args, invalid.data_ptr() if invalid is not None else None,
+                          torch.cuda.current_stream().cuda_stream)
+    assert st == 0, lib.mkv_last_error()
+
+
+@pytest.mark.parametrize("T", [3, 4096, 70001])
+@pytest.mark.parametrize("sentinel", ["both", "k", "v", "none"])
+def test_fp8_one_launch_equals_calibrate_then_store(T, sentinel):
+    """mkv_store_kvcache_fp8_calibrating against the two-kernel sequence
+    mkv_calibrate_fp8_scales + mkv_store_kvcache_fp8, byte for byte and scale for scale:
+    a few tokens, config 2's 4096 (one wave), and 70001 (grid-stride loops), with either,
+    both or neither scale still at the sentinel; slots -1 and out of range included. The
+    calibration words are left at zero."""
+    lib = lib_mod.load()
+    KVH, D, BS = 8, 128, 256
+    NB = (T + 300) // BS + 4
+    g = torch.Generator().manual_seed(T)
+    key = (torch.randn(T, KVH, D, generator=g) * 3).to(torch.bfloat16).cuda()
+    value = (torch.randn(T, KVH, D, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    slots = torch.randperm(NB * BS, generator=g)[:T]
+    slots[::97] = -1
+    slots[1::131] = NB * BS + 5  # out of range: skipped and counted
+    slots = slots.cuda()
+    init = {"both": (1.0, 1.0), "k": (1.0, 0.02), "v": (0.03, 1.0), "none": (0.05, 0.04)}[sentinel]
+    outs = []
+    for fn in ("two_kernels", "mkv_store_kvcache_fp8_calibrating"):
+        kc = torch.zeros(NB, BS, KVH, D, dtype=torch.float8_e4m3fn, device="cuda")
+        vc = torch.zeros_like(kc)
+        ks = torch.tensor([init[0]], device="cuda")
+        vs = torch.tensor([init[1]], device="cuda")
+        work = torch.zeros(lib_mod.FP8_CALIB_WORK_BYTES, dtype=torch.uint8, device="cuda")
+        inv = torch.zeros(1, dtype=torch.int32, device="cuda")
+        if fn == "two_kernels":
+            st = lib.mkv_calibrate_fp8_scales(key.data_ptr(), value.data_ptr(), key.stride(0),
+                                              key.stride(1), value.stride(0), value.stride(1), T,
+                                              KVH, D, 2, ks.data_ptr(), vs.data_ptr(),
+                                              work.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            assert st == 0
+            _fp8_call(lib, "mkv_store_kvcache_fp8", key, value, kc, vc, ks, vs, slots, BS, None, inv)
+        else:
+            _fp8_call(lib, fn, key, value, kc, vc, ks, vs, slots, BS, work.data_ptr(), inv)
+        torch.cuda.synchronize()
+        assert int(work.count_nonzero()) == 0
+        outs.append((kc.view(torch.uint8).cpu(), vc.view(torch.uint8).cpu(), float(ks), float(vs),
+                     int(inv)))
+    (k0, v0, ks0, vs0, i0), (k1, v1, ks1, vs1, i1) = outs
+    assert (ks0, vs0) == (ks1, vs1)
+    if sentinel in ("both", "k"):
+        assert ks1 == fp8_scale_ref(key.cpu())
+    if sentinel in ("both", "v"):
+        assert vs1 == fp8_scale_ref(value.cpu())
+    assert torch.equal(k0, k1) and torch.equal(v0, v1)
+    assert i0 == i1 == len(range(1, T, 131))
+    # and both equal the oracle
+    ek = torch.zeros(NB, BS, KVH, D, dtype=torch.float8_e4m3fn)
+    ev = torch.zeros_like(ek)
+    sl = slots.cpu().clone()
+    sl[sl >= NB * BS] = -1
+    store_kvcache_fp8_ref(key.cpu(), value.cpu(), ek, ev, torch.tensor([ks1]), torch.tensor([vs1]), sl, BS)
+    assert torch.equal(k1, ek.view(torch.uint8)) and torch.equal(v1, ev.view(torch.uint8))

@@ -357,3 +357,69 @@ def test_balanced_schedule_counts_invalid_pages_once():
         assert st == 0, lib.mkv_last_error()
         torch.cuda.synchronize()
         assert int(cnt) == 3, (splits, int(cnt))
+
+
+# ------------------------------------------------------------------ launch options
+@pytest.mark.parametrize("fp8", [False, True])
+def test_overlapped_step_equals_serial_step(fp8):
+    """The decode launched to overlap the append before it (programmatic dependent
+    launch) reads what the append wrote: eager and CUDA-graph replays equal the serial
+    step bit for bit, the FP8 scale calibrated by the append's first call included."""
+    lens = [int(x) for x in torch.randint(1, 3000, (24,), generator=torch.Generator().manual_seed(9))]
+    outs = []
+    for overlap in (False, True, True):
+        w = wl.decode_workload("ovl", 24, 32, 8, 128, 16, lens, fp8=fp8, seed=41)
+        ks = torch.ones(1, device="cuda") if fp8 else None  # sentinel: the first append calibrates
+        vs = torch.ones(1, device="cuda") if fp8 else None
+
+        def step():
+            if fp8:
+                attn.store_kvcache_fp8(w.new_k, w.new_v, w.k_cache, w.v_cache, ks, vs, w.slot_mapping,
+                                       w.block_size, "fp8_per_tensor")
+                return attn.paged_attention_decode_quantized(
+                    w.query, w.k_cache, w.v_cache, ks, vs, w.block_tables, w.context_lens, w.scale,
+                    w.num_heads, w.num_kv_heads, w.head_dim, w.block_size, "fp8_per_tensor",
+                    overlap_previous=overlap)
+            attn.store_kvcache(w.new_k, w.new_v, w.k_cache, w.v_cache, w.slot_mapping, w.block_size)
+            return attn.paged_attention_decode(w.query, w.k_cache, w.v_cache, w.block_tables,
+                                               w.context_lens, w.scale, w.num_heads, w.num_kv_heads,
+                                               w.head_dim, w.block_size, overlap_previous=overlap)
+
+        if len(outs) < 2:
+            outs.append(step().clone())
+        else:  # captured: the graph's first replay does the calibration
+            graph = torch.cuda.CUDAGraph()
+            with fp8_suspended():
+                step()  # warm-up without calibrating (allocates the scratch)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph):
+                static_out = step()
+            graph.replay()
+            graph.replay()
+            torch.cuda.synchronize()
+            outs.append(static_out.clone())
+        torch.cuda.synchronize()
+    assert torch.equal(torch.nan_to_num(outs[0], nan=3.0), torch.nan_to_num(outs[1], nan=3.0))
+    assert torch.equal(torch.nan_to_num(outs[0], nan=3.0), torch.nan_to_num(outs[2], nan=3.0))
+
+
+def fp8_suspended():
+    return attn.fp8_calibration_suspended()
+
+
+def test_decode_ex_rejects_bad_arguments():
+    lib = mkv_module("_lib").load()
+    t = torch.zeros(64, dtype=torch.float32, device="cuda")
+    p = t.data_ptr()
+    base = [p, 4096, 128, 2, p, p]
+    tail = [1, 16, p, 0, 1, 1, p, 1, 1, 8, 2, 128, 0.1, p, 4096, 128, None, 0, 0]
+    stream = torch.cuda.current_stream().cuda_stream
+    # unknown flag bits
+    st = lib.mkv_paged_decode_ex(*base, 2, None, None, None, None, *tail, 8, None, stream)
+    assert st == mkv_module("_lib").ERR_INVALID_ARGUMENT and b"flags" in lib.mkv_last_error()
+    # per-tensor and per-(token, head) scales together
+    st = lib.mkv_paged_decode_ex(*base, 3, p, p, p, p, *tail, 0, None, stream)
+    assert st == mkv_module("_lib").ERR_INVALID_ARGUMENT
+    # scales for an unquantised cache
+    st = lib.mkv_paged_decode_ex(*base, 2, p, p, None, None, *tail, 0, None, stream)
+    assert st == mkv_module("_lib").ERR_INVALID_ARGUMENT
