@@ -320,6 +320,32 @@ MKV_API size_t mkv_paged_prefill_workspace_bytes(int32_t num_seqs, int64_t total
                                                  int32_t cache_dtype);
 
 /*
+ * Causal attention of variable-length sequences over their own contiguous K/V: the
+ * reference's flash_attention_prefill (attention.py:446-516, kernel 336-443), which
+ * Attention.forward takes when the batch is whole prompts (context.is_full_prefill,
+ * attention.py:1771) and the model runner's warm-up takes before a KV cache exists
+ * (model_runner.py:193-200). Sequence b owns rows [cu_seqlens[b], cu_seqlens[b+1]) of
+ * query (total_tokens, num_heads, head_dim) and of key/value (total_tokens, num_kv_heads,
+ * head_dim); row i at position t = i - cu_seqlens[b] attends to that sequence's tokens
+ * 0..t, kv head of query head h being h / (num_heads / num_kv_heads); out has the query's
+ * shape and dtype (f32/f16/bf16, key/value the same dtype, head_dim rows 16-byte aligned).
+ * max_seqlen must bound every sequence's length. The K/V rows are packed into 128-row
+ * pages of the workspace (mkv_varlen_prefill_workspace_bytes, 256-byte aligned) and
+ * mkv_paged_prefill runs over them.
+ */
+MKV_API size_t mkv_varlen_prefill_workspace_bytes(int32_t num_seqs, int64_t total_tokens,
+                                                  int32_t max_seqlen, int32_t num_kv_heads,
+                                                  int32_t head_dim, int32_t dtype);
+MKV_API int mkv_varlen_prefill(
+    const void* query, int64_t q_stride_token, int64_t q_stride_head, int32_t dtype,
+    const void* key, const void* value, int64_t key_stride_token, int64_t key_stride_head,
+    int64_t value_stride_token, int64_t value_stride_head, const void* cu_seqlens,
+    int32_t cu_seqlens_index_type, int32_t num_seqs, int64_t total_tokens, int32_t max_seqlen,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
+    int64_t out_stride_token, int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+    void* stream);
+
+/*
  * Every decode mode behind one entry point, with launch options. The arguments mean
  * what they mean for mkv_paged_decode; the cache mode follows from cache_dtype and the
  * scale pointers: an FP8_E4M3 cache with k_scale/v_scale (one float32 each) is the

@@ -11,6 +11,7 @@ from . import _lib
 from ._lib import LIB_PATH, MkvError, load
 from .layers.attention import (
     Attention,
+    flash_attention_prefill,
     paged_attention_decode,
     paged_attention_decode_quantized,
     store_kvcache,
@@ -19,7 +20,7 @@ from .layers.attention import (
 from .utils.context import Context, get_context, reset_context, set_context
 
 __all__ = [
-    "Attention", "Context", "LIB_PATH", "MkvError", "get_context", "load",
+    "Attention", "Context", "LIB_PATH", "MkvError", "flash_attention_prefill", "get_context", "load",
     "paged_attention_decode", "paged_attention_decode_quantized", "reset_context",
     "set_context", "store_kvcache", "store_kvcache_fp8",
 ]

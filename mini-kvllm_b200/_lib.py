@@ -61,6 +61,10 @@ SIGNATURES: dict[str, tuple] = {
         _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _p, _i32, _p, _i32, _i32, _i64, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _p]),
     "mkv_paged_prefill_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32]),
+    "mkv_varlen_prefill_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32, _i32]),
+    "mkv_varlen_prefill": (ctypes.c_int, [
+        _p, _i64, _i64, _i32, _p, _p, _i64, _i64, _i64, _i64, _p, _i32, _i32, _i64, _i32, _i32, _i32, _i32,
+        _f32, _p, _i64, _i64, _p, _sz, _p]),
     "mkv_allreduce_residual_rmsnorm": (ctypes.c_int, [
         _p, _p, _i64, _p, _i32, _i32, _p, _p, _p, _p, _p, _i64, _i32, _i32, _f32, _p, _i64, _p]),
     "mkv_decode_metadata": (ctypes.c_int, [_p, _i32, _i32, _i32, _p, _p, _p]),

@@ -1517,6 +1517,123 @@ int dispatch_prefill(const PrefillParams& p, int cache_dtype, int64_t units, cud
 }  // namespace
 }  // namespace mkv
 
+// ============================================================ contiguous (varlen) prefill
+// Causal attention of each sequence over its own contiguous K/V rows, the reference's
+// flash_attention_prefill (attention.py:446-516, kernel 336-443), which Attention.forward
+// takes for a batch of whole prompts (context.is_full_prefill, attention.py:1771) and the
+// runner's warm-up takes before any KV cache exists (model_runner.py:193-200).
+// B200 design: the rows are packed once into 128-row pages of a caller workspace (sequence
+// b owns pages [page_start[b], page_start[b] + ceil(len_b / 128)), page_start an exclusive
+// scan of the page counts), with a block table, lengths and positions built on the
+// device; the tcgen05 paged prefill then runs over those pages unchanged (query row q of
+// sequence b at position t sees tokens 0..t). The pack is one read and one write of K/V,
+// small beside the quadratic attention; the host never reads device data.
+namespace mkv {
+namespace {
+constexpr int kVarlenPage = 128;
+
+template <typename I>
+__device__ __forceinline__ int64_t ld_cu(const void* cu, int i) {
+  return (int64_t)reinterpret_cast<const I*>(cu)[i];
+}
+__device__ __forceinline__ int64_t cu_at(const void* cu, int cu_i64, int i) {
+  return cu_i64 ? ld_cu<int64_t>(cu, i) : ld_cu<int32_t>(cu, i);
+}
+
+// One CTA: page starts (exclusive scan of ceil(len / 128) in chunks of the block), block
+// tables (num_seqs x max_pages, -1 padded) and lengths.
+__global__ void __launch_bounds__(1024)
+varlen_tables_kernel(const void* cu, int cu_i64, int num_seqs, int max_pages, int* page_start,
+                     int* bt, int* lens) {
+  __shared__ int warp_sum[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  int carry = 0;
+  for (int base = 0; base < num_seqs; base += blockDim.x) {
+    const int b = base + threadIdx.x;
+    int len = 0;
+    if (b < num_seqs) {
+      const int64_t l = cu_at(cu, cu_i64, b + 1) - cu_at(cu, cu_i64, b);
+      len = l > 0 ? (int)l : 0;
+    }
+    const int np = (len + kVarlenPage - 1) / kVarlenPage;
+    int x = np;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += v;
+    }
+    if (lane == 31) warp_sum[warp] = x;
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < nwarps; ++w) {
+      if (w < warp) before += warp_sum[w];
+      total += warp_sum[w];
+    }
+    const int start = carry + before + x - np;
+    if (b < num_seqs) {
+      page_start[b] = start;
+      lens[b] = len;
+      int* row = bt + (int64_t)b * max_pages;
+      for (int j = 0; j < max_pages; ++j) row[j] = j < np ? start + j : -1;
+    }
+    carry += total;
+    __syncthreads();  // warp_sum is rewritten by the next chunk
+  }
+}
+
+// One thread per 16-byte chunk of a (token, kv head) row of K and of V: token i of
+// sequence b (binary search of cu_seqlens) at position t = i - cu[b] goes to row
+// page_start[b] * 128 + t of the pages; positions[i] = t.
+__global__ void __launch_bounds__(256)
+varlen_pack_kernel(const uint8_t* __restrict__ k, const uint8_t* __restrict__ v, int64_t k_st,
+                   int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
+                   const void* cu, int cu_i64, int num_seqs, int64_t total, int num_kv_heads,
+                   int chunks, const int* __restrict__ page_start, uint8_t* __restrict__ pk,
+                   uint8_t* __restrict__ pv, int* __restrict__ positions) {
+  const int64_t per_token = (int64_t)num_kv_heads * chunks;
+  const int64_t items = total * per_token;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < items;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = idx / per_token;
+    const int rem = (int)(idx - i * per_token);
+    const int h = rem / chunks, c = rem - h * chunks;
+    int lo = 0, hi = num_seqs;  // largest b with cu[b] <= i
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (cu_at(cu, cu_i64, mid) <= i) lo = mid; else hi = mid;
+    }
+    const int64_t t = i - cu_at(cu, cu_i64, lo);
+    const int64_t row = (int64_t)page_start[lo] * kVarlenPage + t;
+    const int64_t dst = (row * num_kv_heads + h) * (int64_t)chunks * 16 + c * 16;
+    st_v4(pk + dst, ld_stream_v4(k + i * k_st + h * k_sh + c * 16));
+    st_v4(pv + dst, ld_stream_v4(v + i * v_st + h * v_sh + c * 16));
+    if (h == 0 && c == 0) positions[i] = (int)t;
+  }
+}
+
+struct VarlenLayout {
+  int64_t pages;
+  size_t pk, pv, bt, lens, pos, start, total;
+};
+VarlenLayout varlen_layout(int num_seqs, int64_t total, int max_seqlen, int num_kv_heads,
+                           int head_dim, int eb) {
+  VarlenLayout L{};
+  const int max_pages = (max_seqlen + kVarlenPage - 1) / kVarlenPage;
+  L.pages = (total + kVarlenPage - 1) / kVarlenPage + num_seqs;
+  const size_t page_bytes = (size_t)kVarlenPage * num_kv_heads * head_dim * eb;
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  L.pk = 0;
+  L.pv = up(L.pages * page_bytes);
+  L.bt = L.pv + up(L.pages * page_bytes);
+  L.lens = L.bt + up((size_t)num_seqs * max_pages * 4);
+  L.pos = L.lens + up((size_t)num_seqs * 4);
+  L.start = L.pos + up((size_t)total * 4);
+  L.total = L.start + up((size_t)num_seqs * 4);
+  return L;
+}
+}  // namespace
+}  // namespace mkv
+
 using namespace mkv;
 
 extern "C" int mkv_paged_prefill(
@@ -1635,3 +1752,80 @@ extern "C" __attribute__((visibility("default"))) int mkv_debug_prefill_trace(un
   return (int)cudaMemcpyFromSymbol(host, mkv::g_pftrace, sizeof(mkv::g_pftrace));
 }
 #endif
+
+extern "C" size_t mkv_varlen_prefill_workspace_bytes(int32_t num_seqs, int64_t total_tokens,
+                                                     int32_t max_seqlen, int32_t num_kv_heads,
+                                                     int32_t head_dim, int32_t dtype) {
+  if (num_seqs <= 0 || total_tokens <= 0 || max_seqlen <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return 0;
+  const int eb = dtype == MKV_DTYPE_F32 ? 4 : 2;
+  return varlen_layout(num_seqs, total_tokens, max_seqlen, num_kv_heads, head_dim, eb).total;
+}
+
+extern "C" int mkv_varlen_prefill(
+    const void* query, int64_t q_stride_token, int64_t q_stride_head, int32_t dtype,
+    const void* key, const void* value, int64_t key_stride_token, int64_t key_stride_head,
+    int64_t value_stride_token, int64_t value_stride_head, const void* cu_seqlens,
+    int32_t cu_seqlens_index_type, int32_t num_seqs, int64_t total_tokens, int32_t max_seqlen,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float scale, void* out,
+    int64_t out_stride_token, int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  clear_error();
+  const char* fn = "mkv_varlen_prefill";
+  if (num_seqs < 0 || total_tokens < 0 || max_seqlen < 0 || num_heads <= 0 || num_kv_heads <= 0 ||
+      head_dim <= 0)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: bad sizes", fn);
+  if (cu_seqlens_index_type != MKV_INDEX_I32 && cu_seqlens_index_type != MKV_INDEX_I64)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: bad cu_seqlens index type", fn);
+  if (dtype != MKV_DTYPE_F32 && dtype != MKV_DTYPE_F16 && dtype != MKV_DTYPE_BF16)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: dtype must be f32, f16 or bf16", fn);
+  if (num_seqs == 0 || total_tokens == 0) return MKV_OK;
+  if (!query || !key || !value || !cu_seqlens || !out || !workspace)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
+  if (max_seqlen <= 0 || max_seqlen > total_tokens)
+    return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: max_seqlen must be in [1, total_tokens]", fn);
+  if (total_tokens >= ((int64_t)1 << 31))
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: total_tokens must be < 2^31", fn);
+  const int eb = dtype == MKV_DTYPE_F32 ? 4 : 2;
+  const int64_t row_bytes = (int64_t)head_dim * eb;
+  if (row_bytes % 16 != 0 || ((uintptr_t)key & 15u) || ((uintptr_t)value & 15u) ||
+      (key_stride_token * eb) % 16 || (key_stride_head * eb) % 16 ||
+      (value_stride_token * eb) % 16 || (value_stride_head * eb) % 16)
+    return set_error(MKV_ERR_UNSUPPORTED, "%s: key/value rows must be 16-byte aligned", fn);
+  const VarlenLayout L = varlen_layout(num_seqs, total_tokens, max_seqlen, num_kv_heads, head_dim, eb);
+  if (workspace_bytes < L.total || ((uintptr_t)workspace & 255u))
+    return set_error(MKV_ERR_WORKSPACE, "%s: workspace of %zu bytes (256-byte aligned) needed, %zu given",
+                     fn, L.total, workspace_bytes);
+  const int max_pages = (max_seqlen + kVarlenPage - 1) / kVarlenPage;
+  uint8_t* ws = (uint8_t*)workspace;
+  int* bt = (int*)(ws + L.bt);
+  int* lens = (int*)(ws + L.lens);
+  int* pos = (int*)(ws + L.pos);
+  int* start = (int*)(ws + L.start);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int cu_i64 = cu_seqlens_index_type == MKV_INDEX_I64;
+  varlen_tables_kernel<<<1, 1024, 0, s>>>(cu_seqlens, cu_i64, num_seqs, max_pages, start, bt, lens);
+  int st = cuda_status(cudaGetLastError(), "varlen_tables launch");
+  if (st != MKV_OK) return st;
+  const int chunks = (int)(row_bytes / 16);
+  const int64_t items = total_tokens * num_kv_heads * chunks;
+  int64_t blocks = (items + 255) / 256;
+  if (blocks > (int64_t)kNumSMs * 16) blocks = (int64_t)kNumSMs * 16;
+  varlen_pack_kernel<<<(unsigned)blocks, 256, 0, s>>>(
+      (const uint8_t*)key, (const uint8_t*)value, key_stride_token * eb, key_stride_head * eb,
+      value_stride_token * eb, value_stride_head * eb, cu_seqlens, cu_i64, num_seqs, total_tokens,
+      num_kv_heads, chunks, start, ws + L.pk, ws + L.pv, pos);
+  st = cuda_status(cudaGetLastError(), "varlen_pack launch");
+  if (st != MKV_OK) return st;
+  st = mkv_paged_prefill(query, q_stride_token, q_stride_head, dtype, ws + L.pk, ws + L.pv, dtype,
+                         nullptr, nullptr, nullptr, nullptr, L.pages, kVarlenPage, bt, MKV_INDEX_I32,
+                         max_pages, max_pages, lens, MKV_INDEX_I32, cu_seqlens, cu_seqlens_index_type,
+                         pos, MKV_INDEX_I32, num_seqs, total_tokens, num_heads, num_kv_heads,
+                         head_dim, scale, out, out_stride_token, out_stride_head, nullptr, 0, stream);
+  if (st != MKV_OK) {  // name this entry point in the message
+    char msg[512];
+    snprintf(msg, sizeof(msg), "%s", mkv_last_error());
+    return set_error(st, "%s: %s", fn, msg);
+  }
+  return MKV_OK;
+}

@@ -492,6 +492,55 @@ def paged_attention_prefill(query: torch.Tensor, k_cache: torch.Tensor, v_cache:
     return output
 
 
+def flash_attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                            cu_seqlens: torch.Tensor, scale: float, num_heads: int,
+                            num_kv_heads: int, head_dim: int,
+                            max_seqlen: int | None = None) -> torch.Tensor:
+    """Causal attention of each sequence over its own contiguous K/V (no KV cache):
+    q (total_tokens, num_heads, head_dim), k/v (total_tokens, num_kv_heads, head_dim),
+    sequence b owning rows [cu_seqlens[b], cu_seqlens[b+1]). Returns q's shape and dtype.
+    Reference: flash_attention_prefill, attention.py:446-516 (kernel 336-443). Like the
+    reference, it reads the longest sequence from cu_seqlens on the host unless
+    `max_seqlen` (an upper bound, e.g. the context's max_seqlen_q) is given."""
+    fn = "flash_attention_prefill"
+    if q.dim() != 3 or q.shape[1] != num_heads or q.shape[2] != head_dim:
+        raise ValueError(f"{fn}: q must be (total_tokens, {num_heads}, {head_dim}), got {tuple(q.shape)}")
+    if q.dtype not in _FLOAT_IO:
+        raise ValueError(f"{fn}: unsupported dtype {q.dtype}")
+    dev = _require_cuda(fn, q, k, v, cu_seqlens)
+    total = q.shape[0]
+    if k.shape != (total, num_kv_heads, head_dim) or v.shape != k.shape:
+        raise ValueError(f"{fn}: k/v must be ({total}, {num_kv_heads}, {head_dim})")
+    if k.dtype != q.dtype:
+        k = k.to(q.dtype)
+    if v.dtype != q.dtype:
+        v = v.to(q.dtype)
+    q = q if q.stride(-1) == 1 and q.stride(1) % 8 == 0 and q.stride(0) % 8 == 0 else q.contiguous()
+    k, v = _row_major_tokens(k), _row_major_tokens(v)
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    cu = _index_tensor(cu_seqlens.reshape(-1), fn, "cu_seqlens")
+    num_seqs = cu.numel() - 1
+    if total == 0 or num_seqs <= 0:
+        return out
+    if max_seqlen is None or max_seqlen <= 0:
+        host = cu.cpu()
+        max_seqlen = int((host[1:] - host[:-1]).max())
+    max_seqlen = max(1, min(int(max_seqlen), total))
+    lib = _lib.load()
+    dt = _DTYPES[q.dtype]
+    ws_n = lib.mkv_varlen_prefill_workspace_bytes(num_seqs, total, max_seqlen, num_kv_heads,
+                                                  head_dim, dt)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
+    with _on_device(dev):
+        st = lib.mkv_varlen_prefill(
+            q.data_ptr(), q.stride(0), q.stride(1), dt, k.data_ptr(), v.data_ptr(), k.stride(0),
+            k.stride(1), v.stride(0), v.stride(1), cu.data_ptr(), _INDEX[cu.dtype], num_seqs, total,
+            max_seqlen, num_heads, num_kv_heads, head_dim, float(scale), out.data_ptr(),
+            out.stride(0), out.stride(1), ws.data_ptr(), ws_n, _stream(dev))
+    _lib.check(fn, st)
+    return out
+
+
 # ---------------------------------------------------------------------------------- module
 class Attention(nn.Module):
     """Attention layer with a paged KV cache (reference attention.py:1617-1807).
@@ -541,6 +590,19 @@ class Attention(nn.Module):
                 store_kvcache(k, v, k_cache, v_cache, context.slot_mapping, self.block_size)
         scale = self.scale / (self.head_dim ** 0.5)
         if context.is_prefill:
+            if getattr(context, "is_full_prefill", False):
+                # every sequence is a whole prompt: attend over the step's own q/k/v, as the
+                # reference does (attention.py:1771), which also serves the runner's
+                # warm-up before the KV cache exists
+                if context.cu_seqlens_q is None:
+                    raise ValueError("cu_seqlens_q must be provided for varlen attention")
+                if k.dim() == 4:
+                    b, n, kvh, d = k.shape
+                    k, v = k.reshape(b * n, kvh, d), v.reshape(b * n, kvh, d)
+                o = flash_attention_prefill(q, k, v, context.cu_seqlens_q, scale, self.num_heads,
+                                            self.num_kv_heads, self.head_dim,
+                                            getattr(context, "max_seqlen_q", 0) or None)
+                return o.reshape(o.shape[0], self.num_heads * self.head_dim)
             return self._prefill(q, k_cache, v_cache, context, scale, mode, quant)
         # The append (if any) was the last kernel launched and writes only the pages (and
         # scales): the decode's prologue may overlap it. Without an append the previous
@@ -568,9 +630,9 @@ class Attention(nn.Module):
                                       self.block_size)
 
     def _prefill(self, q, k_cache, v_cache, context, scale, mode, quant):
-        """Prefill, chunked prefill and extend read the whole visible context from the paged
-        cache (the step's K/V were appended just before), as attention.py:1695-1776 does
-        for its non-full-prefill path; a mixed batch's decode rows go through the decode
+        """Chunked prefill, extend and mixed batches (context.is_full_prefill False) read the
+        whole visible context from the paged cache (the step's K/V were appended just
+        before), as attention.py:1695-1770 does; a mixed batch's decode rows go through the decode
         kernels (1711-1760). Quantised caches are dequantised in the kernel (the reference
         raises NotImplementedError there, 1702-1708)."""
         if context.cu_seqlens_q is None:

@@ -30,4 +30,5 @@ from .kv_oracle import (  # noqa: F401
     store_kvcache_fp8_ref,
     store_kvcache_quant_per_token_head_ref,
     store_kvcache_ref,
+    varlen_prefill_ref,
 )

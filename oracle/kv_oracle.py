@@ -237,6 +237,34 @@ def paged_decode_ref(query, k_cache, v_cache, block_tables, context_lens, scale,
     return out
 
 
+# ------------------------------------------------------------------- contiguous prefill
+def varlen_prefill_ref(query, key, value, cu_seqlens, scale, num_heads, num_kv_heads,
+                       compute_dtype=torch.float64):
+    """flash_attention_prefill (attention.py:446-516) and flash_attention_varlen_kernel
+    (336-443): sequence b owns rows [cu_seqlens[b], cu_seqlens[b+1]) of query / key /
+    value; row m of the sequence attends to the sequence's rows 0..m (mask_causal,
+    :392-393) with kv head h // (num_heads // num_kv_heads) (:357), softmax(scale q.k) v.
+    Returns (total_tokens, num_heads, head_dim) in compute_dtype."""
+    total, _, head_dim = query.shape
+    group = num_heads // num_kv_heads
+    out = torch.empty(total, num_heads, head_dim, dtype=compute_dtype)
+    cu = [int(x) for x in cu_seqlens.reshape(-1).tolist()]
+    for b in range(len(cu) - 1):
+        s, e = cu[b], cu[b + 1]
+        n = e - s
+        if n <= 0:
+            continue
+        q = query[s:e].to(compute_dtype).view(n, num_kv_heads, group, head_dim)
+        k = key[s:e].to(compute_dtype)
+        v = value[s:e].to(compute_dtype)
+        sc = torch.einsum("mhgd,thd->hgmt", q, k) * scale
+        causal = torch.arange(n)[None, :] <= torch.arange(n)[:, None]  # t <= m
+        sc = sc.masked_fill(~causal, float("-inf"))
+        p = torch.softmax(sc, dim=-1)
+        out[s:e] = torch.einsum("hgmt,thd->mhgd", p, v).reshape(n, num_heads, head_dim)
+    return out
+
+
 # ------------------------------------------------------------------- prefill / extend
 def paged_prefill_ref(query, k_cache, v_cache, block_tables, context_lens, cu_seqlens_q,
                       positions, scale, num_heads, num_kv_heads, block_size, k_scale=None,

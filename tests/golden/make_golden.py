@@ -32,6 +32,8 @@ What runs, per fixture (all on the CPU):
   decode_int8      'int8_per_token_head' (the tile kernel, attention.py:1124-1210)
   prefill          paged_attention_prefill_triton (attention.py:852-892; kernel 704-849),
                    chunked prefill over cached prefixes with a -1 page inside one context
+  varlen_prefill   flash_attention_prefill (attention.py:446-516; kernel 336-443), causal
+                   attention of ragged sequences over their own contiguous K/V, fp32
   residual_rmsnorm LayerNorm.residual_rms_forward (layernorm.py:25-27) after a summed
                    all-reduce (linear.py:222-225), run eagerly (see the function)
 """
@@ -328,6 +330,22 @@ def make_residual_rmsnorm(src, rng):
                 eps=np.float64(1e-6), x=_bf16_bits(x), s=_bf16_bits(s), out=_bf16_bits(out))
 
 
+def make_varlen_prefill(ref_attn, rng):
+    import torch
+    H, KVH, D = 4, 2, 32
+    lens = [5, 37, 1, 64, 70]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    T = int(cu[-1])
+    q = rng.standard_normal((T, H, D)).astype(np.float32)
+    k = rng.standard_normal((T, KVH, D)).astype(np.float32)
+    v = rng.standard_normal((T, KVH, D)).astype(np.float32)
+    scale = 1.0 / np.sqrt(D)
+    out = ref_attn.flash_attention_prefill(torch.from_numpy(q), torch.from_numpy(k), torch.from_numpy(v),
+                                           torch.from_numpy(cu), float(scale), H, KVH, D)
+    return dict(query=q, key=k, value=v, cu_seqlens=cu, scale=np.float64(scale),
+                num_heads=np.int64(H), num_kv_heads=np.int64(KVH), out=out.numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", default=os.environ.get("MKV_REFERENCE_SRC"),
@@ -347,6 +365,7 @@ def main():
         ("decode_int8", lambda: make_decode_pth(ref_attn, np.random.default_rng(808), "int8")),
         ("prefill", lambda: make_prefill(ref_attn, np.random.default_rng(909))),
         ("residual_rmsnorm", lambda: make_residual_rmsnorm(args.reference_src, np.random.default_rng(1010))),
+        ("varlen_prefill", lambda: make_varlen_prefill(ref_attn, np.random.default_rng(1111))),
     ]
     only = set(args.only.split(",")) if args.only else None
     for name, job in jobs:

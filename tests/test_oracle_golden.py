@@ -234,3 +234,14 @@ def test_residual_rmsnorm_oracle_matches_reference():
     assert torch.equal(b("partials").float().sum(0).bfloat16(), b("x"))
     assert torch.equal(s, b("s"))
     assert torch.allclose(out.float(), b("out").float(), atol=2e-2, rtol=1e-2)
+
+
+def test_varlen_prefill_oracle_matches_reference():
+    """varlen_prefill_ref against flash_attention_prefill (attention.py:446-516) run by
+    the Triton interpreter on ragged sequences (lengths 5, 37, 1, 64, 70), fp32."""
+    from oracle import varlen_prefill_ref
+    g = golden("varlen_prefill")
+    out = varlen_prefill_ref(torch.from_numpy(g["query"]), torch.from_numpy(g["key"]),
+                             torch.from_numpy(g["value"]), torch.from_numpy(g["cu_seqlens"]),
+                             float(g["scale"]), int(g["num_heads"]), int(g["num_kv_heads"]))
+    assert torch.allclose(out, torch.from_numpy(g["out"]).double(), atol=2e-6, rtol=1e-5)

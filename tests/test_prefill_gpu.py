@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from conftest import golden, mkv_module
-from oracle import paged_prefill_ref
+from oracle import paged_prefill_ref, varlen_prefill_ref
 
 pytestmark = pytest.mark.gpu
 attn = mkv_module("layers.attention")
@@ -213,3 +213,69 @@ def test_prefill_matches_decode_for_last_token(qtiles):
                                       H, KVH, D, BS)
     torch.cuda.synchronize()
     close(out[last.cuda()].cpu(), dec.cpu().double(), torch.bfloat16)
+
+
+# ------------------------------------------------------------ contiguous (full) prefill
+def test_varlen_prefill_golden_fp32():
+    """flash_attention_prefill on the reference's fixture (fp32, CUDA-core path)."""
+    g = golden("varlen_prefill")
+    out = attn.flash_attention_prefill(
+        torch.from_numpy(g["query"]).cuda(), torch.from_numpy(g["key"]).cuda(),
+        torch.from_numpy(g["value"]).cuda(), torch.from_numpy(g["cu_seqlens"]).cuda(),
+        float(g["scale"]), int(g["num_heads"]), int(g["num_kv_heads"]), g["query"].shape[2])
+    assert torch.allclose(out.cpu().double(), torch.from_numpy(g["out"]).double(), atol=2e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("H,KVH,D", [(32, 8, 128), (16, 8, 128), (8, 2, 64)])
+@pytest.mark.parametrize("give_max", [False, True])
+def test_varlen_prefill_against_oracle(dtype, H, KVH, D, give_max):
+    """Ragged whole prompts (1 token, page-boundary lengths, 700) against varlen_prefill_ref,
+    with the longest length read from cu_seqlens or given as an upper bound."""
+    g = torch.Generator().manual_seed(H + D)
+    lens = [1, 128, 129, 700, 37, 256, 5]
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0)), dtype=torch.int32)
+    T = int(cu[-1])
+    q = torch.randn(T, H, D, generator=g).to(dtype)
+    k = torch.randn(T, KVH, D, generator=g).to(dtype)
+    v = torch.randn(T, KVH, D, generator=g).to(dtype)
+    scale = 1.0 / math.sqrt(D)
+    out = attn.flash_attention_prefill(q.cuda(), k.cuda(), v.cuda(), cu.cuda(), scale, H, KVH, D,
+                                       max_seqlen=1024 if give_max else None)
+    ref = varlen_prefill_ref(q, k, v, cu, scale, H, KVH)
+    assert torch.allclose(out.cpu().double(), ref, atol=2e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("mode", ["auto", "fp8_per_tensor", "int8_per_token_head"])
+def test_attention_full_prefill_uses_contiguous_kv(mode):
+    """Attention.forward on a batch of whole prompts (context.is_full_prefill, no block
+    tables, as prepare_prefill sets it without a prefix-cache hit): the output is the
+    causal attention over the step's own q/k/v (attention.py:1771), with the K/V appended
+    to the cache; and with no cache at all (the runner's warm-up) it is the same."""
+    kvc = mkv_module("engine.kv_cache")
+    ctx = mkv_module("utils.context")
+    H, KVH, D, BS = 16, 8, 128, 16
+    lens = [3, 40, 17]
+    cu = torch.tensor([0, 3, 43, 60], dtype=torch.int32)
+    T = 60
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(T, H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, KVH, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, KVH, D, generator=g).to(torch.bfloat16)
+    ref = varlen_prefill_ref(q, k, v, cu, 1.0 / math.sqrt(D), H, KVH)
+    layer = attn.Attention(H, D, scale=1.0, num_kv_heads=KVH, block_size=BS)
+    slots = torch.arange(T, dtype=torch.int64)
+    for with_cache in (False, True):
+        if with_cache:
+            cache = kvc.allocate_kv_cache(1, 8, BS, KVH, D, mode)
+            kvc.bind_kv_cache(layer.modules(), cache)
+        ctx.set_context(True, cu_seqlens_q=cu.cuda(), cu_seqlens_k=cu.cuda(), max_seqlen_q=40,
+                        max_seqlen_k=40, slot_mapping=slots.cuda() if with_cache else None,
+                        is_full_prefill=True)
+        o = layer(q.cuda(), k.cuda(), v.cuda())
+        torch.cuda.synchronize()
+        ctx.reset_context()
+        assert o.shape == (T, H * D)
+        assert torch.allclose(o.view(T, H, D).cpu().double(), ref, atol=2e-2, rtol=1e-2)
+        if with_cache and mode == "auto":  # the step's K/V were appended too
+            assert torch.equal(cache.kv[0, 0].reshape(-1, KVH, D)[:T].cpu(), k)
