@@ -1639,32 +1639,43 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       vt[mt][0] = vld[warp * 32 + mt * 16 + g] != 0;
       vt[mt][1] = vld[warp * 32 + mt * 16 + g + 8] != 0;
     }
-    // kPT: this thread's tokens' K scales and V scales / 2^e (e from the tile's largest)
+    // kPT: this thread's tokens' K scales and V scales / 2^e. O is per warp, so e comes
+    // from the largest V scale of the warp's own 32 tokens (vm < 2^e). e is sticky: it
+    // rises when a tile needs more range and falls only when the tile's bound is more
+    // than 4 binades lower, so O is rarely rescaled, while P * vs / 2^e stays below 2^8
+    // (inside e4m3's range) and within 2^-4 of it for the split's precision.
     float ksv[2][2], vsv[2][2];
     float o_rescale = 1.0f;
     if constexpr (kPT) {
       const float* rs = rs_s + stage * 2 * kF8Tile;
-      float vm = fmaxf(fmaxf(rs[kF8Tile + lane], rs[kF8Tile + 32 + lane]),
-                       fmaxf(rs[kF8Tile + 64 + lane], rs[kF8Tile + 96 + lane]));
-      vm = warp_max(vm);  // every warp finds the same tile maximum
-      // e with vm < 2^e from the exponent field (scales are >= 0), kept in [-126, 126]
-      // so that 2^-e and the power-of-two rescales below are built from bits directly
-      int e = v_exp;
-      const uint32_t vb = __float_as_uint(vm);
-      if (vb != 0u && (vb >> 23) < 0xffu) e = min((int)(vb >> 23) - 126, 126);
-      if (it == 0) v_exp = e;  // O is still zero
-      const int d = max(min(v_exp - e, 127), -126);
-      o_rescale = __uint_as_float((uint32_t)(d + 127) << 23);  // 2^(v_exp - e)
-      v_exp = e;
-      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e
+      float vm = 0.0f;
 #pragma unroll
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
           const int tok = warp * 32 + mt * 16 + g + 8 * rr;
           ksv[mt][rr] = rs[tok];
-          vsv[mt][rr] = rs[kF8Tile + tok] * inv;
+          vsv[mt][rr] = rs[kF8Tile + tok];
+          vm = fmaxf(vm, vsv[mt][rr]);
         }
+      vm = warp_max(vm);
+      // the bound's exponent from the float's exponent field (scales are >= 0), kept in
+      // [-126, 126] so that 2^-e and the power-of-two rescales are built from bits
+      int e = v_exp;
+      const uint32_t vb = __float_as_uint(vm);
+      if (vb != 0u && (vb >> 23) < 0xffu) e = min((int)(vb >> 23) - 126, 126);
+      if (it == 0) {
+        v_exp = e;  // O is still zero
+      } else if (e > v_exp || e < v_exp - 4) {
+        const int d = max(min(v_exp - e, 127), -126);
+        o_rescale = __uint_as_float((uint32_t)(d + 127) << 23);  // 2^(v_exp - e)
+        v_exp = e;
+      }
+      const float inv = __uint_as_float((uint32_t)(127 - v_exp) << 23);  // 2^-v_exp
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) vsv[mt][rr] *= inv;
     }
     uint32_t ph[NT][2], pl[NT][2];
 #pragma unroll
