@@ -353,11 +353,14 @@ MKV_API int mkv_varlen_prefill(
  * k_scales/v_scales (num_blocks, block_size, num_kv_heads) is the per-(token, head)
  * mode of mkv_paged_decode_quant_per_token_head; no scales is mkv_paged_decode.
  * No reference counterpart (the reference launches one Triton kernel per mode).
+ * counters (optional): a caller-kept buffer of at least mkv_paged_decode_counter_bytes(...)
+ *   bytes for the split merge's arrival counters, all zero before its first use and
+ *   used for nothing else. Every decode leaves the counters it touched at zero, so the
+ *   buffer can serve all decodes that are ordered on one stream, whatever their shapes,
+ *   and the call then issues no clearing memset (with counters NULL they live in the
+ *   workspace and are cleared with one cudaMemsetAsync per call). The workspace size
+ *   stays mkv_paged_decode_workspace_bytes(...); its counter part is then unused.
  * flags (bitwise or):
- *   MKV_DECODE_WORKSPACE_ZEROED  the workspace's arrival counters are already zero, so
- *       the call skips clearing them (one cudaMemsetAsync). Every decode leaves them at
- *       zero, so a caller that zeroes its workspace once and keeps it for decodes that
- *       are ordered on one stream may always pass this flag.
  *   MKV_DECODE_OVERLAP_PREVIOUS  programmatic dependent launch: the decode may start
  *       while the previous kernel on the stream still runs. Its prologue (the
  *       schedule's scan of context_lens, the block-table slice, the query rows) then
@@ -366,8 +369,11 @@ MKV_API int mkv_varlen_prefill(
  *       query, block_tables and context_lens, e.g. when it is this library's KV append
  *       of the same step (whose kernels let a dependent start early).
  */
-#define MKV_DECODE_WORKSPACE_ZEROED 1u
 #define MKV_DECODE_OVERLAP_PREVIOUS 2u
+MKV_API size_t mkv_paged_decode_counter_bytes(int32_t num_seqs, int32_t num_heads,
+                                              int32_t num_kv_heads, int32_t head_dim,
+                                              int32_t block_size, int32_t max_num_blocks,
+                                              int32_t num_splits);
 MKV_API int mkv_paged_decode_ex(
     const void* query, int64_t q_stride_seq, int64_t q_stride_head, int32_t q_dtype,
     const void* k_cache, const void* v_cache, int32_t cache_dtype, const float* k_scale,
@@ -376,8 +382,8 @@ MKV_API int mkv_paged_decode_ex(
     int64_t block_table_stride_seq, int32_t max_num_blocks, const void* context_lens,
     int32_t context_lens_index_type, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
     int32_t head_dim, float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
-    void* workspace, size_t workspace_bytes, int32_t num_splits, uint32_t flags,
-    int32_t* invalid_count, void* stream);
+    void* workspace, size_t workspace_bytes, uint32_t* counters, size_t counters_bytes,
+    int32_t num_splits, uint32_t flags, int32_t* invalid_count, void* stream);
 
 /*
  * Paged-attention decode that allocates nothing and needs no workspace argument.

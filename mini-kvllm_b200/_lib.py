@@ -18,7 +18,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_FP8_E4M3, DTYPE_INT8 = 0, 1, 2, 3, 4
 INDEX_I32, INDEX_I64 = 0, 1
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = 0, 1, 2, 3, 4
 FP8_CALIB_WORK_BYTES = 16
-DECODE_WORKSPACE_ZEROED, DECODE_OVERLAP_PREVIOUS = 1, 2
+DECODE_OVERLAP_PREVIOUS = 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
 AR_MAX_RANKS, AR_MAX_BLOCKS, IPC_HANDLE_BYTES = 8, 128, 64
 AR_FLAG_BYTES = AR_MAX_BLOCKS * AR_MAX_RANKS * 4
@@ -53,7 +53,8 @@ SIGNATURES: dict[str, tuple] = {
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _i32, _p, _p]),
     "mkv_paged_decode_ex": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
-        _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, ctypes.c_uint32, _p, _p]),
+        _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _p, _sz, _i32, ctypes.c_uint32, _p, _p]),
+    "mkv_paged_decode_counter_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32, _i32]),
     "mkv_paged_decode_quant_per_token_head": (ctypes.c_int, [
         _p, _i64, _i64, _i32, _p, _p, _i32, _p, _p, _i64, _i32, _p, _i32, _i64, _i32, _p, _i32,
         _i32, _i32, _i32, _i32, _f32, _p, _i64, _i64, _p, _sz, _i32, _p, _p]),

@@ -19,7 +19,8 @@ and NCCL all-reduces. What this script changes, and only at import time in every
     NotImplementedError for chunked prefill over a quantised cache (attention.py:
     1702-1708), so its arm uses kv 'auto' unless told otherwise.
   * the model runs in bf16 (torch.set_default_dtype), as config 5 names; the reference
-    would otherwise build fp32 parameters.
+    would otherwise build fp32 parameters, and its RoPE returns float32 q/k for bf16
+    inputs (a float32 cos/sin cache), so RoPE's outputs are cast back to bf16.
 Workload (config 5, synthetic and seeded): Qwen3-0.6B shape (28 layers, hidden 1024,
 16 Q / 8 KV heads, head_dim 128, MLP 3072, vocab 151936); --requests prompts of random
 token ids with lengths ~ U[128, 1024]; --output tokens each (ignore_eos: random weights
@@ -85,6 +86,18 @@ def random_weights(model, path):  # replaces load_weights_from_checkpoint(model,
 def install(impl: str) -> None:
     """The import-time changes listed in the module docstring (every rank)."""
     torch.set_default_dtype(torch.bfloat16)
+    # The reference's rotary cache is float32 (rotary_embedding.py:89), so a bf16 model's
+    # q/k come out of RoPE as float32 and the float32 attention output then meets the
+    # bf16 o_proj weight: the unmodified engine runs end to end only in float32. Cast
+    # RoPE's outputs back to the input dtype (both arms alike).
+    import myvllm.layers.rotary_embedding as rope
+    rope_forward = rope.RotaryEmbedding.forward
+
+    def rope_same_dtype(self, positions, query, key):
+        q, k = rope_forward(self, positions, query, key)
+        return q.to(query.dtype), k.to(key.dtype)
+
+    rope.RotaryEmbedding.forward = rope_same_dtype
     import myvllm.utils.loader as loader
     loader.load_weights_from_checkpoint = random_weights
     if impl == "ours":

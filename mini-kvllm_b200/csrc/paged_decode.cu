@@ -2093,9 +2093,10 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
                 int bt_type, int64_t bt_sb, int max_blocks, const void* ctx, int ctx_type,
                 int num_seqs, int num_heads, int num_kv_heads, int head_dim, float scale,
                 void* out, int64_t o_sb, int64_t o_sh, void* workspace, size_t ws_bytes,
-                int num_splits, unsigned flags, int32_t* invalid, void* stream) {
+                uint32_t* counters, size_t counters_bytes, int num_splits, unsigned flags,
+                int32_t* invalid, void* stream) {
   clear_error();
-  if (flags & ~(unsigned)(MKV_DECODE_WORKSPACE_ZEROED | MKV_DECODE_OVERLAP_PREVIOUS))
+  if (flags & ~(unsigned)MKV_DECODE_OVERLAP_PREVIOUS)
     return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: unknown flags 0x%x", fn, flags);
   if (num_seqs < 0 || num_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
       max_blocks < 0 || num_blocks < 0 || num_splits < 0)
@@ -2157,11 +2158,18 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   const SplitPlan sp = plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_blocks, num_splits);
   const WorkspaceLayout wl =
       workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits, balanced);
-  if (wl.total > 0 && (workspace == nullptr || ws_bytes < wl.total))
+  // With a caller-kept counter buffer the workspace holds the partials only.
+  const size_t counter_need = wl.total ? wl.total - wl.ctr : 0;
+  const bool own_counters = counters != nullptr && counter_need > 0;
+  const size_t ws_need = own_counters ? wl.ctr : wl.total;
+  if (ws_need > 0 && (workspace == nullptr || ws_bytes < ws_need))
     return set_error(MKV_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn,
-                     wl.total, workspace ? ws_bytes : (size_t)0);
-  if (wl.total > 0 && ((uintptr_t)workspace & 15u))
+                     ws_need, workspace ? ws_bytes : (size_t)0);
+  if (ws_need > 0 && ((uintptr_t)workspace & 15u))
     return set_error(MKV_ERR_INVALID_ARGUMENT, "%s: workspace must be 16-byte aligned", fn);
+  if (own_counters && (counters_bytes < counter_need || ((uintptr_t)counters & 3u)))
+    return set_error(MKV_ERR_WORKSPACE, "%s: counter buffer of %zu bytes (4-byte aligned) needed, %zu given",
+                     fn, counter_need, counters_bytes);
 
   DecodeParams p;
   p.q = query;
@@ -2206,7 +2214,8 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   uint8_t* ws = (uint8_t*)workspace;
   p.part_acc = wl.total ? (float*)(ws + wl.acc) : nullptr;
   p.part_ml = wl.total ? (float*)(ws + wl.ml) : nullptr;
-  p.arrivals = wl.total ? (unsigned int*)(ws + wl.ctr) : nullptr;
+  p.arrivals = wl.total ? (own_counters ? (unsigned int*)counters : (unsigned int*)(ws + wl.ctr))
+                        : nullptr;
   p.invalid = invalid;
   p.pdl = (flags & MKV_DECODE_OVERLAP_PREVIOUS) ? 1 : 0;
 
@@ -2214,9 +2223,9 @@ int decode_impl(const char* fn, const void* query, int64_t q_sb, int64_t q_sh, i
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
   cudaStream_t s = (cudaStream_t)stream;
-  // Arrival counters start at zero. The kernel leaves them at zero, so a caller that
-  // keeps one workspace (zeroed once) for its decodes can skip this clear.
-  if (wl.total && !(flags & MKV_DECODE_WORKSPACE_ZEROED)) {
+  // Arrival counters start at zero. The kernel leaves them at zero, so a caller-kept
+  // counter buffer (zeroed once, used for nothing else) needs no clear.
+  if (wl.total && !own_counters) {
     e = cudaMemsetAsync(ws + wl.ctr, 0, wl.total - wl.ctr, s);
     if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(arrival counters)");
   }
@@ -2356,8 +2365,8 @@ extern "C" int mkv_paged_decode(const void* query, int64_t q_stride_seq, int64_t
                      v_cache, cache_dtype, nullptr, nullptr, nullptr, nullptr, num_blocks,
                      block_size, block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks, context_lens,
                      context_lens_index_type, num_seqs, num_heads, num_kv_heads, head_dim, scale,
-                     out, out_stride_seq, out_stride_head, workspace, workspace_bytes, num_splits,
-                     0u, invalid_count, stream);
+                     out, out_stride_seq, out_stride_head, workspace, workspace_bytes, nullptr, 0,
+                     num_splits, 0u, invalid_count, stream);
 }
 
 extern "C" int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq,
@@ -2377,7 +2386,7 @@ extern "C" int mkv_paged_decode_fp8(const void* query, int64_t q_stride_seq,
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
-                     workspace_bytes, num_splits, 0u, invalid_count, stream);
+                     workspace_bytes, nullptr, 0, num_splits, 0u, invalid_count, stream);
 }
 
 extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
@@ -2416,7 +2425,7 @@ extern "C" int mkv_paged_decode_noalloc(const void* query, int64_t q_stride_seq,
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, scratch,
-                     scratch ? (size_t)MKV_NOALLOC_SCRATCH_BYTES : 0, num_splits, 0u,
+                     scratch ? (size_t)MKV_NOALLOC_SCRATCH_BYTES : 0, nullptr, 0, num_splits, 0u,
                      invalid_count, stream);
 }
 
@@ -2441,7 +2450,7 @@ extern "C" int mkv_paged_decode_quant_per_token_head(
                      block_tables, block_table_index_type, block_table_stride_seq, max_num_blocks,
                      context_lens, context_lens_index_type, num_seqs, num_heads, num_kv_heads,
                      head_dim, scale, out, out_stride_seq, out_stride_head, workspace,
-                     workspace_bytes, num_splits, 0u, invalid_count, stream);
+                     workspace_bytes, nullptr, 0, num_splits, 0u, invalid_count, stream);
 }
 
 extern "C" int mkv_paged_decode_ex(
@@ -2452,8 +2461,8 @@ extern "C" int mkv_paged_decode_ex(
     int64_t block_table_stride_seq, int32_t max_num_blocks, const void* context_lens,
     int32_t context_lens_index_type, int32_t num_seqs, int32_t num_heads, int32_t num_kv_heads,
     int32_t head_dim, float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
-    void* workspace, size_t workspace_bytes, int32_t num_splits, uint32_t flags,
-    int32_t* invalid_count, void* stream) {
+    void* workspace, size_t workspace_bytes, uint32_t* counters, size_t counters_bytes,
+    int32_t num_splits, uint32_t flags, int32_t* invalid_count, void* stream) {
   const char* fn = "mkv_paged_decode_ex";
   clear_error();
   const bool per_token = k_scales != nullptr || v_scales != nullptr;
@@ -2469,6 +2478,23 @@ extern "C" int mkv_paged_decode_ex(
                      k_scales, v_scales, num_blocks, block_size, block_tables,
                      block_table_index_type, block_table_stride_seq, max_num_blocks, context_lens,
                      context_lens_index_type, num_seqs, num_heads, num_kv_heads, head_dim, scale,
-                     out, out_stride_seq, out_stride_head, workspace, workspace_bytes, num_splits,
-                     flags, invalid_count, stream);
+                     out, out_stride_seq, out_stride_head, workspace, workspace_bytes, counters,
+                     counters_bytes, num_splits, flags, invalid_count, stream);
+}
+
+extern "C" size_t mkv_paged_decode_counter_bytes(int32_t num_seqs, int32_t num_heads,
+                                                 int32_t num_kv_heads, int32_t head_dim,
+                                                 int32_t block_size, int32_t max_num_blocks,
+                                                 int32_t num_splits) {
+  if (num_seqs <= 0 || num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads != 0 ||
+      head_dim <= 0 || num_splits < 0)
+    return 0;
+  const int hgs = head_groups_for(num_heads / num_kv_heads);
+  const SplitPlan sp =
+      plan_splits(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, num_splits);
+  const bool balanced =
+      use_balanced(num_seqs, num_kv_heads, hgs, block_size, max_num_blocks, num_splits);
+  const WorkspaceLayout wl =
+      workspace_layout(num_seqs, num_heads, num_kv_heads, head_dim, sp.num_splits, balanced);
+  return wl.total ? wl.total - wl.ctr : 0;
 }

@@ -363,14 +363,11 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
     st_v4(v_cache + dst, quantize16(xv, vs));
   };
 
-  // Destination of a group (-1: nothing to store), counting out-of-range slots once per
-  // token.
+  // Destination of a group: -1 nothing to store (slot -1), -2 out-of-range slot (counted
+  // once per token when the group is stored, never while only loaded).
   auto dest = [&](const Item& it) -> int64_t {
     if (it.slot < 0) return -1;
-    if (it.slot >= num_slots) {
-      if (it.h == 0 && it.g == 0 && invalid != nullptr) atomicAdd(invalid, 1);
-      return -1;
-    }
+    if (it.slot >= num_slots) return (it.h == 0 && it.g == 0) ? -2 : -1;
     return ((it.slot * num_heads + it.h) * groups_per_row + it.g) * 16;
   };
 
@@ -407,7 +404,10 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
     while (true) {
 #pragma unroll
       for (int j = 0; j < GROUPS; ++j) {
-        if (dst[j] < 0) continue;
+        if (dst[j] < 0) {
+          if (dst[j] == -2 && invalid != nullptr) atomicAdd(invalid, 1);
+          continue;
+        }
         if constexpr (kVec) {
           st_v4(k_cache + dst[j], rk[j].quantize(ks));
           st_v4(v_cache + dst[j], rv[j].quantize(vs));

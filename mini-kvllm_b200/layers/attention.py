@@ -271,27 +271,33 @@ def store_kvcache_int8(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Te
 
 # ---------------------------------------------------------------------------------- decode
 _decode_ws: dict[tuple[int, int], torch.Tensor] = {}
+_decode_ctr: dict[tuple[int, int], torch.Tensor] = {}
 
 
-def _decode_workspace(dev: torch.device, stream_ptr: int, nbytes: int):
-    """(workspace, flags) for a decode on `stream_ptr`: one buffer per (device, stream),
-    zeroed when it is allocated. The decode leaves its arrival counters at zero, so
-    decodes ordered on that stream reuse it without clearing it again
-    (MKV_DECODE_WORKSPACE_ZEROED). Inside a CUDA-graph capture a buffer that is too
-    small is not replaced: the call takes a fresh one from the capture's pool and lets
-    the library clear its counters."""
-    if nbytes == 0:
-        return None, _lib.DECODE_WORKSPACE_ZEROED
+def _decode_buffers(dev: torch.device, stream_ptr: int, ws_bytes: int, ctr_bytes: int):
+    """(workspace, counters) for a decode on `stream_ptr`, kept per (device, stream).
+    The counter buffer holds nothing but the split merge's arrival counters: it is zeroed
+    when allocated and every decode leaves it zero, so decodes ordered on that stream
+    share it with no clearing. The workspace holds the partials (no initial value). Inside
+    a CUDA-graph capture a buffer too small is not replaced: the call takes a fresh
+    workspace from the capture's pool and passes no counter buffer, so the library clears
+    the counters in the graph."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     key = (idx, stream_ptr)
-    buf = _decode_ws.get(key)
-    if buf is not None and buf.numel() >= nbytes:
-        return buf, _lib.DECODE_WORKSPACE_ZEROED
+    ws, ctr = _decode_ws.get(key), _decode_ctr.get(key)
+    ws_ok = ws is not None and ws.numel() >= ws_bytes
+    ctr_ok = ctr is not None and ctr.numel() >= ctr_bytes
+    if (ws_ok and ctr_ok) or ws_bytes == 0:
+        return (ws if ws_bytes else None), (ctr if ctr_bytes else None)
     if torch.cuda.is_current_stream_capturing():
-        return torch.empty(nbytes, dtype=torch.uint8, device=dev), 0
-    buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
-    _decode_ws[key] = buf
-    return buf, _lib.DECODE_WORKSPACE_ZEROED
+        return torch.empty(ws_bytes, dtype=torch.uint8, device=dev), None
+    if not ws_ok:
+        ws = torch.empty(max(ws_bytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _decode_ws[key] = ws
+    if not ctr_ok:
+        ctr = torch.zeros(max(ctr_bytes, 64 << 10), dtype=torch.uint8, device=dev)
+        _decode_ctr[key] = ctr
+    return ws, ctr
 
 
 def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, context_lens,
@@ -327,11 +333,12 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
     lib = _lib.load()
     ws_bytes = lib.mkv_paged_decode_workspace_bytes(batch_size, num_heads, num_kv_heads, head_dim,
                                                     block_size, max_num_blocks, num_splits)
+    ctr_bytes = lib.mkv_paged_decode_counter_bytes(batch_size, num_heads, num_kv_heads, head_dim,
+                                                   block_size, max_num_blocks, num_splits)
     with _on_device(dev):
         stream = _stream(dev)
-        ws, flags = _decode_workspace(dev, stream.value or 0, ws_bytes)
-        if overlap_previous and not copied:
-            flags |= _lib.DECODE_OVERLAP_PREVIOUS
+        ws, ctr = _decode_buffers(dev, stream.value or 0, ws_bytes, ctr_bytes)
+        flags = _lib.DECODE_OVERLAP_PREVIOUS if overlap_previous and not copied else 0
         pt = k_scale is not None and not per_token_head  # per-tensor FP8 scales
         st = lib.mkv_paged_decode_ex(
             query.data_ptr(), query.stride(0), query.stride(1), _DTYPES[query.dtype],
@@ -344,7 +351,8 @@ def _decode(fn: str, query, k_cache, v_cache, k_scale, v_scale, block_tables, co
             block_tables.stride(0), max_num_blocks, lens.data_ptr(), _INDEX[lens.dtype],
             batch_size, num_heads, num_kv_heads, head_dim, float(scale), output.data_ptr(),
             output.stride(0), output.stride(1), ws.data_ptr() if ws is not None else None,
-            ws.numel() if ws is not None else 0, num_splits, flags, None, stream)
+            ws.numel() if ws is not None else 0, ctr.data_ptr() if ctr is not None else None,
+            ctr.numel() if ctr is not None else 0, num_splits, flags, None, stream)
     _lib.check(fn, st)
     return output
 

@@ -407,15 +407,41 @@ def fp8_suspended():
     return attn.fp8_calibration_suspended()
 
 
+def test_shared_counter_buffer_across_shapes():
+    """Decodes of different shapes and split counts, back to back on one stream, sharing
+    the wrapper's counter buffer (zeroed once, never cleared again) and workspace: each
+    equals the same decode with the library clearing fresh counters."""
+    lib = mkv_module("_lib").load()
+    cases = [(5, 32, 8, 16, [700, 3, 4000, 1, 128], 0), (3, 8, 2, 256, [9000, 17, 600], 4),
+             (40, 16, 16, 16, [int(x) for x in torch.randint(0, 900, (40,))], 0),
+             (2, 64, 2, 256, [30000, 5], 0), (7, 32, 8, 16, [333] * 7, 2)]
+    for i, (B, H, KVH, BS, lens, splits) in enumerate(cases * 2):
+        w = wl.decode_workload("ctr", B, H, KVH, 128, BS, lens, seed=60 + i, with_append=False)
+        got = attn.paged_attention_decode(w.query, w.k_cache, w.v_cache, w.block_tables,
+                                          w.context_lens, w.scale, H, KVH, 128, BS, num_splits=splits)
+        out = torch.empty_like(w.query)
+        n = lib.mkv_paged_decode_workspace_bytes(B, H, KVH, 128, BS, w.block_tables.shape[1], splits)
+        ws = torch.full((max(n, 1),), 0xAB, dtype=torch.uint8, device="cuda")  # dirty
+        st = lib.mkv_paged_decode(
+            w.query.data_ptr(), w.query.stride(0), w.query.stride(1), 2, w.k_cache.data_ptr(),
+            w.v_cache.data_ptr(), 2, w.k_cache.shape[0], BS, w.block_tables.data_ptr(), 0,
+            w.block_tables.stride(0), w.block_tables.shape[1], w.context_lens.data_ptr(), 1, B, H,
+            KVH, 128, w.scale, out.data_ptr(), out.stride(0), out.stride(1), ws.data_ptr(), n, splits,
+            None, torch.cuda.current_stream().cuda_stream)
+        assert st == 0, lib.mkv_last_error()
+        torch.cuda.synchronize()
+        assert torch.equal(torch.nan_to_num(got, nan=5.0), torch.nan_to_num(out, nan=5.0)), i
+
+
 def test_decode_ex_rejects_bad_arguments():
     lib = mkv_module("_lib").load()
     t = torch.zeros(64, dtype=torch.float32, device="cuda")
     p = t.data_ptr()
     base = [p, 4096, 128, 2, p, p]
-    tail = [1, 16, p, 0, 1, 1, p, 1, 1, 8, 2, 128, 0.1, p, 4096, 128, None, 0, 0]
+    tail = [1, 16, p, 0, 1, 1, p, 1, 1, 8, 2, 128, 0.1, p, 4096, 128, None, 0, None, 0, 0]
     stream = torch.cuda.current_stream().cuda_stream
     # unknown flag bits
-    st = lib.mkv_paged_decode_ex(*base, 2, None, None, None, None, *tail, 8, None, stream)
+    st = lib.mkv_paged_decode_ex(*base, 2, None, None, None, None, *tail, 9, None, stream)
     assert st == mkv_module("_lib").ERR_INVALID_ARGUMENT and b"flags" in lib.mkv_last_error()
     # per-tensor and per-(token, head) scales together
     st = lib.mkv_paged_decode_ex(*base, 3, p, p, p, p, *tail, 0, None, stream)
