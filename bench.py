@@ -79,6 +79,9 @@ def parse_args():
                     help="time eager launches instead of CUDA-graph replays of the step")
     ap.add_argument("--headline-only", action="store_true",
                     help="measure only --config (no config4 / config2 sub-records)")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch the step's decode after the append completes (no programmatic "
+                         "dependent launch)")
     return ap.parse_args()
 
 
@@ -296,7 +299,7 @@ class Replayer:
         self.graphs.clear()
 
 
-def decode_step_fns(attn, w, ks, vs):
+def decode_step_fns(attn, w, ks, vs, overlap=True):
     fp8 = w.fp8
 
     def append(k=None, v=None, slots=None):
@@ -315,6 +318,7 @@ def decode_step_fns(attn, w, ks, vs):
         q = w.query if q is None else q
         bt = w.block_tables if bt is None else bt
         cl = w.context_lens if cl is None else cl
+        after_append = after_append and overlap
         if fp8:
             return attn.paged_attention_decode_quantized(
                 q, w.k_cache, w.v_cache, ks, vs, bt, cl, w.scale, w.num_heads, w.num_kv_heads,
@@ -422,7 +426,7 @@ def measure_decode(args, cfg, rank, world, ranks, replay, attn, lib, headline: b
     vs = w.v_scale.clone() if w.fp8 else None
     splits = lib.mkv_paged_decode_num_splits(w.query.shape[0], w.num_heads, w.num_kv_heads,
                                              w.head_dim, w.block_size, w.block_tables.shape[1])
-    append, decode = decode_step_fns(attn, w, ks, vs)
+    append, decode = decode_step_fns(attn, w, ks, vs, overlap=not args.no_overlap)
 
     def step():
         append()
@@ -635,7 +639,8 @@ def run_ours(args, rank, world, local):
                                    f"rank 0 of a {args.emulate_shard}-way kv-head split, one GPU"
                                    if args.emulate_shard > 1 else "single GPU"),
                    "l2": "working set >> 126 MB L2 (no flush needed)",
-                   "step": "append 1 token/seq + paged decode",
+                   "step": "append 1 token/seq + paged decode" +
+                           ("" if args.no_overlap else " (decode prologue overlaps the append)"),
                    "launch": "eager" if args.eager else
                              "CUDA-graph replay of the step (e2e: one pinned H2D copy, replay, D2H copy per step, "
                              "copies of neighbouring steps overlapped on two copy streams)"},

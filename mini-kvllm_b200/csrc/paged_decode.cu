@@ -1804,6 +1804,9 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
   float* red_l = red_m + 4 * HC;
   float* m_s = red_l + 4 * HC;
   float* l_s = m_s + HC;
+  // kPT: each warp's O is in units of its own 2^v_exp (v_exp in [-126, 126]); it goes
+  // to shared memory in absolute units
+  const float o_unit = kPT ? __uint_as_float((uint32_t)(v_exp + 127) << 23) : 1.0f;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1816,8 +1819,8 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       float* ra = red_acc + (warp * HC + head) * RP;
 #pragma unroll
       for (int j = 0; j < D / 16; ++j) {
-        ra[16 * j + 2 * g] = o[nt][j][e];
-        ra[16 * j + 2 * g + 1] = o[nt][j][e + 2];
+        ra[16 * j + 2 * g] = kPT ? o[nt][j][e] * o_unit : o[nt][j][e];
+        ra[16 * j + 2 * g + 1] = kPT ? o[nt][j][e + 2] * o_unit : o[nt][j][e + 2];
       }
       if (g == 0) {
         red_m[warp * HC + head] = q_ref[nt][e];
@@ -1844,7 +1847,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
 #pragma unroll
     for (int w = 0; w < 4; ++w)
       O = fmaf(exp2f(red_m[w * HC + h] - base), red_acc[(w * HC + h) * RP + d], O);
-    red_acc[h * RP + d] = kPT ? ldexpf(O, v_exp) : O;
+    red_acc[h * RP + d] = O;
   }
   __syncthreads();
   // slots 1-3 of red_acc are free once the warps' results are merged into slot 0

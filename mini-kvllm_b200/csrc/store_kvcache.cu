@@ -46,6 +46,17 @@ inline int per_thread_items(int64_t items) {
   return 1;
 }
 
+// Blocks rounded up to a multiple of the SM count, so that every SM gets the same
+// number of CTAs (the kernels' loops leave surplus threads idle).
+inline int sm_multiple(int blocks) { return (blocks + kNumSMs - 1) / kNumSMs * kNumSMs; }
+
+inline int log2_if_pow2(int64_t x) {
+  if (x <= 0 || (x & (x - 1)) != 0) return -1;
+  int s = 0;
+  while (((int64_t)1 << s) < x) ++s;
+  return s;
+}
+
 // -------------------------------------------------------------------- same-dtype copy
 // CHUNKS 16-byte chunks of K and of V per thread, strided by the grid's thread count:
 // all 2 * CHUNKS loads (and the slot loads) are in flight before the first store.
@@ -56,7 +67,8 @@ store_kv_copy_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict_
                      int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
                      uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
                      const SlotT* __restrict__ slots, int64_t num_slots, uint32_t total,
-                     uint32_t num_heads, uint32_t row_chunks, int32_t* invalid) {
+                     uint32_t num_heads, uint32_t row_chunks, int pt_shift, int rc_shift,
+                     int32_t* invalid) {
   pdl_trigger();  // a dependent decode may begin its prologue now
   const uint32_t per_token = num_heads * row_chunks;
   const uint32_t nthreads = gridDim.x * blockDim.x;
@@ -69,9 +81,10 @@ store_kv_copy_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict_
       const uint32_t i = base + (uint32_t)j * nthreads;
       dst[j] = -1;
       if (i < total) {
-        const uint32_t t = i / per_token;
+        // shifts when the sizes are powers of two (pt_shift / rc_shift >= 0)
+        const uint32_t t = pt_shift >= 0 ? i >> pt_shift : i / per_token;
         const uint32_t rem = i - t * per_token;
-        const uint32_t h = rem / row_chunks;
+        const uint32_t h = rc_shift >= 0 ? rem >> rc_shift : rem / row_chunks;
         const uint32_t c = rem - h * row_chunks;
         const int64_t slot = load_index(slots, (int64_t)t);
         kv[j] = ld_stream_v4(key + (int64_t)t * k_st + (int64_t)h * k_sh + c * 16u);
@@ -262,17 +275,46 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   return (uint32_t)r;
 }
 
-__device__ __forceinline__ float clamp_quotient(float x, float scale) {
-  return fminf(fmaxf(x / scale, -448.0f), 448.0f);  // NaN -> -448, as quantize_e4m3
+// Division by one scale, correctly rounded like IEEE x / scale, in one multiply and two
+// FMAs per element (Markstein's method): y = RN(1 / scale) is taken once by IEEE
+// division; q = RN(x * y) is then within about an ulp of x / scale, the remainder
+// r = x - q * scale is exact in an FMA, and RN(q + r * y) is the correctly rounded
+// quotient. Only quotients of magnitude in [2^-60, 2^60] are corrected: outside it (and
+// for infinities and NaN) the e4m3 byte after the +-448 clamp depends on q's sign and
+// magnitude class alone. A scale that is not a normal number, or whose reciprocal is
+// not, takes the division itself. Tests compare the bytes with IEEE division at every
+// e4m3 rounding midpoint for many scales.
+struct ScaleDiv {
+  float s, y;
+  bool fast;
+  __device__ __forceinline__ explicit ScaleDiv(float scale) : s(scale) {
+    y = 1.0f / scale;
+    const float as = fabsf(scale), ay = fabsf(y);
+    fast = as >= 0x1p-126f && as <= 0x1p126f && ay >= 0x1p-126f && ay <= 0x1p126f;
+  }
+  __device__ __forceinline__ float operator()(float x) const {
+    if (!fast) return x / s;
+    float q = __fmul_rn(x, y);
+    const float aq = fabsf(q);
+    if (aq >= 0x1p-60f && aq <= 0x1p60f) {
+      const float r = fmaf(-q, s, x);
+      if (r != 0.0f) q = fmaf(r, y, q);
+    }
+    return q;
+  }
+};
+
+__device__ __forceinline__ float clamp_quotient(float x, const ScaleDiv& d) {
+  return fminf(fmaxf(d(x), -448.0f), 448.0f);  // NaN -> -448, as quantize_e4m3
 }
 
 // 16 elements quantised with one scale, packed as 16 e4m3 bytes (element 0 lowest).
-__device__ __forceinline__ uint4 quantize16(const float (&x)[16], float scale) {
+__device__ __forceinline__ uint4 quantize16(const float (&x)[16], const ScaleDiv& d) {
   uint32_t w[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    w[i] = e4m3x2(clamp_quotient(x[4 * i], scale), clamp_quotient(x[4 * i + 1], scale)) |
-           (e4m3x2(clamp_quotient(x[4 * i + 2], scale), clamp_quotient(x[4 * i + 3], scale)) << 16);
+    w[i] = e4m3x2(clamp_quotient(x[4 * i], d), clamp_quotient(x[4 * i + 1], d)) |
+           (e4m3x2(clamp_quotient(x[4 * i + 2], d), clamp_quotient(x[4 * i + 3], d)) << 16);
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -291,12 +333,12 @@ template <typename T> struct Raw16 {
     for (int j = 0; j < 16; ++j) x[j] = at(j);
   }
   // the 16 elements quantised with one scale as 16 e4m3 bytes, converted pair by pair
-  __device__ __forceinline__ uint4 quantize(float scale) const {
+  __device__ __forceinline__ uint4 quantize(const ScaleDiv& d) const {
     uint32_t q[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      q[i] = e4m3x2(clamp_quotient(at(4 * i), scale), clamp_quotient(at(4 * i + 1), scale)) |
-             (e4m3x2(clamp_quotient(at(4 * i + 2), scale), clamp_quotient(at(4 * i + 3), scale)) << 16);
+      q[i] = e4m3x2(clamp_quotient(at(4 * i), d), clamp_quotient(at(4 * i + 1), d)) |
+             (e4m3x2(clamp_quotient(at(4 * i + 2), d), clamp_quotient(at(4 * i + 3), d)) << 16);
     return make_uint4(q[0], q[1], q[2], q[3]);
   }
 };
@@ -351,8 +393,8 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
     for (int j = 0; j < 16; ++j) x[j] = to_f32(e[j]);
   };
   // quantise + store one group whose values are in xk / xv
-  auto store_group = [&](const Item& it, const float (&xk)[16], const float (&xv)[16], float ks,
-                         float vs, bool count_invalid) {
+  auto store_group = [&](const Item& it, const float (&xk)[16], const float (&xv)[16],
+                         const ScaleDiv& ks, const ScaleDiv& vs, bool count_invalid) {
     if (it.slot < 0) return;  // -1: nothing to store for this token
     if (it.slot >= num_slots) {
       if (count_invalid && it.h == 0 && it.g == 0 && invalid != nullptr) atomicAdd(invalid, 1);
@@ -401,6 +443,7 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
   const bool need_v = work != nullptr && vs == 1.0f;
 
   if (!need_k && !need_v) {  // ------------------------------------ steady state
+    const ScaleDiv kd(ks), vd(vs);
     while (true) {
 #pragma unroll
       for (int j = 0; j < GROUPS; ++j) {
@@ -409,13 +452,13 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
           continue;
         }
         if constexpr (kVec) {
-          st_v4(k_cache + dst[j], rk[j].quantize(ks));
-          st_v4(v_cache + dst[j], rv[j].quantize(vs));
+          st_v4(k_cache + dst[j], rk[j].quantize(kd));
+          st_v4(v_cache + dst[j], rv[j].quantize(vd));
         } else {
           float xk[16], xv[16];
           load_vals(src_k(it1), xk);
           load_vals(src_v(it1), xv);
-          store_group(it1, xk, xv, ks, vs, false);
+          store_group(it1, xk, xv, kd, vd, false);
         }
       }
       base += nthreads * GROUPS;
@@ -499,8 +542,10 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
     new_scale[1] = sv;
   }
   __syncthreads();
-  const float sk = new_scale[0], sv = new_scale[1];
-  for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {  // this CTA stores the batch
+  const ScaleDiv kd(new_scale[0]), vd(new_scale[1]);
+  // This CTA stores the batch. One group per thread in flight keeps the kernel at the
+  // steady state's 64 registers; the single-CTA store is paid on the first call only.
+  for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {
     Item c;
     locate(i, c);
     float xk[16], xv[16];
@@ -514,7 +559,7 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
       load_vals(src_k(c), xk);
       load_vals(src_v(c), xv);
     }
-    store_group(c, xk, xv, sk, sv, true);
+    store_group(c, xk, xv, kd, vd, true);
   }
 }
 
@@ -528,12 +573,14 @@ __device__ __forceinline__ int8_t quantize_int8(float x, float inv) {
   return (int8_t)__float2int_rz(q);
 }
 
-// One group of LPR lanes (a power of two >= head_dim / 16) per (token, kv head) row:
-// each lane loads 16 elements of K and of V, the group reduces the row's amax with
-// shuffles, and each lane writes its 16 quantised bytes; lane 0 of the group writes
-// the row's two scales. The loop is warp-uniform so that every lane takes part in the
-// shuffles.
-template <typename T, bool kInt8, typename SlotT>
+// One group of LPR lanes (a power of two >= head_dim / 16) per (token, kv head) row; each
+// lane group takes ROWS rows per loop step, ROWS rows apart in the grid's row order (the
+// grid covers rows / ROWS groups). Each lane loads 16 elements of K and of V of every
+// row first (all 4 * ROWS * 16-byte loads in flight), then per row and tensor the group
+// reduces the amax with shuffles and each lane writes its 16 quantised bytes; lane 0 of
+// the group writes the row's scales. The loop is warp-uniform so that every lane takes
+// part in the shuffles.
+template <typename T, bool kInt8, typename SlotT, int ROWS>
 __global__ void __launch_bounds__(kStoreThreads)
 store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
                     int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
@@ -547,79 +594,87 @@ store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__
   const int lane = threadIdx.x & 31;
   const int sub = lane & (lpr - 1);
   const int64_t rows = num_tokens * num_heads;
-  const int64_t step = ((int64_t)gridDim.x * blockDim.x) >> lpr_shift;
+  const int64_t groups = ((int64_t)gridDim.x * blockDim.x) >> lpr_shift;  // lane groups
+  const int64_t step = groups * ROWS;
   for (int64_t r0 = ((int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31)) >> lpr_shift;
        r0 < rows; r0 += step) {
-    const int64_t row = r0 + (lane >> lpr_shift);
-    int64_t t = 0, slot = -1;
-    int h = 0;
-    if (row < rows) {
-      t = row / num_heads;
-      h = (int)(row - t * num_heads);
-      slot = load_index(slots, t);
-      if (slot >= num_slots && h == 0 && sub == 0 && invalid != nullptr) atomicAdd(invalid, 1);
-    }
-    const bool ok = row < rows && slot >= 0 && slot < num_slots;
-    const bool has = ok && sub < groups_per_row;
-    const int64_t src_off = (int64_t)sub * 16 * (int64_t)sizeof(T);
-    const int64_t dst = ((slot * num_heads + h) * groups_per_row + sub) * 16;
-    // K and V of the lane's 16 elements: all loads in flight before either reduction
-    float xs[2][16];
-    if (has) {
-      const uint8_t* pk = key + t * k_st + h * k_sh + src_off;
-      const uint8_t* pv = value + t * v_st + h * v_sh + src_off;
-      if (vec) {
-        Raw16<T> a, b;
-        a.load(pk);
-        b.load(pv);
-        a.get(xs[0]);
-        b.get(xs[1]);
-      } else {
-        load16<T>(pk, false, xs[0]);
-        load16<T>(pv, false, xs[1]);
+    int64_t slot[ROWS], dst[ROWS];
+    bool ok[ROWS], has[ROWS];
+    int hh[ROWS];
+    const uint8_t* src[ROWS][2];
+    Raw16<T> raw[ROWS][2];  // vector form: converted only when the row is processed
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j) {
+      const int64_t row = r0 + (lane >> lpr_shift) + (int64_t)j * groups;
+      int64_t t = 0;
+      int h = 0;
+      slot[j] = -1;
+      if (row < rows) {
+        t = row / num_heads;
+        h = (int)(row - t * num_heads);
+        slot[j] = load_index(slots, t);
+        if (slot[j] >= num_slots && h == 0 && sub == 0 && invalid != nullptr) atomicAdd(invalid, 1);
+      }
+      hh[j] = h;
+      ok[j] = row < rows && slot[j] >= 0 && slot[j] < num_slots;
+      has[j] = ok[j] && sub < groups_per_row;
+      dst[j] = ((slot[j] * num_heads + h) * groups_per_row + sub) * 16;
+      const int64_t src_off = (int64_t)sub * 16 * (int64_t)sizeof(T);
+      src[j][0] = key + t * k_st + h * k_sh + src_off;
+      src[j][1] = value + t * v_st + h * v_sh + src_off;
+      if (has[j] && vec) {
+        raw[j][0].load(src[j][0]);
+        raw[j][1].load(src[j][1]);
       }
     }
 #pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const float (&x)[16] = xs[which];
-      float amax = 0.0f;
-      int nan = 0;
-      if (has) {
+    for (int j = 0; j < ROWS; ++j) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float a = fabsf(x[j]);
-          nan |= isnan(a) ? 1 : 0;
-          amax = fmaxf(amax, a);
+      for (int which = 0; which < 2; ++which) {
+        float x[16];
+        if (has[j]) {
+          if (vec) raw[j][which].get(x);
+          else load16<T>(src[j][which], false, x);
         }
-      }
-      for (int o = 1; o < lpr; o <<= 1) {
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        nan |= __shfl_xor_sync(0xffffffffu, nan, o);
-      }
-      float scale;
-      if (kInt8) {
-        scale = nan ? 1e-6f : fmaxf(amax / 127.0f, 1e-6f);
-      } else {
-        scale = (!nan && amax > 0.0f) ? amax / 448.0f : 1.0f;
-      }
-      if (has) {
-        uint4 packed;
+        float amax = 0.0f;
+        int nan = 0;
+        if (has[j]) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float a = fabsf(x[e]);
+            nan |= isnan(a) ? 1 : 0;
+            amax = fmaxf(amax, a);
+          }
+        }
+        for (int o = 1; o < lpr; o <<= 1) {
+          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+          nan |= __shfl_xor_sync(0xffffffffu, nan, o);
+        }
+        float scale;
         if (kInt8) {
-          const float inv = 1.0f / scale;
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            w[i] = (uint32_t)(uint8_t)quantize_int8(x[4 * i + 0], inv) |
-                   ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 1], inv) << 8) |
-                   ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 2], inv) << 16) |
-                   ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 3], inv) << 24);
-          packed = make_uint4(w[0], w[1], w[2], w[3]);
+          scale = nan ? 1e-6f : fmaxf(amax / 127.0f, 1e-6f);
         } else {
-          packed = quantize16(x, scale);
+          scale = (!nan && amax > 0.0f) ? amax / 448.0f : 1.0f;
         }
-        st_v4((which == 0 ? k_cache : v_cache) + dst, packed);
+        if (has[j]) {
+          uint4 packed;
+          if (kInt8) {
+            const float inv = 1.0f / scale;
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = (uint32_t)(uint8_t)quantize_int8(x[4 * i + 0], inv) |
+                     ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 1], inv) << 8) |
+                     ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 2], inv) << 16) |
+                     ((uint32_t)(uint8_t)quantize_int8(x[4 * i + 3], inv) << 24);
+            packed = make_uint4(w[0], w[1], w[2], w[3]);
+          } else {
+            packed = quantize16(x, ScaleDiv(scale));
+          }
+          st_v4((which == 0 ? k_cache : v_cache) + dst[j], packed);
+        }
+        if (ok[j] && sub == 0) (which == 0 ? k_scales : v_scales)[slot[j] * num_heads + hh[j]] = scale;
       }
-      if (ok && sub == 0) (which == 0 ? k_scales : v_scales)[slot * num_heads + h] = scale;
     }
   }
 }
@@ -740,12 +795,14 @@ int launch_store(const void* key, const void* value, int64_t k_st, int64_t k_sh,
   if (vec && chunks < ((int64_t)1 << 31)) {
     const uint32_t row_chunks = (uint32_t)(row_bytes / 16);
     const int per = per_thread_items(chunks);
-    const int grid = grid_for((chunks + per - 1) / per, kStoreThreads);
+    const int grid = sm_multiple(grid_for((chunks + per - 1) / per, kStoreThreads));
+    const int pt_shift = log2_if_pow2((int64_t)num_heads * row_chunks);
+    const int rc_shift = log2_if_pow2(row_chunks);
 #define MKV_COPY(C)                                                                            \
   store_kv_copy_kernel<SlotT, C><<<grid, kStoreThreads, 0, stream>>>(                         \
       (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb, \
       (uint8_t*)k_cache, (uint8_t*)v_cache, slots, num_slots, (uint32_t)chunks,               \
-      (uint32_t)num_heads, row_chunks, invalid)
+      (uint32_t)num_heads, row_chunks, pt_shift, rc_shift, invalid)
     if (per == 4) MKV_COPY(4);
     else if (per == 2) MKV_COPY(2);
     else MKV_COPY(1);
@@ -794,7 +851,7 @@ int launch_store_fp8(const void* key, const void* value, int64_t k_st, int64_t k
     return cuda_status(cudaGetLastError(), "store_kvcache_fp8 launch");
   }
   const int per = vec ? (per_thread_items(total) >= 2 ? 2 : 1) : 1;
-  const int grid = grid_for((total + per - 1) / per, kStoreThreads);
+  const int grid = sm_multiple(grid_for((total + per - 1) / per, kStoreThreads));
 #define MKV_FP8(G, V)                                                                            \
   store_kv_fp8_calib_kernel<T, SlotT, G, V><<<grid, kStoreThreads, 0, stream>>>(                \
       (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,   \
@@ -819,8 +876,11 @@ int launch_store_pth(const void* key, const void* value, int64_t k_st, int64_t k
   const int groups = head_dim / 16;
   int lpr_shift = 0;
   while ((1 << lpr_shift) < groups) ++lpr_shift;
-  const int grid = grid_for(num_tokens * num_heads << lpr_shift, kStoreThreads);
-  store_kv_pth_kernel<T, kInt8, SlotT><<<grid, kStoreThreads, 0, stream>>>(
+  // One row per lane group: two rows per group (the kernel's ROWS) keeps as many bytes
+  // in flight per SM but needs ~90 registers, so half as many CTAs fit.
+  const int64_t lanes = (num_tokens * num_heads) << lpr_shift;
+  const int grid = sm_multiple(grid_for(lanes, kStoreThreads));
+  store_kv_pth_kernel<T, kInt8, SlotT, 1><<<grid, kStoreThreads, 0, stream>>>(
       (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,
       (uint8_t*)k_cache, (uint8_t*)v_cache, k_scales, v_scales, slots, num_slots, num_tokens,
       num_heads, groups, lpr_shift, vec, invalid);

@@ -1,5 +1,7 @@
 """KV append on the GPU through the C ABI (Python wrappers) against the CPU oracle:
 bf16/fp16/fp32 copies and FP8 E4M3 quantisation must be bit-exact."""
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -339,3 +341,57 @@ def test_fp8_one_launch_equals_calibrate_then_store(T, sentinel):
     sl[sl >= NB * BS] = -1
     store_kvcache_fp8_ref(key.cpu(), value.cpu(), ek, ev, torch.tensor([ks1]), torch.tensor([vs1]), sl, BS)
     assert torch.equal(k1, ek.view(torch.uint8)) and torch.equal(v1, ev.view(torch.uint8))
+
+
+def _e4m3_midpoints():
+    """Every rounding midpoint between consecutive finite e4m3 magnitudes (0 .. 448)."""
+    vals = sorted(set(torch.arange(0, 0x7F, dtype=torch.uint8).view(torch.float8_e4m3fn).float().tolist()))
+    return torch.tensor([(a + b) / 2 for a, b in zip(vals, vals[1:])], dtype=torch.float64)
+
+
+def _scales_for_midpoint_test():
+    g = torch.Generator().manual_seed(77)
+    rnd = (torch.rand(24, generator=g, dtype=torch.float64) * 12 - 9).exp2()  # 2^-9 .. 2^3
+    s = rnd.float().tolist()
+    s += rnd.to(torch.bfloat16).float().tolist()  # calibrated scales are bf16 values
+    s += [2.0 ** k for k in (-7, -3, 0, 2)]
+    s += [float(torch.tensor(1.0 - 2.0 ** -24, dtype=torch.float32)) * 2.0 ** k for k in (-6, 0, 1)]
+    s += [float(torch.tensor(1.0 + 2.0 ** -23, dtype=torch.float32)) * 2.0 ** k for k in (-4, 0)]
+    s += [0.1865234375, 0.169921875, 3.0e-3, 7.0 / 3.0]
+    return s
+
+
+@pytest.mark.parametrize("key_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_fp8_quantiser_at_rounding_midpoints(key_dtype):
+    """The quantiser's quotient x / scale is correctly rounded where it matters: for many
+    scales, inputs whose quotients fall on or within three ulp of every e4m3 rounding
+    midpoint (float32 keys), and every finite bf16 / fp16 value (16-bit keys), with both
+    signs, zeros, infinities and NaN, give the oracle's bytes (IEEE division)."""
+    mids = _e4m3_midpoints()
+    for s in _scales_for_midpoint_test():
+        if key_dtype == torch.float32:
+            base = (torch.cat([mids, -mids]) * s).float()
+            xs = [base]
+            lo = hi = base
+            for _ in range(3):
+                lo = torch.nextafter(lo, torch.full_like(lo, -math.inf))
+                hi = torch.nextafter(hi, torch.full_like(hi, math.inf))
+                xs += [lo, hi]
+            x = torch.cat(xs + [torch.tensor([0.0, -0.0, math.inf, -math.inf, math.nan, 1e-30, -1e30])])
+        else:
+            bits = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16)
+            x = bits.view(key_dtype).float()
+        n = x.numel()
+        T = (n + 15) // 16
+        x = torch.cat([x, torch.zeros(T * 16 - n)]).to(key_dtype).view(T, 1, 16)
+        slots = torch.arange(T, dtype=torch.int64)
+        kc = torch.zeros(T, 1, 1, 16, dtype=torch.float8_e4m3fn, device="cuda")
+        vc = torch.zeros_like(kc)
+        sc = torch.tensor([s], dtype=torch.float32, device="cuda")
+        with attn.fp8_calibration_suspended():  # a scale of exactly 1.0 is not recalibrated
+            attn.store_kvcache_fp8(x.cuda(), x.cuda(), kc, vc, sc, sc.clone(), slots.cuda(), 1,
+                                   "fp8_per_tensor")
+        want = quantize_fp8_ref(x.float(), float(sc)).view(torch.uint8)
+        got = kc.cpu().view(torch.uint8).view(T, 1, 16)
+        bad = got != want
+        assert not bad.any(), (s, x.float()[bad][:5].tolist(), got[bad][:5].tolist(), want[bad][:5].tolist())
