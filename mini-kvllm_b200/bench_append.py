@@ -9,14 +9,14 @@ with 0.1 % outliers x20. The tokens are 16 prefill chunks of 128 consecutive slo
 Each mode is one append call through the Python API:
 - bf16: store_kvcache into bf16 pages;
 - fp8_per_tensor: store_kvcache_fp8, with the scale calibrated by the first (untimed)
-  call. A timed call runs the calibration kernel, which reads the scale and returns,
-  then the quantising store;
+  call. A timed call is one launch that reads the (frozen) scale and quantises;
 - fp8_per_token_head / int8_per_token_head: one scale per (token, head) row, written
   beside the pages.
 
 The working set (~34 MB) fits in the 126 MB L2. So a 512 MB buffer is written before
-every timed call, and only the call sits between its CUDA events. The mean over
-`--iters` calls is reported.
+every timed call, and only the call sits between its CUDA events (the Python launch
+included; bench.py's config2 record times graph replays instead). The mean over
+`--iters` calls is reported. Used for ncu captures of the append kernels.
 
 Algorithmic bytes per call:
 - read: K and V in bf16, plus the int64 slots;
