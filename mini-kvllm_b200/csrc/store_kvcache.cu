@@ -276,45 +276,59 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
 }
 
 // Division by one scale, correctly rounded like IEEE x / scale, in one multiply and two
-// FMAs per element (Markstein's method): y = RN(1 / scale) is taken once by IEEE
-// division; q = RN(x * y) is then within about an ulp of x / scale, the remainder
-// r = x - q * scale is exact in an FMA, and RN(q + r * y) is the correctly rounded
-// quotient. Only quotients of magnitude in [2^-60, 2^60] are corrected: outside it (and
-// for infinities and NaN) the e4m3 byte after the +-448 clamp depends on q's sign and
-// magnitude class alone. A scale that is not a normal number, or whose reciprocal is
-// not, takes the division itself. Tests compare the bytes with IEEE division at every
-// e4m3 rounding midpoint for many scales.
+// FMAs (Markstein's method), two quotients at a time with the packed fp32 instructions:
+// y = RN(1 / scale) is taken once by IEEE division; q = RN(x * y) is then within about
+// an ulp of x / scale, the remainder r = x - q * scale is exact in an FMA, and
+// RN(q + r * y) is the correctly rounded quotient. The quantiser needs it only up to the
+// e4m3 range, so q is first clamped to [-464, 464] (beyond 448 every value saturates to
+// +-448 anyway): infinities, overflows and NaN then need no branch (a NaN x keeps a NaN
+// remainder and ends at -448 like the reference), and copysign restores the sign of an
+// exact zero quotient. A scale that is not a normal number, or whose reciprocal is not,
+// takes the IEEE division itself (a branch per 16 elements, uniform for a call). Tests
+// compare the bytes with IEEE division at every e4m3 rounding midpoint for many scales.
 struct ScaleDiv {
   float s, y;
+  uint64_t y2, ns2;  // (y, y) and (-s, -s) for the packed instructions
   bool fast;
   __device__ __forceinline__ explicit ScaleDiv(float scale) : s(scale) {
     y = 1.0f / scale;
     const float as = fabsf(scale), ay = fabsf(y);
     fast = as >= 0x1p-126f && as <= 0x1p126f && ay >= 0x1p-126f && ay <= 0x1p126f;
+    y2 = f2_pack(y, y);
+    ns2 = f2_pack(-scale, -scale);
   }
-  __device__ __forceinline__ float operator()(float x) const {
-    if (!fast) return x / s;
-    float q = __fmul_rn(x, y);
-    const float aq = fabsf(q);
-    if (aq >= 0x1p-60f && aq <= 0x1p60f) {
-      const float r = fmaf(-q, s, x);
-      if (r != 0.0f) q = fmaf(r, y, q);
+  // clamp(x / scale, -448, 448) for two elements, correctly rounded before the clamp
+  __device__ __forceinline__ void clamped2(float x0, float x1, float& c0, float& c1) const {
+    if (!fast) {
+      c0 = fminf(fmaxf(x0 / s, -448.0f), 448.0f);
+      c1 = fminf(fmaxf(x1 / s, -448.0f), 448.0f);
+      return;
     }
-    return q;
+    const uint64_t x2 = f2_pack(x0, x1);
+    float q0, q1;
+    f2_unpack(f2_mul(x2, y2), q0, q1);
+    const float a0 = fminf(fmaxf(q0, -464.0f), 464.0f), a1 = fminf(fmaxf(q1, -464.0f), 464.0f);
+    const uint64_t a2 = f2_pack(a0, a1);
+    const uint64_t r2 = f2_fma(a2, ns2, x2);  // x - a * scale, exact
+    float b0, b1;
+    f2_unpack(f2_fma(r2, y2, a2), b0, b1);
+    b0 = copysignf(b0, q0);
+    b1 = copysignf(b1, q1);
+    c0 = fminf(fmaxf(b0, -448.0f), 448.0f);  // NaN -> -448, as quantize_e4m3
+    c1 = fminf(fmaxf(b1, -448.0f), 448.0f);
   }
 };
-
-__device__ __forceinline__ float clamp_quotient(float x, const ScaleDiv& d) {
-  return fminf(fmaxf(d(x), -448.0f), 448.0f);  // NaN -> -448, as quantize_e4m3
-}
 
 // 16 elements quantised with one scale, packed as 16 e4m3 bytes (element 0 lowest).
 __device__ __forceinline__ uint4 quantize16(const float (&x)[16], const ScaleDiv& d) {
   uint32_t w[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-    w[i] = e4m3x2(clamp_quotient(x[4 * i], d), clamp_quotient(x[4 * i + 1], d)) |
-           (e4m3x2(clamp_quotient(x[4 * i + 2], d), clamp_quotient(x[4 * i + 3], d)) << 16);
+  for (int i = 0; i < 4; ++i) {
+    float c0, c1, c2, c3;
+    d.clamped2(x[4 * i], x[4 * i + 1], c0, c1);
+    d.clamped2(x[4 * i + 2], x[4 * i + 3], c2, c3);
+    w[i] = e4m3x2(c0, c1) | (e4m3x2(c2, c3) << 16);
+  }
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
@@ -336,9 +350,12 @@ template <typename T> struct Raw16 {
   __device__ __forceinline__ uint4 quantize(const ScaleDiv& d) const {
     uint32_t q[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      q[i] = e4m3x2(clamp_quotient(at(4 * i), d), clamp_quotient(at(4 * i + 1), d)) |
-             (e4m3x2(clamp_quotient(at(4 * i + 2), d), clamp_quotient(at(4 * i + 3), d)) << 16);
+    for (int i = 0; i < 4; ++i) {
+      float c0, c1, c2, c3;
+      d.clamped2(at(4 * i), at(4 * i + 1), c0, c1);
+      d.clamped2(at(4 * i + 2), at(4 * i + 3), c2, c3);
+      q[i] = e4m3x2(c0, c1) | (e4m3x2(c2, c3) << 16);
+    }
     return make_uint4(q[0], q[1], q[2], q[3]);
   }
 };
@@ -367,7 +384,8 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
                           uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
                           float* k_scale, float* v_scale, const SlotT* __restrict__ slots,
                           int64_t num_slots, uint32_t total, uint32_t num_heads,
-                          uint32_t groups_per_row, CalibWork* work, int32_t* invalid) {
+                          uint32_t groups_per_row, int pt_shift, int gr_shift, CalibWork* work,
+                          int32_t* invalid) {
   pdl_trigger();  // a dependent decode may begin its prologue now
   const uint32_t per_token = num_heads * groups_per_row;
   const uint32_t nthreads = gridDim.x * blockDim.x;
@@ -378,10 +396,10 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
     int64_t slot;
     uint32_t t, h, g;
   };
-  auto locate = [&](uint32_t i, Item& it) {
-    it.t = i / per_token;
+  auto locate = [&](uint32_t i, Item& it) {  // shifts when the sizes are powers of two
+    it.t = pt_shift >= 0 ? i >> pt_shift : i / per_token;
     const uint32_t rem = i - it.t * per_token;
-    it.h = rem / groups_per_row;
+    it.h = gr_shift >= 0 ? rem >> gr_shift : rem / groups_per_row;
     it.g = rem - it.h * groups_per_row;
     it.slot = load_index(slots, (int64_t)it.t);
   };
@@ -474,9 +492,9 @@ store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __rest
   float mk = 0.0f, mv = 0.0f;
   for (uint32_t i = tid0; i < total; i += nthreads) {
     Item c;
-    c.t = i / per_token;
+    c.t = pt_shift >= 0 ? i >> pt_shift : i / per_token;
     const uint32_t rem = i - c.t * per_token;
-    c.h = rem / groups_per_row;
+    c.h = gr_shift >= 0 ? rem >> gr_shift : rem / groups_per_row;
     c.g = rem - c.h * groups_per_row;
     float xk[16], xv[16];
     if constexpr (kVec) {
@@ -581,7 +599,7 @@ __device__ __forceinline__ int8_t quantize_int8(float x, float inv) {
 // the group writes the row's scales. The loop is warp-uniform so that every lane takes
 // part in the shuffles.
 template <typename T, bool kInt8, typename SlotT, int ROWS>
-__global__ void __launch_bounds__(kStoreThreads)
+__global__ void __launch_bounds__(kStoreThreads, 4)
 store_kv_pth_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
                     int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
                     uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
@@ -852,11 +870,13 @@ int launch_store_fp8(const void* key, const void* value, int64_t k_st, int64_t k
   }
   const int per = vec ? (per_thread_items(total) >= 2 ? 2 : 1) : 1;
   const int grid = sm_multiple(grid_for((total + per - 1) / per, kStoreThreads));
+  const int pt_shift = log2_if_pow2((int64_t)num_heads * groups);
+  const int gr_shift = log2_if_pow2(groups);
 #define MKV_FP8(G, V)                                                                            \
   store_kv_fp8_calib_kernel<T, SlotT, G, V><<<grid, kStoreThreads, 0, stream>>>(                \
       (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,   \
       (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale, slots, num_slots, (uint32_t)total, \
-      (uint32_t)num_heads, (uint32_t)groups, work, invalid)
+      (uint32_t)num_heads, (uint32_t)groups, pt_shift, gr_shift, work, invalid)
   if (!vec) MKV_FP8(1, false);
   else if (per == 2) MKV_FP8(2, true);
   else MKV_FP8(1, true);
