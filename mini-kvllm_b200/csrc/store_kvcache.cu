@@ -267,8 +267,9 @@ struct CalibWork {  // MKV_FP8_CALIB_WORK_BYTES bytes, zero between calls
 };
 static_assert(sizeof(CalibWork) == MKV_FP8_CALIB_WORK_BYTES, "calibration work layout");
 
-// Two clamped quotients (finite, within +-448) as e4m3 bytes, element `lo` in the low
-// byte: one saturating round-to-nearest-even conversion for the pair.
+// Two quotients as e4m3 bytes, element `lo` in the low byte: one round-to-nearest-even
+// conversion for the pair that saturates finite values beyond +-448 and infinities to
+// +-448 (NaN would stay NaN; the callers never pass one).
 __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
   uint16_t r;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
@@ -279,13 +280,17 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
 // FMAs (Markstein's method), two quotients at a time with the packed fp32 instructions:
 // y = RN(1 / scale) is taken once by IEEE division; q = RN(x * y) is then within about
 // an ulp of x / scale, the remainder r = x - q * scale is exact in an FMA, and
-// RN(q + r * y) is the correctly rounded quotient. The quantiser needs it only up to the
-// e4m3 range, so q is first clamped to [-464, 464] (beyond 448 every value saturates to
-// +-448 anyway): infinities, overflows and NaN then need no branch (a NaN x keeps a NaN
-// remainder and ends at -448 like the reference), and copysign restores the sign of an
-// exact zero quotient. A scale that is not a normal number, or whose reciprocal is not,
-// takes the IEEE division itself (a branch per 16 elements, uniform for a call). Tests
-// compare the bytes with IEEE division at every e4m3 rounding midpoint for many scales.
+// RN(q + r * y) is the correctly rounded quotient. Only quotients within the e4m3 range
+// matter (the conversion saturates everything beyond +-448), so q is capped at 464 before
+// the correction and the result is floored at -464 after it; then no case needs a branch:
+//   +inf or a positive overflow -> a large or infinite quotient -> saturates to 448;
+//   -inf or a negative overflow -> NaN from inf - inf or a large negative quotient -> -464
+//   (NaN is floored to -464, as fmaxf keeps the number) -> -448;
+//   NaN x -> NaN -> -464 -> -448, the reference's clamp(NaN) (fmax/fmin keep the number);
+// and copysign restores the sign of an exact zero quotient. A scale that is not a
+// normal number, or whose reciprocal is not, takes the IEEE division itself (one uniform
+// branch per 16 elements). Tests compare the bytes with IEEE division at every e4m3
+// rounding midpoint for many scales.
 struct ScaleDiv {
   float s, y;
   uint64_t y2, ns2;  // (y, y) and (-s, -s) for the packed instructions
@@ -297,39 +302,55 @@ struct ScaleDiv {
     y2 = f2_pack(y, y);
     ns2 = f2_pack(-scale, -scale);
   }
-  // clamp(x / scale, -448, 448) for two elements, correctly rounded before the clamp
-  __device__ __forceinline__ void clamped2(float x0, float x1, float& c0, float& c1) const {
-    if (!fast) {
-      c0 = fminf(fmaxf(x0 / s, -448.0f), 448.0f);
-      c1 = fminf(fmaxf(x1 / s, -448.0f), 448.0f);
-      return;
-    }
+  // two quotients ready for the saturating e4m3 conversion (fast path)
+  __device__ __forceinline__ void quot2(float x0, float x1, float& c0, float& c1) const {
     const uint64_t x2 = f2_pack(x0, x1);
     float q0, q1;
     f2_unpack(f2_mul(x2, y2), q0, q1);
-    const float a0 = fminf(fmaxf(q0, -464.0f), 464.0f), a1 = fminf(fmaxf(q1, -464.0f), 464.0f);
-    const uint64_t a2 = f2_pack(a0, a1);
+    const uint64_t a2 = f2_pack(fminf(q0, 464.0f), fminf(q1, 464.0f));
     const uint64_t r2 = f2_fma(a2, ns2, x2);  // x - a * scale, exact
     float b0, b1;
     f2_unpack(f2_fma(r2, y2, a2), b0, b1);
-    b0 = copysignf(b0, q0);
-    b1 = copysignf(b1, q1);
-    c0 = fminf(fmaxf(b0, -448.0f), 448.0f);  // NaN -> -448, as quantize_e4m3
-    c1 = fminf(fmaxf(b1, -448.0f), 448.0f);
+    c0 = fmaxf(copysignf(b0, q0), -464.0f);
+    c1 = fmaxf(copysignf(b1, q1), -464.0f);
+  }
+  // the same from IEEE division (scales that are not normal numbers)
+  __device__ __forceinline__ void quot2_ieee(float x0, float x1, float& c0, float& c1) const {
+    c0 = fminf(fmaxf(x0 / s, -448.0f), 448.0f);
+    c1 = fminf(fmaxf(x1 / s, -448.0f), 448.0f);
   }
 };
 
+// Four quantised elements (a..d, a lowest) as e4m3 bytes with the saturating conversion.
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  return e4m3x2(a, b) | (e4m3x2(c, d) << 16);
+}
+
 // 16 elements quantised with one scale, packed as 16 e4m3 bytes (element 0 lowest).
-__device__ __forceinline__ uint4 quantize16(const float (&x)[16], const ScaleDiv& d) {
+template <typename Get>
+__device__ __forceinline__ uint4 quantize16_from(const Get& at, const ScaleDiv& d) {
   uint32_t w[4];
+  if (d.fast) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float c0, c1, c2, c3;
-    d.clamped2(x[4 * i], x[4 * i + 1], c0, c1);
-    d.clamped2(x[4 * i + 2], x[4 * i + 3], c2, c3);
-    w[i] = e4m3x2(c0, c1) | (e4m3x2(c2, c3) << 16);
+    for (int i = 0; i < 4; ++i) {
+      float c0, c1, c2, c3;
+      d.quot2(at(4 * i), at(4 * i + 1), c0, c1);
+      d.quot2(at(4 * i + 2), at(4 * i + 3), c2, c3);
+      w[i] = e4m3x4(c0, c1, c2, c3);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float c0, c1, c2, c3;
+      d.quot2_ieee(at(4 * i), at(4 * i + 1), c0, c1);
+      d.quot2_ieee(at(4 * i + 2), at(4 * i + 3), c2, c3);
+      w[i] = e4m3x4(c0, c1, c2, c3);
+    }
   }
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+__device__ __forceinline__ uint4 quantize16(const float (&x)[16], const ScaleDiv& d) {
+  return quantize16_from([&](int j) { return x[j]; }, d);
 }
 
 // The 16-element group of a (token, head) row as raw 16-byte words, converted to float
@@ -348,15 +369,7 @@ template <typename T> struct Raw16 {
   }
   // the 16 elements quantised with one scale as 16 e4m3 bytes, converted pair by pair
   __device__ __forceinline__ uint4 quantize(const ScaleDiv& d) const {
-    uint32_t q[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float c0, c1, c2, c3;
-      d.clamped2(at(4 * i), at(4 * i + 1), c0, c1);
-      d.clamped2(at(4 * i + 2), at(4 * i + 3), c2, c3);
-      q[i] = e4m3x2(c0, c1) | (e4m3x2(c2, c3) << 16);
-    }
-    return make_uint4(q[0], q[1], q[2], q[3]);
+    return quantize16_from([&](int j) { return at(j); }, d);
   }
 };
 
@@ -378,7 +391,7 @@ __device__ __forceinline__ float amax_step(float m, float a) {  // NaN wins, as 
 // The vector form needs 16-byte aligned rows and strides (kVec); otherwise GROUPS = 1
 // and elements are loaded one by one.
 template <typename T, typename SlotT, int GROUPS, bool kVec>
-__global__ void __launch_bounds__(kStoreThreads)
+__global__ void __launch_bounds__(kStoreThreads, 4)
 store_kv_fp8_calib_kernel(const uint8_t* __restrict__ key, const uint8_t* __restrict__ value,
                           int64_t k_st, int64_t k_sh, int64_t v_st, int64_t v_sh,  // bytes
                           uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
@@ -868,7 +881,8 @@ int launch_store_fp8(const void* key, const void* value, int64_t k_st, int64_t k
         num_heads, groups, vec, invalid);
     return cuda_status(cudaGetLastError(), "store_kvcache_fp8 launch");
   }
-  const int per = vec ? (per_thread_items(total) >= 2 ? 2 : 1) : 1;
+  // two groups per thread for 16-bit keys (fp32 keys would spill at the 64-register cap)
+  const int per = (vec && sizeof(T) == 2 && per_thread_items(total) >= 2) ? 2 : 1;
   const int grid = sm_multiple(grid_for((total + per - 1) / per, kStoreThreads));
   const int pt_shift = log2_if_pow2((int64_t)num_heads * groups);
   const int gr_shift = log2_if_pow2(groups);
@@ -877,9 +891,14 @@ int launch_store_fp8(const void* key, const void* value, int64_t k_st, int64_t k
       (const uint8_t*)key, (const uint8_t*)value, k_st * eb, k_sh * eb, v_st * eb, v_sh * eb,   \
       (uint8_t*)k_cache, (uint8_t*)v_cache, k_scale, v_scale, slots, num_slots, (uint32_t)total, \
       (uint32_t)num_heads, (uint32_t)groups, pt_shift, gr_shift, work, invalid)
-  if (!vec) MKV_FP8(1, false);
-  else if (per == 2) MKV_FP8(2, true);
-  else MKV_FP8(1, true);
+  if (!vec) {
+    MKV_FP8(1, false);
+  } else if constexpr (sizeof(T) == 2) {
+    if (per == 2) MKV_FP8(2, true);
+    else MKV_FP8(1, true);
+  } else {
+    MKV_FP8(1, true);
+  }
 #undef MKV_FP8
   return cuda_status(cudaGetLastError(), "store_kvcache_fp8 launch");
 }
