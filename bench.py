@@ -157,6 +157,26 @@ def cpu_threads() -> int:
     return max(1, min(h["physical_cores"], h["usable_cpus"]))
 
 
+def workload_config(args, world: int) -> dict:
+    """The `config` object of the JSON line: the workload only (both arms print the same
+    one), built from the BASELINE config's definition without touching a GPU."""
+    if args.config == "config4":
+        batch = args.batch or 64
+        lens = [32768] * batch
+        desc = "config4 (BASELINE config 4: FP8 decode, B=64, ctx 32768)"
+    else:
+        batch = args.batch or 256
+        lens = torch.randint(1024, 8193, (batch,), generator=torch.Generator().manual_seed(0)).tolist()
+        desc = "config3 (BASELINE config 3: bf16 decode, B=256, ctx U[1024,8192])"
+    return {"workload": desc, "num_seqs": batch, "num_heads": 32, "num_kv_heads": 8,
+            "head_dim": 128, "block_size": 256, "max_num_blocks": (max(lens) + 255) // 256,
+            "parallelism": (f"kv-head tp{world}" if world > 1 else
+                            f"rank 0 of a {args.emulate_shard}-way kv-head split, one GPU"
+                            if args.emulate_shard > 1 else "single GPU"),
+            "l2": "working set >> 126 MB L2 (no flush needed)",
+            "step": "append 1 token/seq + paged decode"}
+
+
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
 
@@ -629,18 +649,9 @@ def run_ours(args, rank, world, local):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "fp8_e4m3 cache, bf16 q/out, fp32 accumulate" if fp8 else "bf16 (fp32 accumulate)",
         "data": "synthetic (seeded N(0,1), random page permutation)",
-        "config": {"workload": head["workload"] + (" (BASELINE config 4: FP8 decode, B=64, ctx 32768)" if fp8 else
-                                                   " (BASELINE config 3: bf16 decode, B=256, ctx U[1024,8192])"),
-                   "num_seqs": head["batch"], "num_heads": head["num_heads"],
-                   "num_kv_heads": head["num_kv_heads"], "head_dim": head["head_dim"],
-                   "block_size": head["block_size"], "max_num_blocks": head["max_num_blocks"],
-                   "num_splits": head["splits"],
-                   "parallelism": (f"kv-head tp{world}" if world > 1 else
-                                   f"rank 0 of a {args.emulate_shard}-way kv-head split, one GPU"
-                                   if args.emulate_shard > 1 else "single GPU"),
-                   "l2": "working set >> 126 MB L2 (no flush needed)",
-                   "step": "append 1 token/seq + paged decode" +
-                           ("" if args.no_overlap else " (decode prologue overlaps the append)"),
+        "config": workload_config(args, world),
+        "method": {"num_splits": head["splits"],
+                   "overlap": not args.no_overlap,
                    "launch": "eager" if args.eager else
                              "CUDA-graph replay of the step (e2e: one pinned H2D copy, replay, D2H copy per step, "
                              "copies of neighbouring steps overlapped on two copy streams)"},
@@ -748,7 +759,7 @@ def run_reference(args, rank, world):
         "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32 (reference CPU path)",
         "data": "synthetic (seeded N(0,1), random page permutation)",
-        "config": {"workload": args.config, "cpu_sample_sequences_per_step": nseq},
+        "config": workload_config(args, world),
         "layer_decode_tokens_per_s": round(total_seq / total_t, 2),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                          "host": host_cpu(), "sample": sample},
