@@ -483,22 +483,6 @@ __device__ __forceinline__ void pf_cvt16(const uint4 raw, float scale, uint4& lo
                   pf_to_qt<QT, CT, kTok>(h[6], scale), pf_to_qt<QT, CT, kTok>(h[7], scale));
 }
 
-#ifdef MKV_PREFILL_TRACE
-// Debug-only event timeline (globaltimer, ns) of one CTA: [event][tile].
-__device__ unsigned long long g_pftrace[16][64];
-#define PF_TRACE(ev, tile)                                                   \
-  do {                                                                       \
-    if (blockIdx.x == 8 && blockIdx.y == 0 && (tile) < 64) {                 \
-      unsigned long long t_;                                                 \
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                 \
-      g_pftrace[(ev)][(tile)] = t_;                                          \
-    }                                                                        \
-  } while (0)
-#else
-#define PF_TRACE(ev, tile) \
-  do {                     \
-  } while (0)
-#endif
 namespace pf05 {
 using namespace sm100;
 constexpr int kRows = 128;     // MMA M: (query token, head) rows of one query tile
@@ -685,7 +669,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         uint64_t* empty = is_v ? vempty : kempty;
         uint64_t* full = is_v ? vfull : kfull;
         if (!__all_sync(0xffffffffu, mbar_wait(&empty[st], ((t / ns) & 1) ^ 1, abort_flag))) return false;
-        if (lane == 0) PF_TRACE(is_v ? 9 : 0, t);
         uint8_t* dst = smem + (is_v ? L::V0 : L::K0) + st * TILE;
         uint32_t bytes = 0;
         for (int sgi = 0; sgi < nseg; ++sgi) {
@@ -702,7 +685,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         if (is_v) fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes);
-        if (lane == 0 && !is_v) PF_TRACE(1, t);
         for (int sgi = 0; sgi < nseg; ++sgi) {
           const int pg = __shfl_sync(0xffffffffu, seg_page, sgi);
           if (lane == 0 && pg >= 0) {
@@ -753,7 +735,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
     auto qk = [&](int q, int i, int sb, bool release) -> bool {
       const int st = i % kKS;
       if (!__all_sync(0xffffffffu, mbar_wait(&kfull[st], (i / kKS) & 1, abort_flag))) return false;
-      if (lane == 0 && q == 0) PF_TRACE(14, i);
       tc_fence_after_sync();
       if (lane == 0) {
         const uint32_t qaddr = smem_u32(smem + L::Q0 + q * TILE);
@@ -766,7 +747,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         }
         mma_commit(&sfull[sb]);
         if (release) mma_commit(&kempty[st]);
-        if (q == 0) PF_TRACE(2, i);
       }
       __syncwarp();
       issued = true;
@@ -778,7 +758,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       const int st = j % kVS;
       bool got = mbar_wait(&pfull[sb], ph, abort_flag) && mbar_wait(&vfull[st], (j / kVS) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, got)) return false;
-      if (lane == 0 && q == 0) PF_TRACE(12, j);
       tc_fence_after_sync();
       if (lane == 0) {
         const uint32_t vaddr = smem_u32(smem + L::V0 + st * TILE);
@@ -790,10 +769,8 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
           const uint32_t pcol = sb * kTile + (kSplit && k >= 4 ? 32 + 8 * k : 8 * k);
           mma_f16_ts(tmem + 256 + q * kD, tmem + pcol, b, kIdPV, (j > 0 || k > 0) ? 1u : 0u);
         }
-        if (q == 0) PF_TRACE(13, j);
         mma_commit(&ofull[q]);
         if (release) mma_commit(&vempty[st]);
-        if (q == 0) PF_TRACE(3, j);
       }
       __syncwarp();
       issued = true;
@@ -869,7 +846,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], ph, abort_flag));
       if (!ok) break;
       const uint32_t bad = __ballot_sync(0xffffffffu, pg < 0);  // bit s: segment s missing
-      if (warp == 2 && lane == 0) PF_TRACE(4, i);
       tc_fence_after_sync();
       const uint32_t sa = tmem + lane_base + sb * kTile;
       // mask: the causal edge of this row (tokens >= vis, which also covers tokens past
@@ -1016,7 +992,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
           lsum = p_tile(m_new, w0, w1, unused);
         }
       }
-      if (warp == 2 && lane == 0) PF_TRACE(5, i);
       m = m_new;
       l = l * alpha + lsum;
       // P over the first 64 columns of this S buffer (kSplit: each half's P over the first
@@ -1027,12 +1002,10 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         tmem_st32(sa, w0);
         tmem_st32(sa + 32, w1);
       }
-      if (warp == 2 && lane == 0) PF_TRACE(10, i);
       // PV(i-1) done: O may be rescaled, and the next wait on this O barrier is for PV(i)
       if (i > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(&ofull[qt], (i - 1) & 1, abort_flag));
         if (!ok) break;
-        if (warp == 2 && lane == 0) PF_TRACE(11, i);
         tc_fence_after_sync();
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
@@ -1046,7 +1019,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
         }
       }
       tmem_wait_st();
-      if (warp == 2 && lane == 0) PF_TRACE(6, i);
       // V rows past the last visible token of every row may hold anything (the page's
       // other tokens or never-written memory): zero them so that 0 * V stays 0. Query
       // tile 0 does it, before its PV product, which is issued before tile 1's.
@@ -1067,8 +1039,6 @@ paged_prefill_tc05_kernel(const PrefillParams p, const __grid_constant__ CUtenso
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pfull[sb]);
-      if (warp == 2 && lane == 0) PF_TRACE(7, i);
-      if (warp == 5 && lane == 0) PF_TRACE(15, i);
     }
     if (!ok) *abort_flag = 1;
     // ---- epilogue: out = O / l (0/0 = NaN for a row that sees nothing)
@@ -1187,17 +1157,15 @@ typedef CUresult (*PfEncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-PfEncodeTiledFn pf_encode_fn() {
-  static PfEncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
+PfEncodeTiledFn pf_encode_fn() {  // resolved once (thread-safe static initialisation)
+  static const PfEncodeTiledFn fn = []() -> PfEncodeTiledFn {
     cudaDriverEntryPointQueryResult q;
     void* f = nullptr;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PfEncodeTiledFn>(f);
-    tried = true;
-  }
+      return reinterpret_cast<PfEncodeTiledFn>(f);
+    return nullptr;
+  }();
   return fn;
 }
 
@@ -1747,11 +1715,6 @@ extern "C" size_t mkv_paged_prefill_workspace_bytes(
                                max_num_blocks, q_dtype, cache_dtype);
 }
 
-#ifdef MKV_PREFILL_TRACE
-extern "C" __attribute__((visibility("default"))) int mkv_debug_prefill_trace(unsigned long long* host) {
-  return (int)cudaMemcpyFromSymbol(host, mkv::g_pftrace, sizeof(mkv::g_pftrace));
-}
-#endif
 
 extern "C" size_t mkv_varlen_prefill_workspace_bytes(int32_t num_seqs, int64_t total_tokens,
                                                      int32_t max_seqlen, int32_t num_kv_heads,
