@@ -449,3 +449,65 @@ def test_decode_ex_rejects_bad_arguments():
     # scales for an unquantised cache
     st = lib.mkv_paged_decode_ex(*base, 2, p, p, None, None, *tail, 0, None, stream)
     assert st == mkv_module("_lib").ERR_INVALID_ARGUMENT
+
+
+# ------------------------------------------------------------------ FP8 operand split
+def _fp8_cache(n_tokens, kvh, d, g, fill):
+    x = fill(torch.randn(n_tokens, kvh, d, generator=g))
+    return x.clamp(-448, 448).to(torch.float8_e4m3fn)
+
+
+@pytest.mark.parametrize("case", ["peaked", "uniform_32k", "wide_v", "outlier_q", "tiny_scores"])
+def test_decode_fp8_adversarial_ranges(case):
+    """The FP8-MMA kernel splits the query and P into e4m3 hi + lo parts (about 8
+    significant bits each, like bf16) where the reference dequantises to fp32 and dots in
+    fp32. These inputs push that split: a softmax concentrated on one token per
+    sequence, a uniform softmax over 32768 tokens, V spanning e4m3's whole range
+    (subnormals to 448), queries with x100 outlier dimensions, and scores within 1e-3 of
+    each other. Each must stay within the bf16 tolerance of the float64 oracle; the worst
+    error / tolerance is printed."""
+    H, KVH, D, BS = 32, 8, 128, 256
+    g = torch.Generator().manual_seed(["peaked", "uniform_32k", "wide_v", "outlier_q", "tiny_scores"].index(case) + 71)
+    lens = [32768] * 2 if case == "uniform_32k" else [int(x) for x in torch.randint(200, 3000, (6,), generator=g)]
+    B = len(lens)
+    need = [(n + BS - 1) // BS for n in lens]
+    NB = sum(need)
+    bt = torch.full((B, max(need)), -1, dtype=torch.int32)
+    perm = torch.randperm(NB, generator=g)
+    pos = 0
+    for b, k in enumerate(need):
+        bt[b, :k] = perm[pos:pos + k].int()
+        pos += k
+    q = torch.randn(B, H, D, generator=g)
+    ks, vs = 0.02, 0.03
+    kfill = lambda x: x * 40
+    vfill = lambda x: x * 40
+    scale = 1.0 / math.sqrt(D)
+    if case == "wide_v":
+        vfill = lambda x: torch.sign(x) * (2.0 ** (x.abs() * 6 - 9)).clamp(max=448)
+    if case == "outlier_q":
+        q[:, :, ::16] *= 100.0
+    if case == "uniform_32k":
+        scale = 1e-6
+    if case == "tiny_scores":
+        scale = 1e-4
+    kc = _fp8_cache(NB * BS, KVH, D, g, kfill).view(NB, BS, KVH, D)
+    vc = _fp8_cache(NB * BS, KVH, D, g, vfill).view(NB, BS, KVH, D)
+    if case == "peaked":  # one token per sequence aligned with every query head
+        for b in range(B):
+            t = int(torch.randint(0, lens[b], (1,), generator=g))
+            page, off = int(bt[b, t // BS]), t % BS
+            for h in range(KVH):
+                kc[page, off, h] = (q[b, h * (H // KVH)] * 40).clamp(-448, 448).to(torch.float8_e4m3fn)
+    q = q.to(torch.bfloat16)
+    cl = torch.tensor(lens, dtype=torch.int64)
+    kst, vst = torch.tensor([ks]), torch.tensor([vs])
+    ref = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS, k_scale=kst, v_scale=vst)
+    out = attn.paged_attention_decode_quantized(
+        q.cuda(), kc.cuda(), vc.cuda(), kst.cuda(), vst.cuda(), bt.cuda(), cl.cuda(), scale, H, KVH, D,
+        BS, "fp8_per_tensor").cpu()
+    atol, rtol = TOL[torch.bfloat16]
+    margin = float(((out.double() - ref).abs() / (atol + rtol * ref.abs())).max())
+    print(f"\nFP8_ADVERSARIAL {case}: max |err| {float((out.double() - ref).abs().max()):.3e}, "
+          f"max |ref| {float(ref.abs().max()):.3e}, worst err/tol {margin:.4f}")
+    assert margin <= 1.0
