@@ -159,6 +159,17 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+// Two 16x16 matrices of 8-bit elements, transposed (sm_100a): lanes 0-15 give the row
+// addresses of the first, 16-31 those of the second. Lane l receives, per matrix, the
+// column l / 4 (first register) and l / 4 + 8 (second) at rows 4 (l % 4) .. 4 (l % 4) + 3,
+// one row per byte, lowest row in the lowest byte: the A fragment of an 8-bit
+// m16n8k32 MMA whose A is stored K-major.
+__device__ __forceinline__ void ldmatrix_b8_x2_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                     uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
                                                   uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"

@@ -590,6 +590,12 @@ __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
   if (threadIdx.x == 0) *ctr = 0u;
 }
 
+// Swizzle key of an e4m3 V row in the FP8-MMA kernel's tiles: bits 0, 1 and 3 of the row
+// (rows repeat it every 16). That kernel's transposed 8-bit loads read the rows
+// {0,1,8,9,2,3,10,11} (and those + 4) together; their keys are distinct, so each such
+// 8-row read touches every bank once.
+__device__ __forceinline__ int v_swizzle_key(int row) { return (row & 3) | ((row >> 1) & 4); }
+
 // ---------------------------------------------------------------- tensor-core tile loads
 // Issues the cp.async copies of one K/V tile (TILE token rows of ROWB bytes of one kv
 // head, starting at token t0) into the stage's buffers, 16-byte chunks XOR-swizzled by
@@ -598,7 +604,7 @@ __device__ void finish_cta(const DecodeParams& p, const Seg& sg, int h0, int nh,
 // When the tile lies inside one page (power-of-two block_size >= TILE) the thread's
 // rows are one base address plus a constant stride, so a full tile costs two cp.async
 // and one address add per pass.
-template <int TILE, int ROWB>
+template <int TILE, int ROWB, bool kVKey = false>
 __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
                                              const BlockSlice& slice, const int* bt_s,
                                              const TokRange& rng, int t0, uint8_t* kd,
@@ -612,7 +618,9 @@ __device__ __forceinline__ void load_kv_tile(const DecodeParams& p, int seq,
   const int tid = threadIdx.x, ld_c = tid % CPR, ld_r0 = tid / CPR;
   // (r & 7) is the same for all of this thread's rows r = ld_r0 + i * RPP
   const uint32_t soff0 = ld_r0 * ROWB + ((ld_c ^ (ld_r0 & 7)) << 4);
-  const uint32_t kd0 = smem_u32(kd) + soff0, vd0 = smem_u32(vd) + soff0;
+  const uint32_t kd0 = smem_u32(kd) + soff0;
+  const uint32_t vd0 =
+      smem_u32(vd) + (kVKey ? ld_r0 * ROWB + ((ld_c ^ v_swizzle_key(ld_r0)) << 4) : soff0);
   // per-token scales of 8-bit pages: entry r < TILE is row r's K scale, TILE + r its V
   // scale (zero for rows that are not loaded)
   if (rs != nullptr && one_page_per_tile) {  // one page: row r's scales are r * KVH apart
@@ -1188,7 +1196,7 @@ paged_decode_tc_kernel(const DecodeParams p) {
       }
     }
 
-    // ---- per-token scales (kPT): K scale on S^T rows, V scale kept for P
+    // ---- int8 pages: take out the +1152 bias's contribution to S^T
     if (kBias) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -1198,31 +1206,30 @@ paged_decode_tc_kernel(const DecodeParams p) {
         s[nt][3] -= qbias[nt][1];
       }
     }
+    // Score multiplier per token of this thread (kPT: the token's K scale folded in) and
+    // an additive -inf for rows that were not loaded, so a score costs one FFMA (those
+    // rows' K bytes and scales are zero-filled: 0 * c - inf = -inf).
     float vsc0 = 1.0f, vsc1 = 1.0f;
+    float c0 = sc, c1 = sc;
     if (kPT) {
       const float* rs = rs_s + stage * 2 * kTcTile;
-      const float k0 = rs[warp * 16 + g], k1 = rs[warp * 16 + g + 8];
+      c0 = sc * rs[warp * 16 + g];
+      c1 = sc * rs[warp * 16 + g + 8];
       vsc0 = rs[kTcTile + warp * 16 + g];
       vsc1 = rs[kTcTile + warp * 16 + g + 8];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        s[nt][0] *= k0;
-        s[nt][1] *= k0;
-        s[nt][2] *= k1;
-        s[nt][3] *= k1;
-      }
     }
+    const float bias0 = vld[warp * 16 + g] != 0 ? 0.0f : -INFINITY;
+    const float bias1 = vld[warp * 16 + g + 8] != 0 ? 0.0f : -INFINITY;
 
     // ---- online softmax per query head (column of S^T), exp2 domain
-    const bool v0 = vld[warp * 16 + g] != 0, v1 = vld[warp * 16 + g + 8] != 0;
     uint32_t pb[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       float alpha[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const float x0 = v0 ? s[nt][e] * sc : -INFINITY;      // token g
-        const float x1 = v1 ? s[nt][e + 2] * sc : -INFINITY;  // token g + 8
+        const float x0 = fmaf(s[nt][e], c0, bias0);      // token g
+        const float x1 = fmaf(s[nt][e + 2], c1, bias1);  // token g + 8
         float mx = fmaxf(x0, x1);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
@@ -1231,18 +1238,17 @@ paged_decode_tc_kernel(const DecodeParams p) {
         const float base = m_new == -INFINITY ? 0.0f : m_new;
         alpha[e] = exp2f(m_run[nt][e] - base);
         m_run[nt][e] = m_new;
-        const float p0 = exp2f(x0 - base), p1 = exp2f(x1 - base);
+        const float p0 = ex2_approx(x0 - base), p1 = ex2_approx(x1 - base);  // 2^-inf = +0
         l_run[nt][e] = fmaf(l_run[nt][e], alpha[e], p0 + p1);
         s[nt][e] = p0;
         s[nt][e + 2] = p1;
       }
       if (alpha[0] != 1.0f || alpha[1] != 1.0f) {
+        const uint64_t a2 = f2_pack(alpha[0], alpha[1]);  // accumulator pairs: heads 2tig, 2tig + 1
 #pragma unroll
         for (int j = 0; j < D / 16; ++j) {
-          o[nt][j][0] *= alpha[0];
-          o[nt][j][1] *= alpha[1];
-          o[nt][j][2] *= alpha[0];
-          o[nt][j][3] *= alpha[1];
+          f2_unpack(f2_mul(f2_pack(o[nt][j][0], o[nt][j][1]), a2), o[nt][j][0], o[nt][j][1]);
+          f2_unpack(f2_mul(f2_pack(o[nt][j][2], o[nt][j][3]), a2), o[nt][j][2], o[nt][j][3]);
         }
       }
       // P^T as the B operand (K = tokens, N = heads): transpose the 8x8 blocks
@@ -1526,7 +1532,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
   auto load_tile = [&](int it) {
     const int stage = (gt + it) % STAGES;
     uint8_t* kd = smem + stage * STAGE_BYTES;
-    load_kv_tile<kF8Tile, ROWB>(p, seq, slice, bt_s, rng, rng.begin + it * kF8Tile, kd,
+    load_kv_tile<kF8Tile, ROWB, true>(p, seq, slice, bt_s, rng, rng.begin + it * kF8Tile, kd,
                                 kd + TILE_BYTES, valid + stage * kF8Tile, row_stride, head_off,
                                 one_page_per_tile, kPT ? rs_s + stage * 2 * kF8Tile : nullptr, kvh);
   };
@@ -1633,18 +1639,21 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
     }
 
     // ---- softmax update and P^T (e4m3 hi + lo) B fragments
-    bool vt[2][2];
+    // Per token of this thread: the score multiplier and an additive -inf for rows that
+    // were not loaded, so each score costs one FFMA (0 * c - inf = -inf for those rows,
+    // whose K bytes and scales are zero-filled).
+    float cmul[2][2], cbias[2][2];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
-      vt[mt][0] = vld[warp * 32 + mt * 16 + g] != 0;
-      vt[mt][1] = vld[warp * 32 + mt * 16 + g + 8] != 0;
+      cbias[mt][0] = vld[warp * 32 + mt * 16 + g] != 0 ? 0.0f : -INFINITY;
+      cbias[mt][1] = vld[warp * 32 + mt * 16 + g + 8] != 0 ? 0.0f : -INFINITY;
     }
     // kPT: this thread's tokens' K scales and V scales / 2^e. O is per warp, so e comes
     // from the largest V scale of the warp's own 32 tokens (vm < 2^e). e is sticky: it
     // rises when a tile needs more range and falls only when the tile's bound is more
     // than 4 binades lower, so O is rarely rescaled, while P * vs / 2^e stays below 2^8
     // (inside e4m3's range) and within 2^-4 of it for the split's precision.
-    float ksv[2][2], vsv[2][2];
+    float vsv[2][2];
     float o_rescale = 1.0f;
     if constexpr (kPT) {
       const float* rs = rs_s + stage * 2 * kF8Tile;
@@ -1654,15 +1663,15 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
           const int tok = warp * 32 + mt * 16 + g + 8 * rr;
-          ksv[mt][rr] = rs[tok];
+          cmul[mt][rr] = sc * rs[tok];
           vsv[mt][rr] = rs[kF8Tile + tok];
           vm = fmaxf(vm, vsv[mt][rr]);
         }
-      vm = warp_max(vm);
-      // the bound's exponent from the float's exponent field (scales are >= 0), kept in
-      // [-126, 126] so that 2^-e and the power-of-two rescales are built from bits
+      // the warp's largest scale: scales are >= +0, so their bit patterns order like the
+      // values and one integer reduction finds it; its exponent field gives the bound,
+      // kept in [-126, 126] so that 2^-e and the power-of-two rescales are built from bits
+      const uint32_t vb = __reduce_max_sync(0xffffffffu, __float_as_uint(vm));
       int e = v_exp;
-      const uint32_t vb = __float_as_uint(vm);
       if (vb != 0u && (vb >> 23) < 0xffu) e = min((int)(vb >> 23) - 126, 126);
       if (it == 0) {
         v_exp = e;  // O is still zero
@@ -1676,6 +1685,9 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) vsv[mt][rr] *= inv;
+    } else {
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) cmul[mt][0] = cmul[mt][1] = sc;
     }
     uint32_t ph[NT][2], pl[NT][2];
 #pragma unroll
@@ -1684,16 +1696,12 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       float f[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float mx = -INFINITY;
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-          for (int rr = 0; rr < 2; ++rr) {
-            const int i = e + 2 * rr;
-            const float v = vt[mt][rr] ? s[nt][mt][i] * (kPT ? sc * ksv[mt][rr] : sc) : -INFINITY;
-            x[mt][i] = v;
-            mx = fmaxf(mx, v);
-          }
+          for (int rr = 0; rr < 2; ++rr)
+            x[mt][e + 2 * rr] = fmaf(s[nt][mt][e + 2 * rr], cmul[mt][rr], cbias[mt][rr]);
+        float mx = fmaxf(fmax3(x[0][e], x[0][e + 2], x[1][e]), x[1][e + 2]);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
@@ -1702,13 +1710,16 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
         f[e] = q_ref[nt][e] == -INFINITY ? 1.0f : exp2f(q_ref[nt][e] - q_new);
         m_run[nt][e] = m_new;
         q_ref[nt][e] = q_new;
+        // P = 2^(x - q_new + 8) <= 2^8; q_new is -inf only when every x is, and then
+        // 2^(-inf) = +0
+        const float qn8 = q_new == -INFINITY ? 0.0f : q_new - 8.0f;
         float lsum = 0.0f;
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
           for (int rr = 0; rr < 2; ++rr) {
             const int i = e + 2 * rr;
-            const float pv = x[mt][i] == -INFINITY ? 0.0f : exp2f(x[mt][i] - q_new + 8.0f);
+            const float pv = ex2_approx(x[mt][i] - qn8);
             x[mt][i] = kPT ? pv * vsv[mt][rr] : pv;
             lsum += pv;
           }
@@ -1716,12 +1727,11 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
         if (kPT) f[e] *= o_rescale;  // O into the units of this tile's V scales
       }
       if (f[0] != 1.0f || f[1] != 1.0f) {
+        const uint64_t f2 = f2_pack(f[0], f[1]);  // accumulator pairs: (head 2tig, 2tig + 1)
 #pragma unroll
         for (int j = 0; j < D / 16; ++j) {
-          o[nt][j][0] *= f[0];
-          o[nt][j][1] *= f[1];
-          o[nt][j][2] *= f[0];
-          o[nt][j][3] *= f[1];
+          f2_unpack(f2_mul(f2_pack(o[nt][j][0], o[nt][j][1]), f2), o[nt][j][0], o[nt][j][1]);
+          f2_unpack(f2_mul(f2_pack(o[nt][j][2], o[nt][j][3]), f2), o[nt][j][2], o[nt][j][3]);
         }
       }
       // P^T fragments: movmatrix gives (head g; tokens 2tig, 2tig+1) and (head g; tokens
@@ -1738,19 +1748,22 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       }
     }
 
-    // ---- O^T += V^T P^T over the warp's 32 tokens, one 16-row head_dim chunk per MMA pair
+    // ---- O^T += V^T P^T over the warp's 32 tokens, one 16-row head_dim chunk per MMA pair.
+    // ldmatrix.m16n16.x2.trans.b8 hands out the A fragments of V^T directly (lane l gets
+    // rows g = l / 4 and g + 8 of the d chunk, K indices 4 tig .. 4 tig + 3 of each 16):
+    // lane l < 16 addresses the row of K index l of the first 16, lane 16 + l that of K
+    // index 16 + l. K index 4 tig + j is token 8 (j >> 1) + 2 tig + (j & 1), the token
+    // order of the P^T fragments that movmatrix produces; O^T's rows are d = 16c + g and
+    // 16c + g + 8.
     {
-      const int r = warp * 32 + lmat * 8 + lrow;  // matrices: token groups 0-7 .. 24-31
+      const int kk = lane & 15;
+      const int tok = warp * 32 + (lane & 16) + ((kk >> 1) & 1) * 8 + 2 * (kk >> 2) + (kk & 1);
+      const uint32_t vrow = vbase + tok * ROWB;
+      const int sw = v_swizzle_key(tok);
 #pragma unroll
       for (int c = 0; c < D / 16; ++c) {
-        uint32_t x[4];
-        ldmatrix_x4_trans(vbase + r * ROWB + ((c ^ lrow) << 4), x[0], x[1], x[2], x[3]);
-        // x[j]: tokens (8j + 2tig, 8j + 2tig + 1) x d (16c + 2g, 16c + 2g + 1)
         uint32_t a[4];
-        a[0] = __byte_perm(x[0], x[1], 0x6420);  // d even, tokens 2tig,2tig+1,8+2tig,9+2tig
-        a[1] = __byte_perm(x[0], x[1], 0x7531);  // d odd
-        a[2] = __byte_perm(x[2], x[3], 0x6420);  // same for tokens 16-31
-        a[3] = __byte_perm(x[2], x[3], 0x7531);
+        ldmatrix_b8_x2_trans(vrow + ((c ^ sw) << 4), a[0], a[1], a[2], a[3]);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           mma_e4m3(o[nt][c], a, ph[nt][0], ph[nt][1]);
@@ -1781,7 +1794,7 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       for (int s = 0; s < STAGES - 1; ++s) {
         if (s < nt2) {
           uint8_t* kd = smem + ((gt + s) % STAGES) * STAGE_BYTES;
-          load_kv_tile<kF8Tile, ROWB>(p, sched.cur.seq, slice, bt_s, nr, nr.begin + s * kF8Tile,
+          load_kv_tile<kF8Tile, ROWB, true>(p, sched.cur.seq, slice, bt_s, nr, nr.begin + s * kF8Tile,
                                       kd, kd + TILE_BYTES, valid + ((gt + s) % STAGES) * kF8Tile,
                                       row_stride, (int64_t)nkvh * ROWB, one_page_per_tile,
                                       kPT ? rs_s + ((gt + s) % STAGES) * 2 * kF8Tile : nullptr, nkvh);
@@ -1819,8 +1832,8 @@ paged_decode_fp8mma_kernel(const DecodeParams p) {
       float* ra = red_acc + (warp * HC + head) * RP;
 #pragma unroll
       for (int j = 0; j < D / 16; ++j) {
-        ra[16 * j + 2 * g] = kPT ? o[nt][j][e] * o_unit : o[nt][j][e];
-        ra[16 * j + 2 * g + 1] = kPT ? o[nt][j][e + 2] * o_unit : o[nt][j][e + 2];
+        ra[16 * j + g] = kPT ? o[nt][j][e] * o_unit : o[nt][j][e];
+        ra[16 * j + g + 8] = kPT ? o[nt][j][e + 2] * o_unit : o[nt][j][e + 2];
       }
       if (g == 0) {
         red_m[warp * HC + head] = q_ref[nt][e];
