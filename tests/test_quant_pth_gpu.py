@@ -264,3 +264,47 @@ def test_int8_step_in_cuda_graph():
     graph.replay()
     torch.cuda.synchronize()
     assert torch.equal(static_out, eager)
+
+
+PTH_CASES = ["outlier_q", "wide_scales", "peaked", "uniform_long"]
+
+
+@pytest.mark.parametrize("mode", ["fp8", "int8"])
+@pytest.mark.parametrize("case", PTH_CASES)
+def test_decode_per_token_head_adversarial(mode, case):
+    """Inputs that push the 8-bit decodes' arithmetic: queries with x100 outlier
+    dimensions (the e4m3 hi + lo query split; int8's 1152 bias on S), per-(token, head)
+    scales spread over 12 binades (the e4m3 kernel's per-warp power of two for V), a
+    softmax concentrated on one token per sequence, and a uniform softmax over 16384
+    tokens. Each must stay within the bf16 tolerance of the float64 oracle; the worst
+    error / tolerance is printed."""
+    H, KVH, D, BS = 32, 8, 128, 256
+    seed = 101 + PTH_CASES.index(case) + (0 if mode == "fp8" else 50)
+    lens = [16384, 16384] if case == "uniform_long" else [200, 1500, 2900, 777, 64, 2048]
+    q, kc, vc, ks, vs, bt, cl = _paged(len(lens), H, KVH, D, BS, lens, mode, seed=seed,
+                                       qdtype=torch.float32)
+    g = torch.Generator().manual_seed(seed + 1)
+    scale = 1.0 / math.sqrt(D)
+    if case == "outlier_q":
+        q[:, :, ::16] *= 100.0
+    if case == "wide_scales":
+        ks = torch.pow(2.0, torch.rand(ks.shape, generator=g) * 12 - 10)
+        vs = torch.pow(2.0, torch.rand(vs.shape, generator=g) * 12 - 10)
+    if case == "uniform_long":
+        scale = 1e-6
+    if case == "peaked":  # one token per sequence aligned with every query head of its kv head
+        for b, n in enumerate(lens):
+            t = int(torch.randint(0, n, (1,), generator=g))
+            page, off = int(bt[b, t // BS]), t % BS
+            for h in range(KVH):
+                row = q[b, h * (H // KVH)] * 40
+                kc[page, off, h] = (row.to(torch.float8_e4m3fn) if mode == "fp8"
+                                    else row.round().clamp(-127, 127).to(torch.int8))
+    q = q.to(torch.bfloat16)
+    ref = paged_decode_ref(q, kc, vc, bt, cl, scale, H, KVH, D, BS, k_scales=ks, v_scales=vs)
+    out = _decode_cuda(mode, q, kc, vc, ks, vs, bt, cl, scale, H, KVH, D, BS)
+    atol, rtol = TOL[torch.bfloat16]
+    margin = float(((out.double() - ref).abs() / (atol + rtol * ref.abs())).max())
+    print(f"\nPTH_ADVERSARIAL {mode} {case}: max |err| {float((out.double() - ref).abs().max()):.3e}, "
+          f"max |ref| {float(ref.abs().max()):.3e}, worst err/tol {margin:.4f}")
+    assert margin <= 1.0
