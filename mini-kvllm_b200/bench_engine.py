@@ -21,6 +21,12 @@ and NCCL all-reduces. What this script changes, and only at import time in every
   * the model runs in bf16 (torch.set_default_dtype), as config 5 names; the reference
     would otherwise build fp32 parameters, and its RoPE returns float32 q/k for bf16
     inputs (a float32 cos/sin cache), so RoPE's outputs are cast back to bf16.
+  * tensor parallelism (TP > 1): the reference's Sequence pickles a compact state for
+    the workers (sequence.py:98-130) that leaves out block_size and, in decode, all but
+    the last token id, so a worker's prepare_decode (model_runner.py:639) raises at
+    sequence.py:81 whatever the attention. block_size is restored on unpickling and the
+    last block's token count is taken from num_tokens, the value rank 0 computes from
+    its full token list (both arms alike).
 Workload (config 5, synthetic and seeded): Qwen3-0.6B shape (28 layers, hidden 1024,
 16 Q / 8 KV heads, head_dim 128, MLP 3072, vocab 151936); --requests prompts of random
 token ids with lengths ~ U[128, 1024]; --output tokens each (ignore_eos: random weights
@@ -83,9 +89,31 @@ def random_weights(model, path):  # replaces load_weights_from_checkpoint(model,
                 p.copy_(cpu)
 
 
-def install(impl: str) -> None:
+def sequence_state_for_workers(block_size: int) -> None:
+    """Make the reference's Sequence usable on tensor-parallel workers: restore
+    block_size when a Sequence is unpickled (its __getstate__, sequence.py:98-106, does
+    not send it), and count the last block's tokens from num_tokens (sequence.py:80-82
+    slices token_ids, which a worker holds only in part during decode). On rank 0, whose
+    token list is complete, both forms give the same number."""
+    from myvllm.engine.sequence import Sequence
+    if getattr(Sequence, "_mkv_worker_state", False):
+        return
+    unpickle = Sequence.__setstate__
+
+    def setstate(self, state):
+        unpickle(self, state)
+        self.block_size = block_size
+
+    Sequence.__setstate__ = setstate
+    Sequence.last_block_num_tokens = property(
+        lambda self: self.num_tokens - self.num_tokens // self.block_size * self.block_size)
+    Sequence._mkv_worker_state = True
+
+
+def install(impl: str, block_size: int) -> None:
     """The import-time changes listed in the module docstring (every rank)."""
     torch.set_default_dtype(torch.bfloat16)
+    sequence_state_for_workers(block_size)
     # The reference's rotary cache is float32 (rotary_embedding.py:89), so a bf16 model's
     # q/k come out of RoPE as float32 and the float32 attention output then meets the
     # bf16 o_proj weight: the unmodified engine runs end to end only in float32. Cast
@@ -110,7 +138,7 @@ def install(impl: str) -> None:
 
 
 def _worker(config: dict, rank: int, event, impl: str) -> None:
-    install(impl)
+    install(impl, config["block_size"])
     from myvllm.engine.model_runner import ModelRunner
     runner = ModelRunner(config, rank, event)
     runner.loop()
@@ -161,7 +189,7 @@ def main() -> None:
     max_len = args.prompt_max + args.output
     config = qwen3_0p6b_config(args.tp, kv, max_len, args.batched_tokens, args.max_seqs, args.port)
     _patch_rendezvous(args.port)
-    install(args.impl)
+    install(args.impl, config["block_size"])
     from myvllm.engine.model_runner import ModelRunner
     from myvllm.engine.scheduler import Scheduler
     from myvllm.engine.sequence import Sequence

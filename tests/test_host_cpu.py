@@ -117,3 +117,33 @@ def test_kv_head_sharding_two_ranks_gloo():
             heads, t = out[r]
             assert heads == [1.0] * 16  # every query head owned exactly once
             assert t == 2.0
+
+
+def test_engine_harness_sequence_state_for_workers():
+    """The config-5 harness's fix for the reference's tensor-parallel workers: a Sequence
+    that crosses the runner's shared-memory RPC (pickle) keeps block_size, and the
+    worker's last-block token count (the decode slot of model_runner.py:639) equals rank
+    0's at every length, page boundaries included. Uses the reference's own Sequence;
+    skipped when the reference is not installed."""
+    import importlib
+    import pickle
+
+    from conftest import REPO
+    if not os.path.isdir(os.path.join(REPO, "baseline", "_ref", "myvllm")):
+        pytest.skip("reference not installed in baseline/_ref")
+    be = importlib.import_module("mini-kvllm_b200.bench_engine")
+    from myvllm.engine.sequence import Sequence
+    bs = 16
+    seq = Sequence(token_ids=list(range(37)), block_size=bs)
+    with pytest.raises(AttributeError):  # the unmodified round trip loses block_size
+        getattr(pickle.loads(pickle.dumps(seq)), "block_size")
+    be.sequence_state_for_workers(bs)
+    for n_out in range(0, 3 * bs):
+        if n_out:
+            seq.append_token(1000 + n_out)
+        rank0 = len(seq.token_ids[seq.num_tokens // bs * bs:])  # sequence.py:80-82 on rank 0
+        worker = pickle.loads(pickle.dumps(seq))
+        assert worker.block_size == bs
+        assert worker.num_tokens == seq.num_tokens
+        assert seq.last_block_num_tokens == rank0
+        assert worker.last_block_num_tokens == rank0
